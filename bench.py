@@ -1,0 +1,463 @@
+"""Benchmark of the fused top-k / top-p sampling path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints ONE JSON line (rank 0). The metric is BASELINE.json's: µs per sampling call at
+B=1, V=151936, k=50, p=0.9, BF16 (the C1 anchor; lower is better), plus HBM GB/s at B=1024 against
+the measured peak (the C3 config, reported in `roofline`).
+
+* A step is one sampling call on one batch. `value` is the amortised device time per call over
+  exactly K back-to-back steps, inputs resident in HBM, cold L2: the steps rotate over enough
+  distinct input buffers to exceed 2x L2 (126 MB).
+* `e2e` is the same metric through the public API with host buffers: pinned host logits copied
+  to the device, the call, and the ids copied back, every step, inside the timed region.
+* `roofline` is the dominant kernel at B=1024 (311 MB of logits per launch, two rotating buffers
+  > 2x L2): algorithmic bytes B*V*2 + B*8 over the CUDA-event launch time, against
+  MEASURED_PEAKS.json's burst HBM copy bandwidth.
+* `cpu_baseline` / `--impl reference` time the reference semantics on the host CPU (the oracle
+  port of benchmarks/reference.py:sample_eager, all host threads) on a bounded sample.
+* N > 1 (torchrun, one process per GPU): weak scaling of the anchor (each rank samples its own
+  B=1 row; value = max over ranks), plus the B=1024 batch-sharded config (rows split across
+  ranks, no collective on the data path) and the vocab-sharded tensor-parallel config (B=32,
+  V=256000 split into N shards, candidates all-gathered over NCCL, merged and sampled on every
+  rank). All multi-GPU times are CUDA-event times, max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "µs/sampling call (B=1,V=151936,k=50,p=.9 BF16); HBM GB/s at B=1024 vs peak"
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+
+C1 = dict(B=1, V=151936, k=50, p=0.9)
+C3 = dict(B=1024, V=151936, k=50, p=0.95)
+C4 = dict(B=32, V=256000, k=64, p=0.9)
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
+# environment
+# ---------------------------------------------------------------------------------------------
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (burst copy, measured)"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback 6.65 TB/s (earlier measurement on this pool)"
+
+
+def committed_traffic():
+    """Per-launch DRAM bytes of the B=1024 launch from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "fs_cluster_kernel_b1024.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------------------------
+# synthetic inputs (seeded, generated on the device)
+# ---------------------------------------------------------------------------------------------
+
+
+def anchor_buffers(n, B, V, device, seed=1234):
+    """C1: N(0, 2^2) bf16 with 20 random ids per row boosted by +8."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = []
+    for _ in range(n):
+        x = torch.randn(B, V, generator=g, device=device) * 2.0
+        idx = torch.rand(B, V, generator=g, device=device).argsort(dim=-1)[:, :20]
+        x.scatter_add_(1, idx, torch.full((B, 20), 8.0, device=device))
+        out.append(x.to(torch.bfloat16))
+    return out
+
+
+def zipf_buffers(n, B, V, device, seed=7, sigma=3.0, s=1.1):
+    """C3: N(0, 3^2) plus a per-row Zipf(1.1) log-bias over a random permutation of ids."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    ranks = torch.arange(1, V + 1, device=device, dtype=torch.float32)
+    bias = -s * torch.log(ranks)
+    bias = bias - bias.mean()
+    out = []
+    for _ in range(n):
+        x = torch.randn(B, V, generator=g, device=device) * sigma
+        for r0 in range(0, B, 128):
+            rows = min(128, B - r0)
+            perm = torch.rand(rows, V, generator=g, device=device).argsort(dim=-1)
+            x[r0:r0 + rows].scatter_add_(1, perm, bias.expand(rows, V))
+        out.append(x.to(torch.bfloat16))
+        del x
+    torch.cuda.synchronize()
+    return out
+
+
+def tp_logits(B, V, device, seed=11, sigma=2.5):
+    g = torch.Generator(device=device).manual_seed(seed)
+    return (torch.randn(B, V, generator=g, device=device) * sigma).to(torch.bfloat16)
+
+
+# ---------------------------------------------------------------------------------------------
+# timing helpers
+# ---------------------------------------------------------------------------------------------
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def timed_steps(fn, steps, warmup, world):
+    """Warm-up, then exactly `steps` calls between CUDA events on the current stream with a
+    barrier + synchronize on both sides. Returns the device ms of the timed region."""
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(steps):
+        fn(i)
+    e.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    return s.elapsed_time(e)
+
+
+# ---------------------------------------------------------------------------------------------
+# the CPU side (oracle port of the reference semantics)
+# ---------------------------------------------------------------------------------------------
+
+
+def cpu_reference_time(B, V, k, p, budget_s=10.0, min_calls=3):
+    """µs per call of the oracle port of benchmarks/reference.py:sample_eager on host cores."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import sampler_oracle as orc
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    x = orc.anchor_logits(B=B, V=V, seed=1234) if B <= 64 else orc.zipf_logits(B, V, seed=7)
+    orc.sample(x, k, p, seed=1, offset=0)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while n < min_calls or time.perf_counter() - t0 < budget_s:
+        orc.sample(x, k, p, seed=1, offset=n)
+        n += 1
+    dt = time.perf_counter() - t0
+    return dt / n * 1e6, threads, n
+
+
+# ---------------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------------
+
+
+def run_ours(args):
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    sys.path.insert(0, str(ROOT))
+    import llm_sampling_kernel_b200 as pkg
+    from llm_sampling_kernel_b200 import fused
+
+    ops = pkg.ops()
+    result = {}
+    launches = 0
+    sampler = ClockSampler(local)
+    with sampler:
+        # ---- C1 anchor: per-rank B=1 row (weak scaling over ranks) ----
+        per = C1["B"] * C1["V"] * 2
+        nbuf = max(2, (2 * L2_BYTES) // per + 1)
+        bufs = anchor_buffers(nbuf, C1["B"], C1["V"], device, seed=1234 + rank)
+
+        def c1_step(i):
+            ops.sample_fused(bufs[i % nbuf], C1["k"], C1["p"], 0x5EED, i, 0)
+
+        ms = timed_steps(c1_step, args.steps, args.warmup, world)
+        launches += args.steps
+        c1_us = max_over_ranks(ms * 1000.0 / args.steps, world)
+        # hot L2 (one buffer), for reference
+        ms_hot = timed_steps(lambda i: ops.sample_fused(bufs[0], C1["k"], C1["p"], 0x5EED, i, 0),
+                             args.steps, args.warmup, world)
+        c1_hot_us = max_over_ranks(ms_hot * 1000.0 / args.steps, world)
+
+        # ---- e2e through the public API with host buffers (pinned) ----
+        host = [b.cpu().pin_memory() for b in bufs[:8]]
+        ids_host = torch.empty(C1["B"], dtype=torch.int64).pin_memory()
+        dev_in = torch.empty_like(bufs[0])
+
+        def e2e_step(i):
+            dev_in.copy_(host[i % len(host)], non_blocking=True)
+            out = fused.sample_fused(dev_in, C1["k"], C1["p"], offset=i)
+            ids_host.copy_(out, non_blocking=True)
+
+        ms_e2e = timed_steps(e2e_step, args.steps, args.warmup, world)
+        e2e_us = max_over_ranks(ms_e2e * 1000.0 / args.steps, world)
+        del bufs, host
+
+        # ---- C3 B=1024 HBM-bound launch (roofline); rows sharded across ranks ----
+        b_rank = C3["B"] // world
+        big = zipf_buffers(2, b_rank, C3["V"], device, seed=7 + rank)
+        c3_steps = max(3, min(args.steps, 50))
+
+        def c3_step(i):
+            ops.sample_fused(big[i % 2], C3["k"], C3["p"], 0x5EED, i, 0)
+
+        ms3 = timed_steps(c3_step, c3_steps, max(3, args.warmup), world)
+        launches += c3_steps
+        c3_us = max_over_ranks(ms3 * 1000.0 / c3_steps, world)
+        del big
+        torch.cuda.empty_cache()
+
+        # ---- C4 vocab-sharded tensor parallel (N > 1) ----
+        tp = None
+        if world > 1:
+            tp = run_tp(ops, world, rank, device, args)
+            launches += tp.pop("launches")
+
+    clocks = sampler.summary()
+    hbm_peak, peak_src = measured_peaks()
+    alg_bytes = b_rank * C3["V"] * 2 + b_rank * 8
+    achieved = alg_bytes / (c3_us * 1e-6) / 1e9  # per rank
+    plan1 = ops.plan(C1["B"], C1["V"], C1["k"], 0)
+    plan3 = ops.plan(b_rank, C3["V"], C3["k"], 0)
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC,
+        "value": round(c1_us, 3),
+        "unit": "µs/call",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(c1_us / 1000.0, 6),
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "u16-key select + f32 softmax (bf16 logits)",
+        "data": "synthetic (seeded, generated on device)",
+        "config": {
+            "workload": "C1 anchor: B=1 per GPU, V=151936, k=50, p=0.9, BF16 N(0,2^2) + 20 ids boosted by 8",
+            "B_per_gpu": C1["B"], "V": C1["V"], "top_k": C1["k"], "top_p": C1["p"],
+            "l2": f"cold: {nbuf} rotating input buffers ({nbuf * per / 2**20:.0f} MiB > 2x L2)",
+            "plan": {"splits": plan1[0], "chunks": plan1[1], "threads": plan1[2], "capacity": plan1[3]},
+            "parallelism": f"dp{world} (independent rows, no collective)",
+        },
+        "hot_l2_us": round(c1_hot_us, 3),
+        "e2e": {"value": round(e2e_us, 3), "unit": "µs/call", "h2d_bytes_per_step": per,
+                "d2h_bytes_per_step": C1["B"] * 8, "api": "llm_sampling_kernel_b200.fused.sample_fused"},
+        "roofline": {
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "traffic": committed_traffic(),
+            "kernel": f"fs_cluster_kernel<bf16,{plan3[1]}>",
+            "workload": f"C3 B={b_rank} per GPU, V=151936, k=50, p=0.95, Zipf(1.1)-biased N(0,3^2), "
+                        f"2 rotating 311 MB buffers (> 2x L2)",
+            "us_per_launch": round(c3_us, 3), "algorithmic_bytes_per_launch": alg_bytes,
+            "peak_source": peak_src,
+        },
+        "b1024": {"us_per_call": round(c3_us, 3), "rows_per_gpu": b_rank,
+                  "aggregate_hbm_gbs": round(achieved * world, 1), "scaling": "strong",
+                  "plan": {"splits": plan3[0], "chunks": plan3[1]}},
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    if tp is not None:
+        line["tp"] = tp
+    if world == 1 and not args.no_cpu:
+        cpu_us, threads, n = cpu_reference_time(C1["B"], C1["V"], C1["k"], C1["p"], budget_s=args.cpu_budget)
+        line["cpu_baseline"] = {"value": round(cpu_us, 1), "unit": "µs/call", "cores": threads, "kind": "port",
+                                "sample": f"C1 row (B=1, V=151936, k=50, p=0.9) x {n} calls of the oracle port "
+                                          f"of benchmarks/reference.py:sample_eager (torch CPU, {threads} threads)"}
+    print(json.dumps(line), flush=True)
+
+
+def run_tp(ops, world, rank, device, args):
+    """C4: vocab-sharded TP. Local shard top-k -> NCCL all-gather of packed candidates -> merge."""
+    import torch.distributed as dist
+
+    B, V, k, p = C4["B"], C4["V"], C4["k"], C4["p"]
+    vs = V // world
+    full = tp_logits(B, V, device)
+    shard = full[:, rank * vs:(rank + 1) * vs].contiguous()
+    gathered = torch.empty(world, B, k + 1, dtype=torch.int64, device=device)
+
+    def step(i):
+        cand = ops.shard_candidates(shard, k, rank * vs, 0)
+        dist.all_gather_into_tensor(gathered, cand)
+        ops.merge_sample(gathered, True, k, p, None, None, None, 0x5EED, i, 0)
+
+    steps = max(3, min(args.steps, 200))
+    ms = timed_steps(step, steps, max(3, args.warmup), world)
+    us = max_over_ranks(ms * 1000.0 / steps, world)
+    ids, _ = ops.merge_sample(gathered, True, k, p, None, None, None, 0x5EED, 0, 0)
+    all_ids = [torch.empty_like(ids) for _ in range(world)]
+    dist.all_gather(all_ids, ids)
+    agree = all(torch.equal(all_ids[0], t) for t in all_ids)
+    return {"us_per_call": round(us, 3), "B": B, "V": V, "shard_vocab": vs, "top_k": k, "top_p": p,
+            "exchange_bytes_per_rank": B * (k + 1) * 8, "ranks_agree": agree, "launches": 2 * steps,
+            "backend": "nccl all_gather_into_tensor"}
+
+
+# ---------------------------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------------------------
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    cpu_us, threads, n = cpu_reference_time(C1["B"], C1["V"], C1["k"], C1["p"],
+                                            budget_s=max(5.0, min(60.0, args.cpu_budget)))
+    line = {
+        "metric": METRIC,
+        "value": round(cpu_us, 1),
+        "unit": "µs/call",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(cpu_us / 1000.0, 4),
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32 (torch CPU)",
+        "data": "synthetic (seeded)",
+        "impl": "reference",
+        "config": {"workload": "C1 anchor: B=1, V=151936, k=50, p=0.9, BF16", "B": 1, "V": 151936,
+                   "top_k": 50, "top_p": 0.9},
+        "cpu_baseline": {"value": round(cpu_us, 1), "unit": "µs/call", "cores": threads, "kind": "port",
+                         "sample": f"{n} calls of the oracle port of benchmarks/reference.py:sample_eager "
+                                   f"(the reference's CPU implementation of the path; its Python package "
+                                   f"cannot travel to the GPU box), {threads} host threads"},
+        "e2e": {"value": round(cpu_us, 1), "unit": "µs/call", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+    world, _, _ = dist_env()
+    if world > 1 and args.impl == "ours":
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

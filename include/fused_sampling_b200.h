@@ -1,0 +1,179 @@
+/*
+ * fused_sampling_b200.h -- C ABI of the B200 (sm_100a) fused top-k / top-p token sampler.
+ *
+ * Hot path: [B, V] FP16/BF16 logits -> [B] int64 token ids, in one kernel launch per call.
+ * Stage order and semantics are those of the reference operator (sathviknookala/llm_sampling_kernel):
+ *   top-k (exactly k, ties to the lowest token id) -> FP32 softmax over the k survivors ->
+ *   cumulative sum -> exclusive-prefix top-p cut (keep i iff c_{i-1} < p; p >= 1 keeps all) ->
+ *   inverse-CDF draw: first i <= r with cum_i >= u * cum_r.
+ *
+ * Every entry point is asynchronous on the given stream, never aborts, never traps, and allocates
+ * nothing: outputs (and, where stated, workspace) are caller-owned device memory.
+ * Plain C types only; the stream is a cudaStream_t (NULL = legacy default stream).
+ *
+ * Reference interfaces each entry point replaces are cited as path:line inside the reference
+ * project.
+ */
+#ifndef FUSED_SAMPLING_B200_H
+#define FUSED_SAMPLING_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define FS_API __attribute__((visibility("default")))
+#else
+#define FS_API
+#endif
+
+/* Binary-compatible with cudaStream_t. */
+typedef struct CUstream_st* fs_stream_t;
+
+typedef enum fs_status {
+  FS_OK = 0,
+  FS_EINVAL = 1,        /* invalid argument: shape, k, p, null pointer, stride           */
+  FS_EUNSUPPORTED = 2,  /* valid request outside what this build implements             */
+  FS_ELAUNCH = 3,       /* a CUDA launch / attribute call failed (see fs_last_error)     */
+  FS_ETIMEOUT = 4,      /* a bounded device-side wait ran out (multi-GPU exchange)       */
+  FS_EWORKSPACE = 5     /* workspace pointer missing or smaller than fs_*_workspace_size */
+} fs_status;
+
+typedef enum fs_dtype { FS_F16 = 0, FS_BF16 = 1 } fs_dtype;
+
+/* Per-row status codes written to row_status (when non-NULL). A row with a non-zero status
+ * gets token id -1, keep = 0 and renormed = 0; its input matches the rejections of the
+ * reference's validate_logits (benchmarks/reference.py:20-26). */
+enum {
+  FS_ROW_OK = 0,
+  FS_ROW_NAN = 1,         /* "logits contain NaN"                          */
+  FS_ROW_POSINF = 2,      /* "logits contain +inf"                         */
+  FS_ROW_ALL_NEGINF = 3,  /* "logits contain a row that is entirely -inf"  */
+  FS_ROW_BAD_PARAM = 4    /* per-row k < 1, or per-row p outside (0, 1]     */
+};
+
+/* Source of the per-row uniform u in [0, 1), in priority order:
+ *   uniforms != NULL : u = uniforms[b]                      (caller-supplied)
+ *   seed_ptr != NULL : seed = *seed_ptr, offset = *offset_ptr + offset_intragraph
+ *                      (graph-captured torch generator state, at::PhiloxCudaState "captured")
+ *   otherwise        : seed, offset by value.
+ * The generated uniform is the reference's splitmix64 contract
+ * (csrc/fused_sampling.cuh:65-71) evaluated at row index (row_base + b). */
+typedef struct fs_rng {
+  const float* uniforms;
+  uint64_t seed;
+  uint64_t offset;
+  const int64_t* seed_ptr;
+  const int64_t* offset_ptr;
+  uint64_t offset_intragraph;
+  int64_t row_base;
+} fs_rng;
+
+typedef struct fs_sample_args {
+  const void* logits;        /* device, rows of 16-bit floats                            */
+  int32_t dtype;             /* fs_dtype                                                 */
+  int64_t batch;             /* B >= 1 (<= 65535)                                        */
+  int64_t vocab;             /* V >= 1 (<= 1 << 19)                                      */
+  int64_t row_stride;        /* elements between row starts, >= V                        */
+  int64_t id_base;           /* added to every emitted id (vocab-shard offset), else 0   */
+  int64_t top_k;             /* k >= 1, clamped to V; with top_k_rows, the bound K       */
+  float top_p;               /* p in (0, 1]; ignored when top_p_rows != NULL             */
+  const int32_t* top_k_rows; /* optional device [B] per-row k (each clamped to K)        */
+  const float* top_p_rows;   /* optional device [B] per-row p                            */
+  fs_rng rng;
+  int64_t* out_ids;          /* device [B] sampled ids (required by fs_sample)           */
+  int64_t* topk_ids;         /* optional device [B, K]: top-K ids, value desc, id asc    */
+  uint8_t* keep;             /* optional device [B, K]: nucleus mask                     */
+  float* renormed;           /* optional device [B, K]: p_i / Z_p inside the nucleus     */
+  int32_t* row_status;       /* optional device [B]: FS_ROW_*                            */
+  int32_t splits;            /* 0 = auto; else CTAs per row (cluster size 1..16)         */
+  int32_t stop_phase;        /* 0 = full pipeline; 1..FS_NUM_PHASES ablation stop point  */
+} fs_sample_args;
+
+#define FS_NUM_PHASES 7
+
+/* Fused top-k + top-p + sample, [B, V] -> [B].
+ * Replaces: sample_fused / stages_fused / run_fused  (csrc/fused_sampling.cu:426-458,503-513)
+ * and the pybind entries sample_fused, stages_fused (csrc/bindings.cpp:20,22). */
+FS_API fs_status fs_sample(const fs_sample_args* args, fs_stream_t stream);
+
+/* Top-K candidate ids only ([B, K] into args->topk_ids; out_ids may be NULL).
+ * Replaces: topk_fused (csrc/fused_sampling.cu:460-473, csrc/bindings.cpp:21). */
+FS_API fs_status fs_topk(const fs_sample_args* args, fs_stream_t stream);
+
+/* Ablation: run the pipeline up to phase args->stop_phase (1..FS_NUM_PHASES) and write a
+ * phase-dependent int64 per row into out_ids. Phase FS_NUM_PHASES is the production path.
+ * Replaces: probe_phase (csrc/fused_sampling.cu:475-501, csrc/bindings.cpp:23). */
+FS_API fs_status fs_probe_phase(const fs_sample_args* args, fs_stream_t stream);
+
+/* ---- vocab-sharded tensor parallelism (no counterpart in the reference) -------------------
+ * Packed candidate = (order_key << 32) | (0xFFFFFFFF - global_id), where order_key is the
+ * 16-bit order-preserving key of the logit (-0 folded onto +0). Larger packed value = larger
+ * logit, lower id on ties. Each row of a candidate block holds K packed candidates sorted
+ * descending, followed by one status word (FS_ROW_* of the shard row). Padding is 0. */
+
+/* Local half: top-K candidates of a [B, V_shard] shard, ids offset by args->id_base.
+ * cand_out: device [B, K + 1] uint64. Uses args: logits, dtype, batch, vocab, row_stride,
+ * id_base, top_k, splits. */
+FS_API fs_status fs_shard_candidates(const fs_sample_args* args, uint64_t* cand_out, fs_stream_t stream);
+
+/* Merge half: exact top-k over `parts` candidate blocks laid out [parts, B, K + 1] (the
+ * all-gather of every shard's cand_out), then the softmax / top-p / draw tail. Every rank
+ * that runs it with the same rng produces the same ids. Uses args: dtype, batch, top_k (K),
+ * top_p, top_k_rows, top_p_rows, rng, out_ids, topk_ids, keep, renormed, row_status. */
+FS_API fs_status fs_merge_sample(const fs_sample_args* args, const uint64_t* cand, int32_t parts,
+                          fs_stream_t stream);
+
+/* ---- floor probes (measurement brackets) ---------------------------------------------------
+ * Replace: probe_noop / probe_scan_rowblock / probe_scan_split (csrc/probes.cu:86-125). */
+FS_API fs_status fs_probe_noop(int64_t* out, int64_t batch, fs_stream_t stream);
+/* argmax per row (lowest id on ties), one CTA per row. */
+FS_API fs_status fs_probe_scan_rowblock(const void* logits, int32_t dtype, int64_t batch, int64_t vocab,
+                                 int64_t row_stride, int64_t* out, fs_stream_t stream);
+/* argmax per row with `splits` CTAs per row, merged through a thread-block cluster. */
+FS_API fs_status fs_probe_scan_split(const void* logits, int32_t dtype, int64_t batch, int64_t vocab,
+                              int64_t row_stride, int32_t splits, int64_t* out,
+                              fs_stream_t stream);
+
+/* ---- introspection ------------------------------------------------------------------------
+ * Replaces: kernel_attrs (csrc/fused_sampling.cu:515-540, csrc/bindings.cpp:24). */
+typedef struct fs_kernel_attr {
+  char name[64];
+  int32_t param;          /* kernel variant parameter (uint4 chunks per thread, or 0)   */
+  int32_t block;          /* threads per CTA                                            */
+  int32_t regs;           /* registers per thread                                       */
+  int32_t local_bytes;    /* local (spill) memory per thread                            */
+  int32_t static_smem;    /* static shared memory per CTA                               */
+  int32_t blocks_per_sm;  /* theoretical resident CTAs per SM at the typical smem size  */
+} fs_kernel_attr;
+
+/* Fills up to `cap` rows, returns the number of kernels described (may exceed cap), or -1. */
+FS_API int32_t fs_kernel_attrs(fs_kernel_attr* rows, int32_t cap);
+
+/* Human-readable message of the last error raised on the calling host thread. */
+FS_API const char* fs_last_error(void);
+
+/* Plan of a call, for logging and tests: CTAs per row (cluster size), uint4 chunks per
+ * thread, threads per CTA, survivor capacity, and maxima per thread / lanes per maximum. */
+typedef struct fs_plan_info {
+  int32_t splits;
+  int32_t chunks;
+  int32_t threads;
+  int32_t capacity;
+  int32_t maxima_per_thread;
+  int32_t lanes_per_max;
+  int32_t smem_bytes;
+} fs_plan_info;
+FS_API fs_status fs_plan(int64_t batch, int64_t vocab, int64_t top_k, int32_t splits, fs_plan_info* out);
+
+/* Library version string. */
+FS_API const char* fs_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FUSED_SAMPLING_B200_H */

@@ -1,0 +1,1073 @@
+// Fused top-k / top-p sampler for B200 (sm_100a): one thread-block cluster per row.
+//
+// Design (one launch per call, logits read from HBM exactly once):
+//   * The row is split across the S CTAs of a cluster (S <= 16). Each thread holds its part of
+//     the row in registers (C x 16-byte vectors) for the whole kernel.
+//   * Phase 1 - maxima: each thread reduces its values to a few sub-chunk maxima with the
+//     NaN-propagating packed max (two logits per instruction). The maxima also classify the
+//     row (NaN / +inf / all -inf).
+//   * Phase 2 - threshold: the maxima are counted into a 4096-bin histogram of the 16-bit order
+//     key held in the leader CTA's shared memory (remote atomics over distributed shared
+//     memory). The bin where the suffix count reaches k gives L, a value that at least k
+//     distinct elements reach, so every element of the top-k is >= L.
+//   * Phase 3/4 - filter: every element >= L (packed compare, two logits per instruction) is
+//     a survivor; survivors are written as packed (key, ~id) words into the leader's buffer in
+//     a deterministic order. Typically about 1.2k of them remain.
+//   * If the survivors overflow the buffer (heavy ties: constant rows, few distinct values),
+//     an exact two-level 8-bit radix select over the register-resident data finds the k-th
+//     key T, and the lowest-id ties at T are chosen by an id-ordered prefix count.
+//   * Phase 5..7 in the leader: bitonic sort of the survivors (value desc, id asc), FP32
+//     softmax over the top k (expf, no fast-math), cumulative sum accumulated in double and
+//     rounded per element, exclusive-prefix top-p cut, inverse-CDF draw against u * Z_p.
+//
+// Reference algorithm followed (sathviknookala/llm_sampling_kernel):
+//   selection semantics  benchmarks/reference.py:47-54 (stable descending sort, first k)
+//   softmax/cumsum/cut   benchmarks/reference.py:55-62, csrc/fused_sampling.cu:264-293
+//   draw                 csrc/fused_sampling.cu:294-309
+//   phase ablation       csrc/fused_sampling.cu:168-214,475-501
+#include <cooperative_groups.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "fs_device.cuh"
+#include "fs_internal.h"
+
+namespace cg = cooperative_groups;
+
+namespace fsb {
+
+constexpr int NT = 256;  // threads per CTA (the fallback histograms assume NT == 256)
+static_assert(NT == 256, "fallback radix passes map one thread per 8-bit bin");
+
+struct Params {
+  const uint16_t* logits;
+  int64_t row_stride;
+  int32_t vocab;
+  int32_t K;  // bound on k: min(top_k, V)
+  uint32_t id_base;
+  float top_p;
+  const int32_t* k_rows;
+  const float* p_rows;
+  const float* uniforms;
+  uint64_t seed, offset;
+  const int64_t* seed_ptr;
+  const int64_t* offset_ptr;
+  uint64_t offset_intragraph;
+  int64_t row_base;
+  int64_t* out;
+  int64_t* topk_ids;
+  uint8_t* keep;
+  float* renormed;
+  int32_t* status;
+  uint64_t* cand_out;  // shard candidates, [B, K + 1]
+  int32_t cap;         // survivor capacity, power of two
+  int32_t mpt;         // maxima per thread: 1, 2, 4 or 8
+  int32_t mgroup;      // lanes per maximum (power of two <= 32), used when mpt == 1
+  int32_t vec;         // 16-byte vector loads allowed
+  int32_t stop;        // 0 = full pipeline, else ablation phase
+  int32_t mode;        // kModeSample / kModeTopk / kModeShard
+};
+
+constexpr int kModeSample = 0;
+constexpr int kModeTopk = 1;
+constexpr int kModeShard = 2;
+
+// ctl[] slots
+constexpr int kCtlFlags = 0;     // leader: OR of row flags pushed by every CTA
+constexpr int kCtlLocalFlags = 1;
+constexpr int kCtlLKey = 2;      // broadcast: threshold key
+constexpr int kCtlStatus = 3;    // broadcast: row status
+constexpr int kCtlBin = 4;       // leader scratch: boundary bin
+constexpr int kCtlHb = 5;        // fallback scratch
+constexpr int kCtlAbove = 6;
+constexpr int kCtlT = 7;
+constexpr int kCtlNgt = 8;
+
+constexpr uint32_t kFlagNaN = 1u, kFlagPosInf = 2u, kFlagAboveNegInf = 4u;
+
+struct alignas(16) Shared {
+  uint32_t hist[kHistBins];   // leader: histogram of maxima (key >> 4)
+  uint32_t fh1[256];          // leader: fallback level-1 histogram (key >> 8)
+  uint32_t fh2[256];          // leader: fallback level-2 histogram (key & 0xFF at hb)
+  uint32_t lh[256];           // local histogram before it is pushed
+  uint32_t cnt[kMaxSplits];   // per-rank survivor counts (written by every rank)
+  uint32_t cnt2[kMaxSplits];  // per-rank tie counts (fallback)
+  uint32_t ctl[16];
+  int iscr[40];
+  uint32_t uscr[40];
+  double dscr[40];
+};
+
+__host__ __device__ constexpr size_t shared_bytes(int cap) {
+  return sizeof(Shared) + static_cast<size_t>(cap) * (sizeof(uint64_t) + 2 * sizeof(float));
+}
+
+extern __shared__ __align__(16) unsigned char g_smem[];
+
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int q) {
+  return q == 0 ? v.x : q == 1 ? v.y : q == 2 ? v.z : v.w;
+}
+
+// Warp-aggregated shared-memory histogram add: lanes with the same bin elect one adder.
+// All 32 lanes must call it.
+__device__ __forceinline__ void hist_add_warp(uint32_t* h, uint32_t bin, bool valid) {
+  const uint32_t tag = valid ? bin : 0xFFFFFFFFu;
+  const unsigned peers = __match_any_sync(0xFFFFFFFFu, tag);
+  if (valid && (threadIdx.x & 31) == (__ffs(peers) - 1)) atomicAdd(&h[bin], __popc(peers));
+}
+
+__device__ __forceinline__ float row_uniform(const Params& p, int b) {
+  if (p.uniforms != nullptr) return p.uniforms[b];
+  uint64_t seed = p.seed, off = p.offset;
+  if (p.seed_ptr != nullptr) {
+    seed = static_cast<uint64_t>(*p.seed_ptr);
+    off = static_cast<uint64_t>(*p.offset_ptr) + p.offset_intragraph;
+  }
+  return splitmix_uniform(seed, off, static_cast<uint64_t>(p.row_base + b));
+}
+
+// Writes the outputs of a row that cannot be sampled (bad input or parameters).
+__device__ void write_invalid_row(const Params& p, int b, int st) {
+  const int t = threadIdx.x;
+  if (t == 0) {
+    if (p.out != nullptr) p.out[b] = -1;
+    if (p.status != nullptr) p.status[b] = st;
+  }
+  for (int i = t; i < p.K; i += NT) {
+    const size_t o = static_cast<size_t>(b) * p.K + i;
+    if (p.topk_ids != nullptr) p.topk_ids[o] = -1;
+    if (p.keep != nullptr) p.keep[o] = 0;
+    if (p.renormed != nullptr) p.renormed[o] = 0.0f;
+  }
+  if (p.cand_out != nullptr) {
+    uint64_t* co = p.cand_out + static_cast<size_t>(b) * (p.K + 1);
+    for (int i = t; i < p.K; i += NT) co[i] = 0ull;
+    if (t == 0) co[p.K] = static_cast<uint64_t>(st);
+  }
+}
+
+// FP32 softmax over the top kk sorted candidates, exclusive-prefix top-p cut, inverse-CDF draw.
+// cand: shared, sorted descending, >= kk valid entries. All NT threads call it.
+template <int DT>
+__device__ void sample_tail(const Params& p, int b, const uint64_t* cand, int kk, float pp,
+                            float* prob, float* cum, double* dscr, int* iscr) {
+  const int t = threadIdx.x;
+  const float m = key_to_float<DT>(packed_key(cand[0]));
+  double part = 0.0;
+  for (int i = t; i < kk; i += NT) {
+    const float w = expf(key_to_float<DT>(packed_key(cand[i])) - m);
+    prob[i] = w;
+    part += static_cast<double>(w);
+  }
+  const float z = static_cast<float>(block_sum<double, NT>(part, dscr));
+  for (int i = t; i < kk; i += NT) prob[i] = prob[i] / z;
+  __syncthreads();
+
+  // Inclusive cumulative sum accumulated in double and rounded once per element.
+  const int ipt = (kk + NT - 1) / NT;
+  const int lo = min(kk, t * ipt), hi = min(kk, lo + ipt);
+  double run = 0.0;
+  for (int i = lo; i < hi; ++i) run += static_cast<double>(prob[i]);
+  double total;
+  double acc = block_incl_scan<double, NT>(run, dscr, &total) - run;
+  for (int i = lo; i < hi; ++i) {
+    acc += static_cast<double>(prob[i]);
+    cum[i] = static_cast<float>(acc);
+  }
+  __syncthreads();
+
+  // r = (first i >= 1 with !((c_i - p_i) < p)) - 1, or kk - 1 when p >= 1.
+  int fail = kk;
+  if (pp < 1.0f) {
+    for (int i = t; i < kk; i += NT)
+      if (i >= 1 && !((cum[i] - prob[i]) < pp)) fail = min(fail, i);
+  }
+  fail = block_min<NT>(fail, iscr);
+  const int r = fail - 1;
+  if (p.stop == 6) {
+    if (t == 0) p.out[b] = r + 1;
+    return;
+  }
+  const float zp = cum[r];
+  const float target = row_uniform(p, b) * zp;
+  int pick = r;
+  for (int i = t; i <= r; i += NT)
+    if (cum[i] >= target) pick = min(pick, i);
+  pick = block_min<NT>(pick, iscr);
+
+  if (t == 0) {
+    if (p.out != nullptr) p.out[b] = static_cast<int64_t>(packed_id(cand[pick]));
+    if (p.status != nullptr) p.status[b] = FS_ROW_OK;
+  }
+  for (int i = t; i < p.K; i += NT) {
+    const size_t o = static_cast<size_t>(b) * p.K + i;
+    if (p.topk_ids != nullptr) p.topk_ids[o] = i < kk ? static_cast<int64_t>(packed_id(cand[i])) : -1;
+    if (p.keep != nullptr) p.keep[o] = (i <= r) ? 1 : 0;
+    if (p.renormed != nullptr) p.renormed[o] = (i <= r) ? prob[i] / zp : 0.0f;
+  }
+}
+
+// Per-row k and p (a bad per-row value marks the row FS_ROW_BAD_PARAM).
+__device__ __forceinline__ void row_params(const Params& p, int b, int* kk, float* pp, bool* bad) {
+  *kk = p.K;
+  *pp = p.top_p;
+  *bad = false;
+  if (p.k_rows != nullptr) {
+    const int kr = p.k_rows[b];
+    if (kr < 1) *bad = true;
+    *kk = min(max(kr, 1), p.K);
+  }
+  if (p.p_rows != nullptr) {
+    const float pr = p.p_rows[b];
+    if (!(pr > 0.0f && pr <= 1.0f)) *bad = true;
+    *pp = pr;
+  }
+}
+
+// One 16-byte chunk (8 logits) of a row starting at element e0; lanes at or past V read as -inf.
+template <int DT>
+__device__ __forceinline__ uint4 load_chunk(const uint16_t* __restrict__ row, int e0, int V, int vec) {
+  if (vec && e0 + 8 <= V) return __ldg(reinterpret_cast<const uint4*>(row) + (e0 >> 3));
+  uint32_t w[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t lo16 = (e0 + 2 * q < V) ? static_cast<uint32_t>(row[e0 + 2 * q]) : Fmt<DT>::kNegInf;
+    const uint32_t hi16 = (e0 + 2 * q + 1 < V) ? static_cast<uint32_t>(row[e0 + 2 * q + 1]) : Fmt<DT>::kNegInf;
+    w[q] = lo16 | (hi16 << 16);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Exact top-kk selection of the cluster's row, used when the survivor filter overflows the
+// buffer (heavy ties). Two 8-bit radix levels over the order key give the k-th key T and the
+// count above it (csrc/fused_sampling.cu:163-209 computes the same two levels per slice);
+// the ties at T are then ranked in id order - rank boundaries follow the (rank, chunk,
+// thread, lane) layout, which is increasing in token id - and the lowest `need` are kept.
+// The slice is re-read from global memory (L2) chunk by chunk, so this rare path does not
+// hold the row in registers. Every thread of every CTA of the cluster calls it; it writes kk
+// packed candidates into the leader's buffer and returns kk.
+template <int DT, int C>
+__device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict__ row, int V, int vec,
+                                         uint32_t id_base, int vbase, int kk, uint64_t* lsurv) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int S = static_cast<int>(cluster.num_blocks());
+  const int s = static_cast<int>(cluster.block_rank());
+  const int t = threadIdx.x;
+
+  // level 1: high byte
+  sh.lh[t] = 0u;
+  __syncthreads();
+#pragma unroll 1
+  for (int c = 0; c < C; ++c) {
+    const int e0 = (vbase + c * NT + t) * 8;
+    const uint4 v = load_chunk<DT>(row, e0, V, vec);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t w = word_of(v, q);
+      hist_add_warp(sh.lh, order_key(w & 0xFFFFu) >> 8, e0 + 2 * q < V);
+      hist_add_warp(sh.lh, order_key(w >> 16) >> 8, e0 + 2 * q + 1 < V);
+    }
+  }
+  __syncthreads();
+  if (sh.lh[t] != 0u) atomicAdd(cluster.map_shared_rank(&sh.fh1[t], 0), sh.lh[t]);
+  cluster.sync();  // F1
+  {
+    const uint32_t h = *cluster.map_shared_rank(&sh.fh1[255 - t], 0);
+    uint32_t total;
+    const uint32_t inc = block_incl_scan<uint32_t, NT>(h, sh.uscr, &total);
+    if (inc >= static_cast<uint32_t>(kk) && inc - h < static_cast<uint32_t>(kk)) {
+      sh.ctl[kCtlHb] = static_cast<uint32_t>(255 - t);
+      sh.ctl[kCtlAbove] = inc - h;
+    }
+    sh.lh[t] = 0u;
+    __syncthreads();
+  }
+  const uint32_t hb = sh.ctl[kCtlHb];
+  const uint32_t n_above = sh.ctl[kCtlAbove];
+
+  // level 2: low byte inside bucket hb
+#pragma unroll 1
+  for (int c = 0; c < C; ++c) {
+    const int e0 = (vbase + c * NT + t) * 8;
+    const uint4 v = load_chunk<DT>(row, e0, V, vec);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t w = word_of(v, q);
+      const uint32_t k0 = order_key(w & 0xFFFFu), k1 = order_key(w >> 16);
+      hist_add_warp(sh.lh, k0 & 0xFFu, e0 + 2 * q < V && (k0 >> 8) == hb);
+      hist_add_warp(sh.lh, k1 & 0xFFu, e0 + 2 * q + 1 < V && (k1 >> 8) == hb);
+    }
+  }
+  __syncthreads();
+  if (sh.lh[t] != 0u) atomicAdd(cluster.map_shared_rank(&sh.fh2[t], 0), sh.lh[t]);
+  cluster.sync();  // F2
+  {
+    const uint32_t want = static_cast<uint32_t>(kk) - n_above;
+    const uint32_t h = *cluster.map_shared_rank(&sh.fh2[255 - t], 0);
+    uint32_t total;
+    const uint32_t inc = block_incl_scan<uint32_t, NT>(h, sh.uscr, &total);
+    if (inc >= want && inc - h < want) {
+      sh.ctl[kCtlT] = (hb << 8) | static_cast<uint32_t>(255 - t);
+      sh.ctl[kCtlNgt] = n_above + inc - h;
+    }
+    __syncthreads();
+  }
+  const uint32_t T = sh.ctl[kCtlT];
+  const uint32_t n_gt = sh.ctl[kCtlNgt];
+  const uint32_t need = static_cast<uint32_t>(kk) - n_gt;
+
+  // counts of keys > T and == T per thread, then per rank
+  uint32_t ngt = 0u, ntie = 0u;
+#pragma unroll 1
+  for (int c = 0; c < C; ++c) {
+    const int e0 = (vbase + c * NT + t) * 8;
+    const uint4 v = load_chunk<DT>(row, e0, V, vec);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t w = word_of(v, q);
+      const uint32_t k0 = order_key(w & 0xFFFFu), k1 = order_key(w >> 16);
+      if (e0 + 2 * q < V) {
+        ngt += k0 > T;
+        ntie += k0 == T;
+      }
+      if (e0 + 2 * q + 1 < V) {
+        ngt += k1 > T;
+        ntie += k1 == T;
+      }
+    }
+  }
+  uint32_t gt_total, tie_total;
+  const uint32_t gt_off = block_incl_scan<uint32_t, NT>(ngt, sh.uscr, &gt_total) - ngt;
+  block_incl_scan<uint32_t, NT>(ntie, sh.uscr, &tie_total);
+  if (t < S) {
+    cluster.map_shared_rank(sh.cnt, t)[s] = gt_total;
+    cluster.map_shared_rank(sh.cnt2, t)[s] = tie_total;
+  }
+  cluster.sync();  // F3
+  uint32_t gt_base = 0u, tie_base = 0u;
+  for (int r = 0; r < s; ++r) {
+    gt_base += sh.cnt[r];
+    tie_base += sh.cnt2[r];
+  }
+  // keys strictly above T, and the ties at T ranked in id order
+  uint32_t slot = gt_base + gt_off;
+  uint32_t chunk_base = tie_base;
+#pragma unroll 1
+  for (int c = 0; c < C; ++c) {
+    const int e0 = (vbase + c * NT + t) * 8;
+    const uint4 v = load_chunk<DT>(row, e0, V, vec);
+    uint32_t mask = 0u;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t w = word_of(v, q);
+      const uint32_t k0 = order_key(w & 0xFFFFu), k1 = order_key(w >> 16);
+      if (e0 + 2 * q < V) {
+        if (k0 > T) lsurv[slot++] = pack(k0, id_base + e0 + 2 * q);
+        if (k0 == T) mask |= 1u << (2 * q);
+      }
+      if (e0 + 2 * q + 1 < V) {
+        if (k1 > T) lsurv[slot++] = pack(k1, id_base + e0 + 2 * q + 1);
+        if (k1 == T) mask |= 1u << (2 * q + 1);
+      }
+    }
+    const uint32_t cnt = __popc(mask);
+    uint32_t ctot;
+    const uint32_t excl = block_incl_scan<uint32_t, NT>(cnt, sh.uscr, &ctot) - cnt;
+    uint32_t rank = chunk_base + excl;
+    while (mask != 0u && rank < need) {
+      const int j = __ffs(mask) - 1;
+      mask &= mask - 1;
+      lsurv[n_gt + rank] = pack(T, id_base + e0 + j);
+      ++rank;
+    }
+    chunk_base += ctot;
+  }
+  return kk;
+}
+
+template <int DT, int C>
+__global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int S = static_cast<int>(cluster.num_blocks());
+  const int s = static_cast<int>(cluster.block_rank());
+  const int b = blockIdx.y;
+  const int t = threadIdx.x;
+  const bool leader = (s == 0);
+  const int V = p.vocab;
+
+  Shared& sh = *reinterpret_cast<Shared*>(g_smem);
+  uint64_t* surv = reinterpret_cast<uint64_t*>(g_smem + sizeof(Shared));
+  float* prob = reinterpret_cast<float*>(surv + p.cap);
+  float* cum = prob + p.cap;
+
+  int kk;
+  float pp;
+  bool bad;
+  row_params(p, b, &kk, &pp, &bad);
+
+  // ---- issue every load of this thread's slice (one HBM read of the row) ----
+  const uint16_t* row = p.logits + static_cast<int64_t>(b) * p.row_stride;
+  const int vbase = s * C * NT;
+  uint4 v[C];
+#pragma unroll
+  for (int c = 0; c < C; ++c) v[c] = load_chunk<DT>(row, (vbase + c * NT + t) * 8, V, p.vec);
+
+  // ---- shared-memory init, then the first cluster barrier ----
+  if (leader) {
+    for (int i = t; i < kHistBins; i += NT) sh.hist[i] = 0u;
+    for (int i = t; i < 256; i += NT) {
+      sh.fh1[i] = 0u;
+      sh.fh2[i] = 0u;
+    }
+  }
+  if (t < 16) sh.ctl[t] = 0u;
+  if (t == 0) sh.ctl[kCtlBin] = 0xFFFFFFFFu;
+  cluster.sync();  // B1: every CTA of the cluster is running; leader state is zeroed
+
+  // ---- phase 1: sub-chunk maxima ----
+  uint32_t mx[4] = {Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2};
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) mx[q] = pair_max_nan<DT>(mx[q], word_of(v[c], q));
+  }
+  uint32_t m16[8];
+  int nm;
+  if (p.mpt == 8) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      m16[2 * q] = mx[q] & 0xFFFFu;
+      m16[2 * q + 1] = mx[q] >> 16;
+    }
+    nm = 8;
+  } else if (p.mpt == 4) {
+    const uint32_t a = pair_max_nan<DT>(mx[0], mx[2]), c2 = pair_max_nan<DT>(mx[1], mx[3]);
+    m16[0] = a & 0xFFFFu;
+    m16[1] = a >> 16;
+    m16[2] = c2 & 0xFFFFu;
+    m16[3] = c2 >> 16;
+    nm = 4;
+  } else {
+    const uint32_t a = pair_max_nan<DT>(pair_max_nan<DT>(mx[0], mx[2]), pair_max_nan<DT>(mx[1], mx[3]));
+    if (p.mpt == 2) {
+      m16[0] = a & 0xFFFFu;
+      m16[1] = a >> 16;
+      nm = 2;
+    } else {
+      uint32_t m1 = half_max_nan<DT>(a & 0xFFFFu, a >> 16);
+      for (int off = 1; off < p.mgroup; off <<= 1)
+        m1 = half_max_nan<DT>(m1, __shfl_xor_sync(0xFFFFFFFFu, m1, off));
+      m16[0] = m1;
+      nm = ((t & (p.mgroup - 1)) == 0) ? 1 : 0;
+    }
+  }
+  if (p.stop == 1) {
+    if (leader && t == 0) p.out[b] = static_cast<int64_t>(m16[0]);
+    return;  // no distributed shared memory access is pending
+  }
+
+  // ---- phase 2: maxima histogram in the leader + row flags ----
+  uint32_t* lhist = cluster.map_shared_rank(sh.hist, 0);
+  uint32_t flags = 0u;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (i >= nm) break;
+    const uint32_t bits = m16[i];
+    if (Fmt<DT>::is_nan(bits)) {
+      flags |= kFlagNaN;
+    } else {
+      if (bits == Fmt<DT>::kPosInf) flags |= kFlagPosInf;
+      if (bits != Fmt<DT>::kNegInf) flags |= kFlagAboveNegInf;
+    }
+    atomicAdd(lhist + (order_key(bits) >> 4), 1u);
+  }
+  flags = __reduce_or_sync(0xFFFFFFFFu, flags);
+  if ((t & 31) == 0 && flags != 0u) atomicOr(&sh.ctl[kCtlLocalFlags], flags);
+  __syncthreads();
+  if (t == 0 && sh.ctl[kCtlLocalFlags] != 0u)
+    atomicOr(cluster.map_shared_rank(&sh.ctl[kCtlFlags], 0), sh.ctl[kCtlLocalFlags]);
+  cluster.sync();  // B2: leader histogram and flags are complete
+  if (p.stop == 2) {
+    if (leader && t == 0) p.out[b] = static_cast<int64_t>(sh.ctl[kCtlFlags]);
+    return;
+  }
+
+  // ---- phase 3: threshold in the leader, broadcast to every rank ----
+  if (leader) {
+    const uint32_t f = sh.ctl[kCtlFlags];
+    int st = FS_ROW_OK;
+    if (bad) st = FS_ROW_BAD_PARAM;
+    else if (f & kFlagNaN) st = FS_ROW_NAN;
+    else if (f & kFlagPosInf) st = FS_ROW_POSINF;
+    else if (!(f & kFlagAboveNegInf)) st = FS_ROW_ALL_NEGINF;
+    uint32_t lkey = order_key(Fmt<DT>::kNegInf);
+    if (st == FS_ROW_OK) {
+      constexpr int BPT = kHistBins / NT;
+      const int hi = kHistBins - 1 - t * BPT;
+      uint32_t sum = 0u;
+#pragma unroll
+      for (int j = 0; j < BPT; ++j) sum += sh.hist[hi - j];
+      uint32_t total;
+      const uint32_t inc = block_incl_scan<uint32_t, NT>(sum, sh.uscr, &total);
+      const uint32_t want = static_cast<uint32_t>(kk);
+      if (inc >= want && inc - sum < want) {
+        uint32_t acc = inc - sum;
+        for (int j = 0; j < BPT; ++j) {
+          acc += sh.hist[hi - j];
+          if (acc >= want) {
+            sh.ctl[kCtlBin] = static_cast<uint32_t>(hi - j);
+            break;
+          }
+        }
+      }
+      __syncthreads();
+      const uint32_t bin = sh.ctl[kCtlBin];
+      if (bin != 0xFFFFFFFFu) lkey = max(bin << 4, order_key(Fmt<DT>::kNegInf));
+    }
+    for (int r = t; r < S; r += NT) {
+      uint32_t* rc = cluster.map_shared_rank(sh.ctl, r);
+      rc[kCtlLKey] = lkey;
+      rc[kCtlStatus] = static_cast<uint32_t>(st);
+    }
+  }
+  cluster.sync();  // B3: threshold and row status visible in every rank
+  const int st = static_cast<int>(sh.ctl[kCtlStatus]);
+  const uint32_t lkey = sh.ctl[kCtlLKey];
+  if (st != FS_ROW_OK) {
+    if (leader) write_invalid_row(p, b, st);
+    return;
+  }
+  if (p.stop == 3) {
+    if (leader && t == 0) p.out[b] = static_cast<int64_t>(lkey);
+    return;
+  }
+
+  // ---- phase 4: survivors (every element >= L), staged locally, then placed in the leader ----
+  // Staging reuses this CTA's prob/cum region (cap packed words); the leader's surv[] is the
+  // destination of every rank. Order inside a rank's segment is arbitrary; the sort fixes it.
+  const uint32_t lbits = key_to_bits(lkey);
+  const uint32_t l2 = lbits | (lbits << 16);
+  uint64_t* stage = reinterpret_cast<uint64_t*>(prob);
+  if (t == 0) sh.ctl[kCtlLocalFlags] = 0u;  // reused as the local survivor counter
+  __syncthreads();
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t w = word_of(v[c], q);
+      const uint32_t m = pair_ge_mask<DT>(w, l2);
+      if (m != 0u) {
+        const int e = (vbase + c * NT + t) * 8 + 2 * q;
+        if ((m & 0xFFFFu) && e < V) {
+          const uint32_t slot = atomicAdd(&sh.ctl[kCtlLocalFlags], 1u);
+          if (slot < static_cast<uint32_t>(p.cap)) stage[slot] = pack(order_key(w & 0xFFFFu), p.id_base + e);
+        }
+        if ((m >> 16) && e + 1 < V) {
+          const uint32_t slot = atomicAdd(&sh.ctl[kCtlLocalFlags], 1u);
+          if (slot < static_cast<uint32_t>(p.cap)) stage[slot] = pack(order_key(w >> 16), p.id_base + e + 1);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const uint32_t cta_total = sh.ctl[kCtlLocalFlags];
+  if (t < S) cluster.map_shared_rank(sh.cnt, t)[s] = cta_total;
+  cluster.sync();  // B4a: every rank knows every rank's survivor count
+  uint32_t n_surv = 0u, base = 0u;
+  for (int r = 0; r < S; ++r) {
+    const uint32_t cr = sh.cnt[r];
+    base += (r < s) ? cr : 0u;
+    n_surv += cr;
+  }
+  uint64_t* lsurv = cluster.map_shared_rank(surv, 0);
+  if (n_surv <= static_cast<uint32_t>(p.cap)) {
+    for (uint32_t i = t; i < cta_total; i += NT) lsurv[base + i] = stage[i];
+  } else {
+    n_surv = static_cast<uint32_t>(
+        exact_select<DT, C>(sh, row, V, p.vec, p.id_base, vbase, kk, lsurv));
+  }
+  cluster.sync();  // B4b: the leader holds every survivor
+  if (!leader) return;
+  if (p.stop == 4) {
+    if (t == 0) p.out[b] = static_cast<int64_t>(n_surv);
+    return;
+  }
+
+  // ---- phase 5: sort the survivors (value desc, id asc) ----
+  const int n = static_cast<int>(n_surv);
+  int P = 32;
+  while (P < n) P <<= 1;
+  for (int i = n + t; i < P; i += NT) surv[i] = 0ull;
+  __syncthreads();
+  block_sort_desc<NT>(surv, P);
+  if (p.stop == 5) {
+    if (t == 0) p.out[b] = static_cast<int64_t>(packed_id(surv[0]));
+    return;
+  }
+  if (p.mode == kModeTopk) {
+    for (int i = t; i < p.K; i += NT)
+      p.topk_ids[static_cast<size_t>(b) * p.K + i] = i < kk ? static_cast<int64_t>(packed_id(surv[i])) : -1;
+    if (t == 0 && p.status != nullptr) p.status[b] = FS_ROW_OK;
+    return;
+  }
+  if (p.mode == kModeShard) {
+    uint64_t* co = p.cand_out + static_cast<size_t>(b) * (p.K + 1);
+    for (int i = t; i < p.K; i += NT) co[i] = i < kk ? surv[i] : 0ull;
+    if (t == 0) co[p.K] = FS_ROW_OK;
+    return;
+  }
+  // ---- phase 6/7: softmax, top-p cut, draw ----
+  sample_tail<DT>(p, b, surv, kk, pp, prob, cum, sh.dscr, sh.iscr);
+}
+
+// Merge of per-shard candidate blocks [parts, B, K + 1] for vocab-sharded tensor parallelism:
+// one CTA per row, exact top-k over parts*K packed candidates, then the same tail.
+template <int DT>
+__global__ void __launch_bounds__(NT) fs_merge_kernel(const Params p, const uint64_t* __restrict__ cand,
+                                                      int parts, int64_t B) {
+  Shared& sh = *reinterpret_cast<Shared*>(g_smem);
+  uint64_t* surv = reinterpret_cast<uint64_t*>(g_smem + sizeof(Shared));
+  float* prob = reinterpret_cast<float*>(surv + p.cap);
+  float* cum = prob + p.cap;
+  const int b = blockIdx.x;
+  const int t = threadIdx.x;
+  int kk;
+  float pp;
+  bool bad;
+  row_params(p, b, &kk, &pp, &bad);
+  const int n = parts * p.K;
+  int P = 32;
+  while (P < n) P <<= 1;
+  for (int i = t; i < P; i += NT) {
+    uint64_t x = 0ull;
+    if (i < n) {
+      const int part = i / p.K, j = i - part * p.K;
+      x = cand[(static_cast<size_t>(part) * B + b) * (p.K + 1) + j];
+    }
+    surv[i] = x;
+  }
+  // Combined row status: NaN or +inf in any shard; all -inf only if every shard is.
+  if (t == 0) {
+    int nan = 0, inf = 0, neg = 0;
+    for (int part = 0; part < parts; ++part) {
+      const uint64_t w = cand[(static_cast<size_t>(part) * B + b) * (p.K + 1) + p.K];
+      nan |= w == FS_ROW_NAN;
+      inf |= w == FS_ROW_POSINF;
+      neg += w == FS_ROW_ALL_NEGINF;
+    }
+    int st = bad ? FS_ROW_BAD_PARAM
+                 : nan ? FS_ROW_NAN : inf ? FS_ROW_POSINF : (neg == parts ? FS_ROW_ALL_NEGINF : FS_ROW_OK);
+    sh.ctl[kCtlStatus] = static_cast<uint32_t>(st);
+  }
+  __syncthreads();
+  const int st = static_cast<int>(sh.ctl[kCtlStatus]);
+  if (st != FS_ROW_OK) {
+    write_invalid_row(p, b, st);
+    return;
+  }
+  block_sort_desc<NT>(surv, P);
+  // A shard that held fewer than K real values padded with 0; kk never exceeds the real count
+  // because the global row holds sum(V_shard) >= kk values.
+  if (p.mode == kModeTopk) {
+    for (int i = t; i < p.K; i += NT)
+      p.topk_ids[static_cast<size_t>(b) * p.K + i] = i < kk ? static_cast<int64_t>(packed_id(surv[i])) : -1;
+    return;
+  }
+  sample_tail<DT>(p, b, surv, kk, pp, prob, cum, sh.dscr, sh.iscr);
+}
+
+// ------------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------------
+
+using KernelFn = void (*)(const Params);
+
+constexpr int kChunkOptions[] = {1, 2, 3, 4, 5, 6, 8, 10, 12, 16};
+
+template <int DT>
+KernelFn cluster_kernel_for(int C) {
+  switch (C) {
+    case 1: return fs_cluster_kernel<DT, 1>;
+    case 2: return fs_cluster_kernel<DT, 2>;
+    case 3: return fs_cluster_kernel<DT, 3>;
+    case 4: return fs_cluster_kernel<DT, 4>;
+    case 5: return fs_cluster_kernel<DT, 5>;
+    case 6: return fs_cluster_kernel<DT, 6>;
+    case 8: return fs_cluster_kernel<DT, 8>;
+    case 10: return fs_cluster_kernel<DT, 10>;
+    case 12: return fs_cluster_kernel<DT, 12>;
+    case 16: return fs_cluster_kernel<DT, 16>;
+    default: return nullptr;
+  }
+}
+
+static int pow2_ceil(int64_t x) {
+  int p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+static int pow2_floor(int64_t x) {
+  int p = 1;
+  while (static_cast<int64_t>(p) * 2 <= x) p <<= 1;
+  return p;
+}
+
+constexpr int kMaxCap = 8192;
+
+// Plan of one call: cluster size, chunks per thread, survivor capacity, maxima granularity.
+fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, PlanOut* out) {
+  const int64_t per_cta_chunk = static_cast<int64_t>(NT) * 8;  // elements per chunk per CTA
+  int S;
+  if (splits > 0) {
+    S = std::min<int>(splits, kMaxSplits);
+  } else {
+    S = (B <= 32) ? 16 : 8;
+    // small rows need fewer CTAs
+    const int64_t min_s = (V + per_cta_chunk - 1) / per_cta_chunk;
+    S = static_cast<int>(std::min<int64_t>(S, std::max<int64_t>(1, min_s)));
+  }
+  // smallest chunk option that covers the row
+  int C = 0;
+  for (int opt : kChunkOptions) {
+    if (static_cast<int64_t>(opt) * per_cta_chunk * S >= V) {
+      C = opt;
+      break;
+    }
+  }
+  if (C == 0) {
+    set_error("vocabulary of %lld does not fit %d CTAs x %d threads x 128 values",
+              static_cast<long long>(V), S, NT);
+    return FS_EUNSUPPORTED;
+  }
+  const int threads_total = S * NT;
+  int mpt = 1, mgroup = 1;
+  const int64_t target = 4 * K;
+  if (target <= threads_total) {
+    mgroup = std::min(32, pow2_floor(threads_total / target));
+  } else {
+    mpt = std::min<int64_t>(8, pow2_ceil((target + threads_total - 1) / threads_total));
+  }
+  int cap = std::max(256, pow2_ceil(4 * K));
+  cap = std::min(cap, kMaxCap);
+  if (cap < K) {
+    set_error("top_k of %lld exceeds the %d-candidate capacity of this build",
+              static_cast<long long>(K), kMaxCap);
+    return FS_EUNSUPPORTED;
+  }
+  out->splits = S;
+  out->chunks = C;
+  out->threads = NT;
+  out->capacity = cap;
+  out->mpt = mpt;
+  out->mgroup = mgroup;
+  out->smem = static_cast<int>(shared_bytes(cap));
+  return FS_OK;
+}
+
+static fs_status prepare_kernel(KernelFn fn, int S, int smem) {
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) {
+    set_error("cudaFuncSetAttribute(max dynamic smem %d): %s", smem, cudaGetErrorString(e));
+    return FS_ELAUNCH;
+  }
+  if (S > 8) {
+    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) {
+      set_error("cudaFuncSetAttribute(non-portable cluster): %s", cudaGetErrorString(e));
+      return FS_ELAUNCH;
+    }
+  }
+  return FS_OK;
+}
+
+static fs_status launch_cluster(int dtype, const PlanOut& plan, int64_t B, const Params& prm,
+                                cudaStream_t stream) {
+  KernelFn fn = dtype == FS_BF16 ? cluster_kernel_for<1>(plan.chunks) : cluster_kernel_for<0>(plan.chunks);
+  if (fn == nullptr) {
+    set_error("no kernel for %d chunks", plan.chunks);
+    return FS_EUNSUPPORTED;
+  }
+  fs_status st = prepare_kernel(fn, plan.splits, plan.smem);
+  if (st != FS_OK) return st;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan.splits, static_cast<unsigned>(B), 1);
+  cfg.blockDim = dim3(NT, 1, 1);
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = plan.splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, prm);
+  if (e != cudaSuccess) {
+    set_error("cluster launch (splits=%d chunks=%d smem=%d B=%lld): %s", plan.splits, plan.chunks,
+              plan.smem, static_cast<long long>(B), cudaGetErrorString(e));
+    return FS_ELAUNCH;
+  }
+  return FS_OK;
+}
+
+static fs_status check_common(const fs_sample_args* a, bool need_logits) {
+  if (a == nullptr) {
+    set_error("args is NULL");
+    return FS_EINVAL;
+  }
+  if (a->dtype != FS_F16 && a->dtype != FS_BF16) {
+    set_error("logits must be float16 or bfloat16");
+    return FS_EINVAL;
+  }
+  if (a->batch < 1 || a->batch > 65535) {
+    set_error("batch must be in [1, 65535], got %lld", static_cast<long long>(a->batch));
+    return FS_EINVAL;
+  }
+  if (need_logits) {
+    if (a->logits == nullptr) {
+      set_error("logits is NULL");
+      return FS_EINVAL;
+    }
+    if (a->vocab < 1 || a->vocab > (1 << 19)) {
+      set_error("vocab must be in [1, 524288], got %lld", static_cast<long long>(a->vocab));
+      return FS_EINVAL;
+    }
+    if (a->row_stride < a->vocab) {
+      set_error("row_stride %lld is smaller than vocab %lld", static_cast<long long>(a->row_stride),
+                static_cast<long long>(a->vocab));
+      return FS_EINVAL;
+    }
+    if (a->id_base < 0 || a->id_base + a->vocab > 0xFFFFFFFFll) {
+      set_error("id_base + vocab must fit in 32 bits");
+      return FS_EINVAL;
+    }
+  }
+  if (a->top_k < 1) {
+    set_error("top_k must be >= 1");
+    return FS_EINVAL;
+  }
+  return FS_OK;
+}
+
+static fs_status check_top_p(const fs_sample_args* a) {
+  if (a->top_p_rows == nullptr && !(a->top_p > 0.0f && a->top_p <= 1.0f)) {
+    set_error("top_p must be in (0, 1]");
+    return FS_EINVAL;
+  }
+  return FS_OK;
+}
+
+static Params base_params(const fs_sample_args* a, int64_t K) {
+  Params prm = {};
+  prm.logits = static_cast<const uint16_t*>(a->logits);
+  prm.row_stride = a->row_stride;
+  prm.vocab = static_cast<int32_t>(a->vocab);
+  prm.K = static_cast<int32_t>(K);
+  prm.id_base = static_cast<uint32_t>(a->id_base);
+  prm.top_p = a->top_p;
+  prm.k_rows = a->top_k_rows;
+  prm.p_rows = a->top_p_rows;
+  prm.uniforms = a->rng.uniforms;
+  prm.seed = a->rng.seed;
+  prm.offset = a->rng.offset;
+  prm.seed_ptr = a->rng.seed_ptr;
+  prm.offset_ptr = a->rng.offset_ptr;
+  prm.offset_intragraph = a->rng.offset_intragraph;
+  prm.row_base = a->rng.row_base;
+  prm.out = a->out_ids;
+  prm.topk_ids = a->topk_ids;
+  prm.keep = a->keep;
+  prm.renormed = a->renormed;
+  prm.status = a->row_status;
+  prm.vec = 0;
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(a->logits);
+  if (addr % 16 == 0 && a->row_stride % 8 == 0) prm.vec = 1;
+  return prm;
+}
+
+fs_status run_cluster(const fs_sample_args* a, int mode, uint64_t* cand_out, cudaStream_t stream) {
+  const int64_t K = std::min<int64_t>(a->top_k, a->vocab);
+  PlanOut plan;
+  fs_status st = make_plan(a->batch, a->vocab, K, a->splits, &plan);
+  if (st != FS_OK) return st;
+  Params prm = base_params(a, K);
+  prm.cand_out = cand_out;
+  prm.cap = plan.capacity;
+  prm.mpt = plan.mpt;
+  prm.mgroup = plan.mgroup;
+  prm.stop = a->stop_phase;
+  prm.mode = mode;
+  return launch_cluster(a->dtype, plan, a->batch, prm, stream);
+}
+
+fs_status run_merge(const fs_sample_args* a, const uint64_t* cand, int parts, cudaStream_t stream) {
+  const int64_t K = a->top_k;
+  const int64_t n = static_cast<int64_t>(parts) * K;
+  int cap = std::max(32, pow2_ceil(n));
+  if (cap > kMaxCap) {
+    set_error("parts * top_k = %lld exceeds the merge capacity %d", static_cast<long long>(n), kMaxCap);
+    return FS_EUNSUPPORTED;
+  }
+  Params prm = base_params(a, K);
+  prm.vec = 0;
+  prm.cap = cap;
+  prm.mode = a->topk_ids != nullptr && a->out_ids == nullptr ? kModeTopk : kModeSample;
+  const int smem = static_cast<int>(shared_bytes(cap));
+  auto fn = a->dtype == FS_BF16 ? fs_merge_kernel<1> : fs_merge_kernel<0>;
+  cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) {
+    set_error("cudaFuncSetAttribute(merge smem %d): %s", smem, cudaGetErrorString(e));
+    return FS_ELAUNCH;
+  }
+  fn<<<static_cast<unsigned>(a->batch), NT, smem, stream>>>(prm, cand, parts, a->batch);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("merge launch: %s", cudaGetErrorString(e));
+    return FS_ELAUNCH;
+  }
+  return FS_OK;
+}
+
+void append_cluster_attrs(std::vector<fs_kernel_attr>& rows) {
+  for (int dt = 0; dt < 2; ++dt) {
+    for (int C : kChunkOptions) {
+      KernelFn fn = dt ? cluster_kernel_for<1>(C) : cluster_kernel_for<0>(C);
+      fs_kernel_attr r = {};
+      std::snprintf(r.name, sizeof(r.name), "fs_cluster_kernel<%s>", dt ? "bf16" : "fp16");
+      r.param = C;
+      r.block = NT;
+      fill_attr(reinterpret_cast<const void*>(fn), NT, static_cast<int>(shared_bytes(256)), &r);
+      rows.push_back(r);
+    }
+    fs_kernel_attr r = {};
+    std::snprintf(r.name, sizeof(r.name), "fs_merge_kernel<%s>", dt ? "bf16" : "fp16");
+    r.param = 0;
+    r.block = NT;
+    fill_attr(reinterpret_cast<const void*>(dt ? fs_merge_kernel<1> : fs_merge_kernel<0>), NT,
+              static_cast<int>(shared_bytes(256)), &r);
+    rows.push_back(r);
+  }
+}
+
+}  // namespace fsb
+
+// ------------------------------------------------------------------------------------------
+// C ABI
+// ------------------------------------------------------------------------------------------
+
+extern "C" fs_status fs_sample(const fs_sample_args* a, fs_stream_t stream) {
+  fs_status st = fsb::check_common(a, true);
+  if (st != FS_OK) return st;
+  if ((st = fsb::check_top_p(a)) != FS_OK) return st;
+  if (a->out_ids == nullptr) {
+    fsb::set_error("out_ids is NULL");
+    return FS_EINVAL;
+  }
+  fs_sample_args b = *a;
+  b.stop_phase = 0;
+  return fsb::run_cluster(&b, fsb::kModeSample, nullptr, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" fs_status fs_topk(const fs_sample_args* a, fs_stream_t stream) {
+  fs_status st = fsb::check_common(a, true);
+  if (st != FS_OK) return st;
+  if (a->topk_ids == nullptr) {
+    fsb::set_error("topk_ids is NULL");
+    return FS_EINVAL;
+  }
+  fs_sample_args b = *a;
+  b.stop_phase = 0;
+  b.top_p = 1.0f;
+  b.top_p_rows = nullptr;
+  return fsb::run_cluster(&b, fsb::kModeTopk, nullptr, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" fs_status fs_probe_phase(const fs_sample_args* a, fs_stream_t stream) {
+  fs_status st = fsb::check_common(a, true);
+  if (st != FS_OK) return st;
+  if ((st = fsb::check_top_p(a)) != FS_OK) return st;
+  if (a->stop_phase < 1 || a->stop_phase > FS_NUM_PHASES) {
+    fsb::set_error("phase must be in [1, %d]", FS_NUM_PHASES);
+    return FS_EINVAL;
+  }
+  if (a->out_ids == nullptr) {
+    fsb::set_error("out_ids is NULL");
+    return FS_EINVAL;
+  }
+  fs_sample_args b = *a;
+  b.topk_ids = nullptr;
+  b.keep = nullptr;
+  b.renormed = nullptr;
+  if (b.stop_phase == FS_NUM_PHASES) b.stop_phase = 0;
+  return fsb::run_cluster(&b, fsb::kModeSample, nullptr, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" fs_status fs_shard_candidates(const fs_sample_args* a, uint64_t* cand_out,
+                                         fs_stream_t stream) {
+  fs_status st = fsb::check_common(a, true);
+  if (st != FS_OK) return st;
+  if (cand_out == nullptr) {
+    fsb::set_error("cand_out is NULL");
+    return FS_EINVAL;
+  }
+  if (a->top_k > a->vocab) {
+    fsb::set_error("shard top_k (%lld) must not exceed the shard vocab (%lld)",
+                   static_cast<long long>(a->top_k), static_cast<long long>(a->vocab));
+    return FS_EINVAL;
+  }
+  fs_sample_args b = *a;
+  b.stop_phase = 0;
+  b.top_k_rows = nullptr;
+  b.top_p_rows = nullptr;
+  b.top_p = 1.0f;
+  b.out_ids = nullptr;
+  b.topk_ids = nullptr;
+  b.keep = nullptr;
+  b.renormed = nullptr;
+  b.row_status = nullptr;
+  return fsb::run_cluster(&b, fsb::kModeShard, cand_out, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" fs_status fs_merge_sample(const fs_sample_args* a, const uint64_t* cand, int32_t parts,
+                                     fs_stream_t stream) {
+  fs_status st = fsb::check_common(a, false);
+  if (st != FS_OK) return st;
+  if (cand == nullptr || parts < 1) {
+    fsb::set_error("cand is NULL or parts < 1");
+    return FS_EINVAL;
+  }
+  if (a->out_ids == nullptr && a->topk_ids == nullptr) {
+    fsb::set_error("out_ids and topk_ids are both NULL");
+    return FS_EINVAL;
+  }
+  if (a->out_ids != nullptr && (st = fsb::check_top_p(a)) != FS_OK) return st;
+  return fsb::run_merge(a, cand, parts, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" fs_status fs_plan(int64_t batch, int64_t vocab, int64_t top_k, int32_t splits,
+                             fs_plan_info* out) {
+  if (out == nullptr || batch < 1 || vocab < 1 || top_k < 1) {
+    fsb::set_error("invalid fs_plan arguments");
+    return FS_EINVAL;
+  }
+  fsb::PlanOut p;
+  fs_status st = fsb::make_plan(batch, vocab, std::min(top_k, vocab), splits, &p);
+  if (st != FS_OK) return st;
+  out->splits = p.splits;
+  out->chunks = p.chunks;
+  out->threads = p.threads;
+  out->capacity = p.capacity;
+  out->maxima_per_thread = p.mpt;
+  out->lanes_per_max = p.mgroup;
+  out->smem_bytes = p.smem;
+  return FS_OK;
+}

@@ -1,0 +1,110 @@
+"""The C-ABI library loads and exports exactly what include/fused_sampling_b200.h declares, and
+its host-only entry points (plan, version, argument validation) behave. CPU only: no compute."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from llm_sampling_kernel_b200 import abi
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "fused_sampling_b200.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^FS_API\s+[\w\s\*]+?\b(fs_\w+)\(", text, flags=re.M)))
+
+
+def test_header_declares_the_documented_entry_points():
+    assert declared_functions() == sorted(abi.EXPORTED)
+
+
+@pytest.mark.parametrize("name", declared_functions())
+def test_library_exports_every_declared_symbol(name):
+    lib = abi.lib()
+    assert hasattr(lib, name), f"{name} missing from libfs_b200.so"
+    assert ctypes.cast(getattr(lib, name), ctypes.c_void_p).value
+
+
+def test_version_names_the_target():
+    assert "sm_100a" in abi.version()
+
+
+def test_struct_layout_matches_the_header(tmp_path):
+    # offsets of every field as the C compiler lays them out, against the ctypes mirror
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    structs = {"fs_sample_args": abi.FsSampleArgs, "fs_rng": abi.FsRng, "fs_kernel_attr": abi.FsKernelAttr,
+               "fs_plan_info": abi.FsPlanInfo}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void) {"]
+    for cname, cls in structs.items():
+        lines.append(f'printf("{cname} sizeof %zu\\n", sizeof({cname}));')
+        for fname, _ in cls._fields_:
+            lines.append(f'printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([cc, str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    for line in filter(None, out):
+        cname, field, value = line.split()
+        cls = structs[cname]
+        got = ctypes.sizeof(cls) if field == "sizeof" else getattr(cls, field).offset
+        assert got == int(value), f"{cname}.{field}: ctypes {got} vs C {value}"
+
+
+def test_plan_table():
+    p = abi.plan(1, 151936, 50)
+    assert (p.splits, p.chunks, p.threads) == (16, 5, 256)
+    assert p.splits * p.chunks * p.threads * 8 >= 151936
+    q = abi.plan(1024, 151936, 50)
+    assert q.splits * q.chunks * q.threads * 8 >= 151936
+    r = abi.plan(8, 151936, 1024)
+    assert r.capacity >= 4 * 1024
+    assert r.splits * r.threads * r.maxima_per_thread // r.lanes_per_max >= 4 * 1024
+    small = abi.plan(16, 4001, 100)
+    assert small.splits * small.chunks * small.threads * 8 >= 4001
+    for B in (1, 4, 16, 64, 1024):
+        for V in (2000, 4001, 32000, 128256, 151936, 256000):
+            for k in (1, 50, 256, 1024):
+                pl = abi.plan(B, V, k)
+                assert pl.splits * pl.chunks * pl.threads * 8 >= V
+                assert 1 <= pl.splits <= 16
+                assert pl.capacity >= min(k, V)
+
+
+def test_plan_rejects_a_vocabulary_beyond_the_register_budget():
+    with pytest.raises(abi.FsError) as e:
+        abi.plan(1, 1 << 21, 50)
+    assert e.value.status == abi.FS_EUNSUPPORTED
+
+
+def test_invalid_arguments_are_rejected_before_any_launch():
+    lib = abi.lib()
+    a = abi.FsSampleArgs()
+    a.dtype = 7
+    assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EINVAL
+    assert "float16 or bfloat16" in lib.fs_last_error().decode()
+    a.dtype = abi.FS_BF16
+    a.batch, a.vocab, a.row_stride, a.top_k, a.top_p = 2, 100, 100, 5, 1.5
+    a.logits = 0x1000
+    assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EINVAL
+    assert "top_p must be in (0, 1]" in lib.fs_last_error().decode()
+    a.top_p, a.top_k = 0.9, 0
+    assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EINVAL
+    assert "top_k must be >= 1" in lib.fs_last_error().decode()
+    a.top_k, a.row_stride = 5, 50
+    assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EINVAL
+    a.row_stride, a.stop_phase = 100, 9
+    assert lib.fs_probe_phase(ctypes.byref(a), None) == abi.FS_EINVAL
+    assert "phase must be in [1, 7]" in lib.fs_last_error().decode()
+    assert lib.fs_sample(None, None) == abi.FS_EINVAL
+    assert lib.fs_probe_noop(None, 4, None) == abi.FS_EINVAL
+    assert lib.fs_merge_sample(ctypes.byref(a), None, 2, None) == abi.FS_EINVAL

@@ -1,0 +1,457 @@
+"""CUDA parity tests: the fused kernel against the CPU oracle on the same seeded inputs.
+
+Bars (from the reference's Gate A, tests/test_fused_kernel.py, and the north-star contract):
+* the surviving top-k set and its order are bit-exact (lowest id wins ties);
+* token ids are identical for the same per-row uniform, except rows the oracle flags as within
+  1e-6 (relative) of a CDF step or with an exclusive prefix within 4 ulp of top_p;
+* the keep mask is exact outside those rows; renormed probabilities within 64 ulp and 2e-6 abs;
+* sampled frequencies pass a chi-square test against the exact FP64 categorical.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from llm_sampling_kernel_b200 import abi
+from llm_sampling_kernel_b200 import fused
+from oracle import sampler_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = [torch.float16, torch.bfloat16]
+RENORM_ULP = 64
+RENORM_ATOL = 2e-6
+CDF_REL_TOL = 1e-6
+
+
+def dev_randn(B, V, scale, dtype, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(B, V, generator=g) * scale).to(dtype).cuda()
+
+
+def oracle_topk(x, k):
+    return torch.from_numpy(orc.topk_order(orc.bits16(x.cpu()), min(k, x.shape[1])))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("top_k", [1, 20, 50, 100, 256, 1024])
+@pytest.mark.parametrize("vocab", [2000, 4001, 128256, 151936])
+def test_candidate_set_matches_the_oracle_exactly(vocab, top_k, dtype):
+    x = dev_randn(16, vocab, 4.0, dtype, seed=vocab + top_k)
+    got = fused.topk_fused(x, top_k).cpu()
+    assert torch.equal(got, oracle_topk(x, top_k))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("splits", [1, 2, 4, 8, 16])
+def test_candidate_set_is_independent_of_the_split(splits, dtype):
+    x = dev_randn(8, 151936, 2.0, dtype, seed=splits)
+    want = oracle_topk(x, 50)
+    if splits * 128 * 256 * 16 < 151936:
+        pytest.skip("row does not fit this many CTAs")
+    assert torch.equal(fused.topk_fused(x, 50, splits=splits).cpu(), want)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_all_equal_logits_resolve_to_the_lowest_token_ids(dtype):
+    x = torch.zeros(4, 4000, device="cuda", dtype=dtype)
+    assert torch.equal(fused.topk_fused(x, 50).cpu(), torch.arange(50).expand(4, 50))
+
+
+@pytest.mark.parametrize("vocab,splits", [(151936, 1 + 0), (151936, 8), (20000, 4), (5000, 1)])
+@pytest.mark.parametrize("top_k", [1, 50, 100, 1024])
+def test_ties_past_the_buffer_are_still_resolved_exactly(vocab, splits, top_k):
+    if splits * 128 * 256 * 16 < vocab:
+        splits = 0
+    x = torch.zeros(2, vocab, device="cuda", dtype=torch.bfloat16)
+    ids = fused.topk_fused(x, top_k, splits=splits).cpu()
+    assert torch.equal(ids, torch.arange(top_k).expand(2, top_k))
+
+
+@pytest.mark.parametrize("vocab", [20000, 151936])
+def test_dense_tie_rows_match_the_oracle(vocab):
+    x = dev_randn(8, vocab, 0.05, torch.bfloat16, seed=3)
+    for top_k in (20, 50, 100, 1024):
+        assert torch.equal(fused.topk_fused(x, top_k).cpu(), oracle_topk(x, top_k))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("sigma", [1.0, 4.0])
+def test_grid_rounded_ties_and_signed_zeros_match(dtype, sigma):
+    x = orc.grid_logits(16, 128256, sigma, dtype, seed=int(sigma)).cuda()
+    for top_k in (1, 50, 256, 1024):
+        assert torch.equal(fused.topk_fused(x, top_k).cpu(), oracle_topk(x, top_k))
+
+
+def test_signed_zeros_tie_on_the_k_boundary():
+    x = torch.full((2, 4096), -1.0)
+    x[0, ::3] = 0.0
+    x[0, 1::3] = -0.0
+    x[1, 100:200] = -0.0
+    x[1, 300:400] = 0.0
+    for dtype in DTYPES:
+        xd = x.to(dtype).cuda()
+        for k in (5, 150, 1500):
+            assert torch.equal(fused.topk_fused(xd, k).cpu(), oracle_topk(xd, k))
+
+
+def check_draw(x, top_k, top_p, uniforms=None, seed=0, offset=0):
+    """Kernel ids vs oracle ids for the same u; returns the number of exempt rows."""
+    B = x.shape[0]
+    if uniforms is None:
+        u = orc.splitmix_uniforms(seed, offset, B)
+        got = fused.sample_fused(x, top_k, top_p, seed=seed, offset=offset).cpu().numpy()
+    else:
+        u = uniforms.cpu().numpy()
+        got = fused.sample(x, top_k, top_p, uniforms=uniforms).token_ids.cpu().numpy()
+    d = orc.sample(x.cpu(), top_k, top_p, uniforms=u)
+    ok = (got == d.ids) | d.near_boundary
+    assert ok.all(), f"rows {np.nonzero(~ok)[0][:8]}: kernel {got[~ok][:8]} oracle {d.ids[~ok][:8]}"
+    return int(d.near_boundary.sum())
+
+
+def test_anchor_config_ids_match_the_oracle_for_the_same_uniform():
+    # C1: B=1, V=151936, BF16 N(0, 2^2) with 20 ids boosted by +8; k=50, p=0.9
+    x = orc.anchor_logits(B=1, V=151936, seed=1234).cuda()
+    exempt = 0
+    for off in range(64):
+        exempt += check_draw(x, 50, 0.9, seed=0x5EED, offset=off)
+    assert exempt <= 2
+
+
+def test_anchor_config_with_caller_uniforms_over_many_rows():
+    x = orc.anchor_logits(B=64, V=151936, seed=99).cuda()
+    u = torch.rand(64, generator=torch.Generator().manual_seed(1)).cuda()
+    assert check_draw(x, 50, 0.9, uniforms=u) <= 2
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("top_k", [1, 50, 256, 1024])
+@pytest.mark.parametrize("top_p", [0.5, 0.9, 1.0])
+def test_grid_config_ids_match_the_oracle(dtype, top_k, top_p):
+    # C2 cells (B=16, V=128256, sigma=4)
+    x = orc.grid_logits(16, 128256, 4.0, dtype, seed=top_k).cuda()
+    assert check_draw(x, top_k, top_p, seed=11, offset=top_k) <= 2
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("top_p", [0.5, 0.90, 0.95, 1.0])
+def test_sampled_token_is_inside_the_reference_nucleus(top_p, dtype):
+    x = dev_randn(8, 151936, 4.0, dtype)
+    st = orc.stages(x.cpu(), 50, top_p)
+    for off in range(32):
+        tok = fused.sample_fused(x, 50, top_p, offset=off).cpu()
+        hit = st.topk_ids == tok.unsqueeze(-1)
+        assert hit.any(dim=-1).all()
+        rank = hit.float().argmax(dim=-1)
+        assert (rank < st.cutoff).all()
+
+
+def test_top_k_one_is_the_argmax_and_ignores_the_rng():
+    x = dev_randn(8, 4000, 4.0, torch.bfloat16)
+    expected = x.float().argmax(dim=-1)
+    for off in range(8):
+        assert torch.equal(fused.sample_fused(x, 1, 0.9, offset=off), expected)
+
+
+def test_one_hot_logits_always_sample_the_spike():
+    x = torch.full((8, 4000), -30.0, device="cuda", dtype=torch.bfloat16)
+    x[:, 1234] = 30.0
+    for off in range(8):
+        assert (fused.sample_fused(x, 50, 0.9, offset=off) == 1234).all()
+
+
+def test_sampling_frequencies_match_the_renormalized_distribution():
+    probs = [0.40, 0.30, 0.15, 0.10, 0.05]
+    n = 20000
+    x = torch.tensor(probs).log().expand(n, 5).contiguous().to(torch.bfloat16).cuda()
+    tok = fused.sample_fused(x, 5, 1.0, offset=0).cpu()
+    freq = torch.bincount(tok, minlength=5).float() / n
+    assert (freq - torch.tensor(probs)).abs().max().item() < 4 * math.sqrt(0.4 * 0.6 / n)
+
+
+def test_chi_square_of_one_million_draws_against_the_fp64_categorical():
+    from scipy import stats
+
+    V, rows, rounds = 128, 50_000, 20
+    n = rows * rounds
+    row = (torch.randn(V, generator=torch.Generator().manual_seed(5)) * 2.0).to(torch.bfloat16)
+    x = row.expand(rows, V).contiguous().cuda()
+    ids, pr = orc.categorical_fp64(row, 100, 0.9)
+    tok = torch.cat([fused.sample_fused(x, 100, 0.9, seed=123, offset=o) for o in range(rounds)]).cpu().numpy()
+    counts = np.bincount(tok, minlength=V)
+    assert counts[np.setdiff1d(np.arange(V), ids)].sum() == 0, "sampled outside the FP64 nucleus"
+    obs = counts[ids]
+    exp = pr * n
+    chi2 = float(((obs - exp) ** 2 / exp).sum())
+    pval = stats.chi2.sf(chi2, df=len(ids) - 1)
+    assert pval > 1e-4, f"chi2={chi2:.1f} df={len(ids) - 1} p={pval:.2e}"
+
+
+def test_equal_logits_sample_close_to_uniform():
+    k, n = 8, 4096
+    x = torch.zeros(n, k, device="cuda", dtype=torch.bfloat16)
+    counts = torch.bincount(fused.sample_fused(x, k, 1.0, offset=0).cpu(), minlength=k).float()
+    assert (counts > 0).all()
+    assert (counts - n / k).abs().max().item() < 4 * math.sqrt(n * (1 / k) * (1 - 1 / k))
+
+
+def test_same_seed_and_offset_reproduce_and_different_offsets_advance():
+    x = dev_randn(64, 4000, 4.0, torch.bfloat16)
+    a = fused.sample_fused(x, 50, 0.9, seed=7, offset=3)
+    assert torch.equal(a, fused.sample_fused(x, 50, 0.9, seed=7, offset=3))
+    assert not torch.equal(a, fused.sample_fused(x, 50, 0.9, seed=7, offset=4))
+    assert not torch.equal(a, fused.sample_fused(x, 50, 0.9, seed=8, offset=3))
+
+
+def test_rejects_shapes_and_dtypes_outside_the_regime():
+    x = torch.randn(2, 4000, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="float16 or bfloat16"):
+        fused.sample_fused(x.float(), 50, 0.9)
+    with pytest.raises(RuntimeError, match=r"top_p must be in \(0, 1\]"):
+        fused.sample_fused(x, 50, 1.5)
+    with pytest.raises(RuntimeError, match="contiguous cuda"):
+        fused.sample_fused(x.t().contiguous().t(), 50, 0.9)
+    with pytest.raises(RuntimeError, match="top_k must be >= 1"):
+        fused.sample_fused(x, 0, 0.9)
+    # the reference capped top_k at 128; this build accepts any k up to V (clamped like the oracle)
+    assert fused.topk_fused(x, 200).shape == (2, 200)
+    assert fused.topk_fused(x, 10**6).shape == (2, 4000)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("batch", [1, 8])
+def test_the_last_ablation_phase_is_the_production_path(batch, dtype):
+    ops = fused.ops()
+    x = dev_randn(batch, 4000, 4.0, dtype)
+    for top_k in (20, 50):
+        got = ops.probe_phase(x, top_k, 0.9, ops.NUM_PHASES, 0)
+        want = ops.sample_fused(x, top_k, 0.9, 0, 0, 0)
+        assert torch.equal(got, want)
+
+
+def test_early_ablation_phases_stop_before_the_answer_exists():
+    ops = fused.ops()
+    x = dev_randn(4, 4000, 4.0, torch.bfloat16)
+    full = ops.probe_phase(x, 50, 0.9, ops.NUM_PHASES, 0)
+    for phase in range(1, ops.NUM_PHASES):
+        assert ops.probe_phase(x, 50, 0.9, phase, 0).shape == full.shape
+    assert not torch.equal(ops.probe_phase(x, 50, 0.9, ops.NUM_PHASES - 1, 0), full)
+
+
+def test_ablation_rejects_phases_outside_the_pipeline():
+    ops = fused.ops()
+    x = torch.zeros(2, 4000, device="cuda", dtype=torch.bfloat16)
+    for phase in (0, -1, ops.NUM_PHASES + 1):
+        with pytest.raises(RuntimeError):
+            ops.probe_phase(x, 50, 0.9, phase, 0)
+
+
+def stage_gap(x, top_k, top_p):
+    ref = orc.stages(x.cpu(), top_k, top_p)
+    _, keep, renormed = fused.stages_fused(x, top_k, top_p, 0, 0, 0)
+    return keep.cpu(), renormed.cpu(), ref
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("top_p", [0.9, 0.95, 1.0])
+@pytest.mark.parametrize("top_k", [1, 20, 50, 100, 256, 1024])
+def test_keep_mask_matches_the_oracle(top_k, top_p, dtype):
+    x = dev_randn(64, 151936, 4.0, dtype, seed=top_k)
+    keep, _, ref = stage_gap(x, top_k, top_p)
+    d = orc.draw(ref, np.zeros(64, dtype=np.float32), top_p)
+    rows = ~torch.from_numpy(d.near_boundary)
+    assert torch.equal(keep[rows], ref.keep[rows])
+    assert int((~rows).sum()) <= 2
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("top_k", [20, 50, 100, 1024])
+def test_renormed_matches_the_oracle_to_a_few_ulp(top_k, dtype):
+    x = dev_randn(64, 151936, 4.0, dtype, seed=7 * top_k)
+    keep, ren, ref = stage_gap(x, top_k, 0.9)
+    both = keep & ref.keep
+    ulp = (ren[both].view(torch.int32) - ref.renormed[both].view(torch.int32)).abs()
+    assert ulp.max().item() <= RENORM_ULP
+    assert torch.allclose(ren[both], ref.renormed[both], atol=RENORM_ATOL, rtol=0)
+    assert (ren[~keep] == 0).all()
+
+
+def test_renormed_sums_to_one_over_the_nucleus():
+    x = dev_randn(32, 151936, 4.0, torch.bfloat16)
+    for top_p in (0.9, 0.95, 1.0):
+        _, ren, _ = stage_gap(x, 50, top_p)
+        assert torch.allclose(ren.sum(-1), torch.ones(32), atol=1e-5)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("top_p,expected_kept", [(0.25, 2), (0.5, 4), (0.75, 6), (0.875, 7)])
+def test_cut_lands_exactly_on_the_boundary(top_p, expected_kept, dtype):
+    x = torch.full((4, 4000), -30.0, device="cuda", dtype=dtype)
+    x[:, :8] = 10.0
+    _, keep, _ = fused.stages_fused(x, 8, top_p, 0, 0, 0)
+    assert keep.sum(-1).tolist() == [expected_kept] * 4
+    assert torch.equal(keep.cpu(), orc.stages(x.cpu(), 8, top_p).keep)
+
+
+def _capture(x, top_k, top_p):
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            fused.sample_fused(x, top_k, top_p)
+    torch.cuda.current_stream().wait_stream(s)
+    with torch.cuda.graph(g):
+        out = fused.sample_fused(x, top_k, top_p)
+    return g, out
+
+
+def test_graph_replay_advances_the_rng_stream():
+    x = dev_randn(8, 4000, 2.0, torch.bfloat16)
+    g, out = _capture(x, 50, 0.95)
+    draws = []
+    for _ in range(16):
+        g.replay()
+        torch.cuda.synchronize()
+        draws.append(out.clone())
+    assert not all(torch.equal(draws[0], d) for d in draws)
+    assert len({tuple(d.tolist()) for d in draws}) > 8
+
+
+def test_graph_replay_still_samples_inside_the_nucleus():
+    x = dev_randn(8, 4000, 2.0, torch.bfloat16)
+    ref = orc.stages(x.cpu(), 50, 0.95)
+    g, out = _capture(x, 50, 0.95)
+    for _ in range(16):
+        g.replay()
+        torch.cuda.synchronize()
+        rank = (ref.topk_ids == out.cpu().unsqueeze(-1)).float().argmax(dim=-1)
+        assert (rank < ref.cutoff).all()
+
+
+def test_generator_mode_uses_torch_generator_state():
+    x = dev_randn(8, 4000, 2.0, torch.bfloat16)
+    torch.cuda.manual_seed(42)
+    a = fused.sample_fused(x, 50, 0.95)
+    torch.cuda.manual_seed(42)
+    b = fused.sample_fused(x, 50, 0.95)
+    assert torch.equal(a, b)
+    # the generator hands out seed 42 at offset 0 first, so the explicit form agrees
+    torch.cuda.manual_seed(42)
+    gen = torch.cuda.default_generators[torch.cuda.current_device()]
+    seed, off = gen.initial_seed(), gen.get_offset()
+    c = fused.sample_fused(x, 50, 0.95, seed=seed, offset=off)
+    assert torch.equal(a, c)
+
+
+def test_an_explicit_offset_is_still_reproducible():
+    ops = fused.ops()
+    x = dev_randn(8, 4000, 2.0, torch.bfloat16)
+    a = ops.sample_fused(x, 50, 0.9, 1234, 7, 0)
+    b = ops.sample_fused(x, 50, 0.9, 1234, 7, 0)
+    c = ops.sample_fused(x, 50, 0.9, 1234, 8, 0)
+    assert torch.equal(a, b)
+    assert not torch.equal(a, c)
+
+
+def test_row_status_for_invalid_inputs():
+    x = orc.adversarial_logits(4, B=8, V=151936).cuda()
+    res = fused.sample(x, 50, 0.9, seed=1, offset=1)
+    want = orc.row_status(x.cpu())
+    assert res.status.cpu().numpy().tolist() == want.tolist()
+    bad = torch.from_numpy(want != 0)
+    assert (res.token_ids.cpu()[bad] == -1).all()
+    good = ~bad
+    d = orc.sample(x.cpu()[good], 50, 0.9, uniforms=orc.splitmix_uniforms(1, 1, 8)[good.numpy()])
+    assert np.array_equal(res.token_ids.cpu()[good].numpy(), d.ids)
+    with pytest.raises(ValueError, match=r"\+inf"):
+        fused.sample(x, 50, 0.9, check_inputs=True)
+    y = x.clone()
+    y[0, 5] = float("nan")
+    with pytest.raises(ValueError, match="NaN"):
+        fused.sample(y, 50, 0.9, check_inputs=True)
+
+
+def test_neg_inf_is_legal_and_never_sampled():
+    x = torch.full((64, 500), float("-inf"))
+    x[:, :10] = torch.randn(64, 10, generator=torch.Generator().manual_seed(0))
+    xd = x.to(torch.bfloat16).cuda()
+    for off in range(20):
+        assert (fused.sample_fused(xd, 100, 1.0, offset=off) < 10).all()
+    assert torch.equal(fused.topk_fused(xd, 100).cpu(), oracle_topk(xd, 100))
+
+
+def test_per_row_k_and_p_match_per_row_scalar_calls():
+    x = dev_randn(12, 151936, 3.0, torch.bfloat16, seed=8)
+    ks = torch.tensor([1, 5, 50, 100, 256, 1024, 50, 7, 64, 300, 2, 999], dtype=torch.int32)
+    ps = torch.tensor([0.5, 0.9, 1.0, 0.95, 0.8, 0.99, 0.3, 1.0, 0.9, 0.9, 0.6, 0.7])
+    u = torch.rand(12, generator=torch.Generator().manual_seed(2))
+    res = fused.sample(x, ks.cuda(), ps.cuda(), uniforms=u.cuda(), return_stages=True)
+    for b in range(12):
+        one = fused.sample(x[b:b + 1], int(ks[b]), float(ps[b]), uniforms=u[b:b + 1].cuda(), return_stages=True)
+        assert res.token_ids[b].item() == one.token_ids[0].item()
+        k = int(ks[b])
+        assert torch.equal(res.topk_ids[b, :k], one.topk_ids[0, :k])
+        assert (res.topk_ids[b, k:] == -1).all()
+
+
+def test_vocab_sharded_candidates_merge_to_the_unsharded_result():
+    # tensor-parallel emulation on one GPU: w shards of the row, local top-k with global ids,
+    # all-gather (concatenate), merge + sample; identical to the unsharded call
+    x = dev_randn(32, 256000, 2.5, torch.bfloat16, seed=4)
+    u = torch.rand(32, generator=torch.Generator().manual_seed(3)).cuda()
+    want = fused.sample(x, 64, 0.9, uniforms=u, return_stages=True)
+    ops = fused.ops()
+    for world in (2, 4, 8):
+        vs = 256000 // world
+        parts = [ops.shard_candidates(x[:, r * vs:(r + 1) * vs], 64, r * vs) for r in range(world)]
+        cand = torch.stack(parts)
+        ids, status = ops.merge_sample(cand, True, 64, 0.9, uniforms=u)
+        assert torch.equal(ids, want.token_ids)
+        assert (status == 0).all()
+        abi_ids, _ = abi.merge_sample(cand, True, 64, 0.9, uniforms=u)
+        assert torch.equal(abi_ids, want.token_ids)
+
+
+def test_c_abi_path_equals_the_torch_operator_path():
+    x = dev_randn(16, 151936, 2.0, torch.bfloat16, seed=9)
+    for k, p in ((50, 0.9), (1, 1.0), (1024, 0.99)):
+        a = abi.sample(x, k, p, seed=5, offset=6)
+        b = fused.sample_fused(x, k, p, seed=5, offset=6)
+        assert torch.equal(a, b)
+        assert torch.equal(abi.topk(x, k), fused.topk_fused(x, k))
+
+
+def test_strided_and_unaligned_rows():
+    base = dev_randn(8, 151936 + 24, 3.0, torch.bfloat16, seed=10)
+    view = base[:, 8:8 + 151936]  # row stride 151960, 16-byte aligned start
+    assert torch.equal(fused.topk_fused(view, 50).cpu(), oracle_topk(view.contiguous(), 50))
+    odd = base[:, 3:3 + 151936]  # start not 16-byte aligned: scalar load path
+    assert torch.equal(fused.topk_fused(odd, 50).cpu(), oracle_topk(odd.contiguous(), 50))
+    u = torch.rand(8, generator=torch.Generator().manual_seed(4)).cuda()
+    a = fused.sample(odd, 50, 0.9, uniforms=u).token_ids
+    b = fused.sample(odd.contiguous(), 50, 0.9, uniforms=u).token_ids
+    assert torch.equal(a, b)
+
+
+def test_floor_probes():
+    ops = fused.ops()
+    x = dev_randn(8, 151936, 4.0, torch.bfloat16, seed=12)
+    assert (ops.probe_noop(x) == 0).all()
+    want = torch.from_numpy(orc.topk_order(orc.bits16(x.cpu()), 1)[:, 0])
+    assert torch.equal(ops.probe_scan_rowblock(x).cpu(), want)
+    for s in (1, 4, 16):
+        assert torch.equal(ops.probe_scan_split(x, s).cpu(), want)
+
+
+def test_kernel_attrs_report_every_kernel():
+    rows = fused.ops().kernel_attrs()
+    names = {r[0] for r in rows}
+    assert any(n.startswith("fs_cluster_kernel") for n in names)
+    assert "fs_scan_split_kernel" in names
+    for r in rows:
+        assert r[3] > 0, r  # registers
+        assert r[4] == 0, f"{r[0]} spills to local memory"
