@@ -385,7 +385,7 @@ def run_tp(ops, world, rank, device, args):
 
     def step(i):
         cand = ops.shard_candidates(shard, k, rank * vs, 0)
-        dist.all_gather_into_tensor(gathered, cand)
+        dist.all_gather_into_tensor(gathered.view(world * B, k + 1), cand)
         ops.merge_sample(gathered, True, k, p, None, None, None, 0x5EED, i, 0)
 
     steps = max(3, min(args.steps, 200))

@@ -721,14 +721,18 @@ constexpr int kMaxCap = 8192;
 // Plan of one call: cluster size, chunks per thread, survivor capacity, maxima granularity.
 fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, PlanOut* out) {
   const int64_t per_cta_chunk = static_cast<int64_t>(NT) * 8;  // elements per chunk per CTA
+  constexpr int kMaxChunks = 16;
+  const int64_t min_s = std::max<int64_t>(1, (V + per_cta_chunk * kMaxChunks - 1) / (per_cta_chunk * kMaxChunks));
   int S;
   if (splits > 0) {
-    S = std::min<int>(splits, kMaxSplits);
+    // a requested split that cannot hold the row in registers is raised to the smallest that can
+    S = static_cast<int>(std::min<int64_t>(kMaxSplits, std::max<int64_t>(splits, min_s)));
   } else {
     S = (B <= 32) ? 16 : 8;
     // small rows need fewer CTAs
-    const int64_t min_s = (V + per_cta_chunk - 1) / per_cta_chunk;
-    S = static_cast<int>(std::min<int64_t>(S, std::max<int64_t>(1, min_s)));
+    const int64_t one_chunk = (V + per_cta_chunk - 1) / per_cta_chunk;
+    S = static_cast<int>(std::min<int64_t>(S, std::max<int64_t>(1, one_chunk)));
+    S = static_cast<int>(std::min<int64_t>(kMaxSplits, std::max<int64_t>(S, min_s)));
   }
   // smallest chunk option that covers the row
   int C = 0;
@@ -768,22 +772,55 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, PlanOut* ou
   return FS_OK;
 }
 
+// Per-kernel attribute state: the dynamic shared memory limit already granted and whether
+// non-portable cluster sizes were enabled. Set once per kernel and size, not on every launch.
+struct KernelState {
+  const void* fn;
+  int smem_granted;
+  bool nonportable;
+};
+
 static fs_status prepare_kernel(KernelFn fn, int S, int smem) {
   static std::mutex mu;
+  static KernelState states[64];
+  static int n_states = 0;
+  const void* f = reinterpret_cast<const void*>(fn);
   std::lock_guard<std::mutex> lock(mu);
-  cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) {
-    set_error("cudaFuncSetAttribute(max dynamic smem %d): %s", smem, cudaGetErrorString(e));
-    return FS_ELAUNCH;
+  KernelState* ks = nullptr;
+  for (int i = 0; i < n_states; ++i)
+    if (states[i].fn == f) ks = &states[i];
+  if (ks == nullptr) {
+    if (n_states == 64) {
+      set_error("kernel state table full");
+      return FS_ELAUNCH;
+    }
+    ks = &states[n_states++];
+    *ks = KernelState{f, 0, false};
   }
-  if (S > 8) {
-    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
-                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  // the attribute is per device; re-grant when the current device has not seen this size
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static unsigned long long seen_devices[64] = {};
+  const int idx = static_cast<int>(ks - states);
+  const bool new_device = (seen_devices[idx] & (1ull << (dev & 63))) == 0;
+  if (new_device || smem > ks->smem_granted) {
+    const int grant = std::max(smem, ks->smem_granted);
+    cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, grant);
+    if (e != cudaSuccess) {
+      set_error("cudaFuncSetAttribute(max dynamic smem %d): %s", grant, cudaGetErrorString(e));
+      return FS_ELAUNCH;
+    }
+    ks->smem_granted = grant;
+    if (new_device) ks->nonportable = false;
+    seen_devices[idx] |= 1ull << (dev & 63);
+  }
+  if (S > 8 && !ks->nonportable) {
+    cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) {
       set_error("cudaFuncSetAttribute(non-portable cluster): %s", cudaGetErrorString(e));
       return FS_ELAUNCH;
     }
+    ks->nonportable = true;
   }
   return FS_OK;
 }

@@ -49,8 +49,7 @@ def test_candidate_set_matches_the_oracle_exactly(vocab, top_k, dtype):
 def test_candidate_set_is_independent_of_the_split(splits, dtype):
     x = dev_randn(8, 151936, 2.0, dtype, seed=splits)
     want = oracle_topk(x, 50)
-    if splits * 128 * 256 * 16 < 151936:
-        pytest.skip("row does not fit this many CTAs")
+    # a split too small to hold the row in registers is raised to the smallest that can
     assert torch.equal(fused.topk_fused(x, 50, splits=splits).cpu(), want)
 
 
@@ -60,11 +59,9 @@ def test_all_equal_logits_resolve_to_the_lowest_token_ids(dtype):
     assert torch.equal(fused.topk_fused(x, 50).cpu(), torch.arange(50).expand(4, 50))
 
 
-@pytest.mark.parametrize("vocab,splits", [(151936, 1 + 0), (151936, 8), (20000, 4), (5000, 1)])
+@pytest.mark.parametrize("vocab,splits", [(151936, 1), (151936, 8), (20000, 4), (5000, 1)])
 @pytest.mark.parametrize("top_k", [1, 50, 100, 1024])
 def test_ties_past_the_buffer_are_still_resolved_exactly(vocab, splits, top_k):
-    if splits * 128 * 256 * 16 < vocab:
-        splits = 0
     x = torch.zeros(2, vocab, device="cuda", dtype=torch.bfloat16)
     ids = fused.topk_fused(x, top_k, splits=splits).cpu()
     assert torch.equal(ids, torch.arange(top_k).expand(2, top_k))

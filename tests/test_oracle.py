@@ -152,3 +152,22 @@ def test_adversarial_generators_have_their_shapes():
     d = orc.adversarial_logits(4, B=4, V=1000)
     st = orc.row_status(d)
     assert st.tolist() == [0, 2, 3, 0]
+
+
+REF_RNG = np.load(Path(__file__).parent / "golden" / "ref_rng_vectors.npz")
+
+
+def test_splitmix_matches_the_reference_kernel_bit_for_bit():
+    # vectors from the reference's own rng_uniform run on a B200 (tests/golden/make_rng_golden.py)
+    got = np.array([orc.splitmix_uniform(int(s), int(o), int(r))
+                    for s, o, r in zip(REF_RNG["seed"], REF_RNG["offset"], REF_RNG["row"])], dtype=np.float32)
+    assert np.array_equal(got.view(np.uint32), REF_RNG["u_bits"])
+
+
+def test_order_keys_match_the_reference_except_the_negative_zero_fold():
+    ref = REF_RNG["mono_key"]
+    ours = orc.order_keys(np.arange(1 << 16, dtype=np.uint32).astype(np.uint16))
+    diff = np.nonzero(ref != ours)[0]
+    # the reference keys -0 (0x8000) as 0x7FFF, one below +0; the oracle folds it onto +0
+    assert diff.tolist() == [0x8000]
+    assert ref[0x8000] == 0x7FFF and ours[0x8000] == 0x8000
