@@ -1,24 +1,27 @@
 // Fused top-k / top-p sampler for B200 (sm_100a): one thread-block cluster per row.
 //
-// Design (one launch per call, logits read from HBM exactly once):
+// One launch per call; the logits are read from HBM exactly once.
 //   * The row is split across the S CTAs of a cluster (S <= 16). Each thread holds its part of
 //     the row in registers (C x 16-byte vectors) for the whole kernel.
 //   * Phase 1 - maxima: each thread reduces its values to a few sub-chunk maxima with the
 //     NaN-propagating packed max (two logits per instruction). The maxima also classify the
 //     row (NaN / +inf / all -inf).
-//   * Phase 2 - threshold: the maxima are counted into a 4096-bin histogram of the 16-bit order
-//     key held in the leader CTA's shared memory (remote atomics over distributed shared
-//     memory). The bin where the suffix count reaches k gives L, a value that at least k
-//     distinct elements reach, so every element of the top-k is >= L.
-//   * Phase 3/4 - filter: every element >= L (packed compare, two logits per instruction) is
-//     a survivor; survivors are written as packed (key, ~id) words into the leader's buffer in
-//     a deterministic order. Typically about 1.2k of them remain.
+//   * Phase 2 - histograms: every CTA counts its maxima into its own coarse (key >> 8) and fine
+//     (key >> 4) shared-memory histograms of the 16-bit order key. One cluster barrier.
+//   * Phase 3 - threshold: every CTA pulls the coarse histograms of all ranks over distributed
+//     shared memory, then the 16 fine bins of the boundary coarse bin, and computes the same L:
+//     the lower edge of the fine bin where the count of maxima from the top reaches k. At least
+//     k distinct elements reach L, so every element of the top-k is >= L.
+//   * Phase 4 - filter: every element >= L (packed compare, two logits per instruction) is a
+//     survivor, staged locally and appended to the leader CTA's buffer as a packed (key, ~id)
+//     word through one remote atomic per CTA. One cluster barrier. Typically ~1.2k remain.
 //   * If the survivors overflow the buffer (heavy ties: constant rows, few distinct values),
-//     an exact two-level 8-bit radix select over the register-resident data finds the k-th
-//     key T, and the lowest-id ties at T are chosen by an id-ordered prefix count.
-//   * Phase 5..7 in the leader: bitonic sort of the survivors (value desc, id asc), FP32
-//     softmax over the top k (expf, no fast-math), cumulative sum accumulated in double and
-//     rounded per element, exclusive-prefix top-p cut, inverse-CDF draw against u * Z_p.
+//     an exact two-level 8-bit radix select over the row finds the k-th key T, and the
+//     lowest-id ties at T are chosen by an id-ordered prefix count.
+//   * Phases 5..7 in the leader: bitonic sort of the survivors (value desc, id asc) in one
+//     warp's registers when they fit, FP32 softmax over the top k (expf, no fast-math),
+//     cumulative sum accumulated in double and rounded per element, exclusive-prefix top-p cut,
+//     inverse-CDF draw against u * Z_p. Non-leader CTAs leave right after the survivor barrier.
 //
 // Reference algorithm followed (sathviknookala/llm_sampling_kernel):
 //   selection semantics  benchmarks/reference.py:47-54 (stable descending sort, first k)
@@ -40,8 +43,8 @@ namespace cg = cooperative_groups;
 
 namespace fsb {
 
-constexpr int NT = 256;  // threads per CTA (the fallback histograms assume NT == 256)
-static_assert(NT == 256, "fallback radix passes map one thread per 8-bit bin");
+constexpr int NT = 256;  // threads per CTA (the 8-bit histograms map one thread per bin)
+static_assert(NT == 256, "the 8-bit histogram passes map one thread per bin");
 
 struct Params {
   const uint16_t* logits;
@@ -64,7 +67,7 @@ struct Params {
   float* renormed;
   int32_t* status;
   uint64_t* cand_out;  // shard candidates, [B, K + 1]
-  int32_t cap;         // survivor capacity, power of two
+  int32_t cap;         // survivor capacity, power of two, >= 256
   int32_t mpt;         // maxima per thread: 1, 2, 4 or 8
   int32_t mgroup;      // lanes per maximum (power of two <= 32), used when mpt == 1
   int32_t vec;         // 16-byte vector loads allowed
@@ -75,27 +78,33 @@ struct Params {
 constexpr int kModeSample = 0;
 constexpr int kModeTopk = 1;
 constexpr int kModeShard = 2;
+constexpr int kWarpPathMax = 256;  // survivors sorted in one warp's registers up to this count
 
-// ctl[] slots
-constexpr int kCtlFlags = 0;     // leader: OR of row flags pushed by every CTA
-constexpr int kCtlLocalFlags = 1;
-constexpr int kCtlLKey = 2;      // broadcast: threshold key
-constexpr int kCtlStatus = 3;    // broadcast: row status
-constexpr int kCtlBin = 4;       // leader scratch: boundary bin
-constexpr int kCtlHb = 5;        // fallback scratch
-constexpr int kCtlAbove = 6;
-constexpr int kCtlT = 7;
-constexpr int kCtlNgt = 8;
+// ctl[] slots (per CTA unless noted)
+constexpr int kCtlCount = 0;    // leader: survivors appended by every rank (remote atomics)
+constexpr int kCtlFlags = 1;    // this rank's row flags
+constexpr int kCtlGFlags = 2;   // row flags of every rank
+constexpr int kCtlLKey = 3;     // threshold key
+constexpr int kCtlStatus = 4;   // row status
+constexpr int kCtlLocal = 5;    // this rank's staged survivors
+constexpr int kCtlBase = 6;     // this rank's first slot in the leader's buffer
+constexpr int kCtlN = 7;        // survivors in the leader's buffer
+constexpr int kCtlHb = 8;       // fallback scratch
+constexpr int kCtlAbove = 9;
+constexpr int kCtlT = 10;
+constexpr int kCtlNgt = 11;
 
 constexpr uint32_t kFlagNaN = 1u, kFlagPosInf = 2u, kFlagAboveNegInf = 4u;
 
 struct alignas(16) Shared {
-  uint32_t hist[kHistBins];   // leader: histogram of maxima (key >> 4)
+  uint32_t fine[kHistBins];   // this rank's maxima histogram, key >> 4
+  uint32_t coarse[256];       // this rank's maxima histogram, key >> 8
+  uint32_t gcoarse[256];      // sum of every rank's coarse histogram
   uint32_t fh1[256];          // leader: fallback level-1 histogram (key >> 8)
-  uint32_t fh2[256];          // leader: fallback level-2 histogram (key & 0xFF at hb)
+  uint32_t fh2[256];          // leader: fallback level-2 histogram (key & 0xFF inside hb)
   uint32_t lh[256];           // local histogram before it is pushed
-  uint32_t cnt[kMaxSplits];   // per-rank survivor counts (written by every rank)
-  uint32_t cnt2[kMaxSplits];  // per-rank tie counts (fallback)
+  uint32_t cnt[kMaxSplits];   // fallback: per-rank counts above T
+  uint32_t cnt2[kMaxSplits];  // fallback: per-rank tie counts
   uint32_t ctl[16];
   int iscr[40];
   uint32_t uscr[40];
@@ -110,6 +119,37 @@ extern __shared__ __align__(16) unsigned char g_smem[];
 
 __device__ __forceinline__ uint32_t word_of(const uint4& v, int q) {
   return q == 0 ? v.x : q == 1 ? v.y : q == 2 ? v.z : v.w;
+}
+
+// Split cluster barrier: arrive (release) now, wait (acquire) later. Used so that ranks that have
+// nothing left to do can leave while the leader, whose shared memory they read last, finishes.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+// 32-bit distributed-shared-memory addressing: the address of `local` (a shared-memory
+// location of this CTA) in the CTA of cluster rank `rank`, and loads through it.
+__device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(local));
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ uint32_t ld_dsmem(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];\n" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// Sum of one 32-bit shared word over the first S ranks of the cluster.
+__device__ __forceinline__ uint32_t pull_sum(const uint32_t* local, int S) {
+  uint32_t acc = 0u;
+#pragma unroll 4
+  for (int r = 0; r < S; ++r) acc += ld_dsmem(dsmem_addr(local, static_cast<uint32_t>(r)));
+  return acc;
 }
 
 // Warp-aggregated shared-memory histogram add: lanes with the same bin elect one adder.
@@ -137,7 +177,7 @@ __device__ void write_invalid_row(const Params& p, int b, int st) {
     if (p.out != nullptr) p.out[b] = -1;
     if (p.status != nullptr) p.status[b] = st;
   }
-  for (int i = t; i < p.K; i += NT) {
+  for (int i = t; i < p.K; i += blockDim.x) {
     const size_t o = static_cast<size_t>(b) * p.K + i;
     if (p.topk_ids != nullptr) p.topk_ids[o] = -1;
     if (p.keep != nullptr) p.keep[o] = 0;
@@ -145,16 +185,47 @@ __device__ void write_invalid_row(const Params& p, int b, int st) {
   }
   if (p.cand_out != nullptr) {
     uint64_t* co = p.cand_out + static_cast<size_t>(b) * (p.K + 1);
-    for (int i = t; i < p.K; i += NT) co[i] = 0ull;
+    for (int i = t; i < p.K; i += blockDim.x) co[i] = 0ull;
     if (t == 0) co[p.K] = static_cast<uint64_t>(st);
   }
 }
 
-// FP32 softmax over the top kk sorted candidates, exclusive-prefix top-p cut, inverse-CDF draw.
-// cand: shared, sorted descending, >= kk valid entries. All NT threads call it.
+// Writes the top-K ids or the shard candidates of a sorted candidate list (shared memory).
+// Returns true when the mode ends here. Called by `nthreads` threads starting at thread 0.
+__device__ bool write_selection(const Params& p, int b, const uint64_t* cand, int kk, int nthreads) {
+  const int t = threadIdx.x;
+  if (p.mode == kModeTopk) {
+    for (int i = t; i < p.K; i += nthreads)
+      p.topk_ids[static_cast<size_t>(b) * p.K + i] = i < kk ? static_cast<int64_t>(packed_id(cand[i])) : -1;
+    if (t == 0 && p.status != nullptr) p.status[b] = FS_ROW_OK;
+    return true;
+  }
+  if (p.mode == kModeShard) {
+    uint64_t* co = p.cand_out + static_cast<size_t>(b) * (p.K + 1);
+    for (int i = t; i < p.K; i += nthreads) co[i] = i < kk ? cand[i] : 0ull;
+    if (t == 0) co[p.K] = FS_ROW_OK;
+    return true;
+  }
+  return false;
+}
+
+// Stage outputs (top-K ids, keep, renormed) from the sorted candidates and the per-rank
+// probabilities / cumulative sums held in shared memory.
+__device__ void write_stages(const Params& p, int b, const uint64_t* cand, const float* prob, int kk, int r,
+                             float zp, int nthreads) {
+  for (int i = threadIdx.x; i < p.K; i += nthreads) {
+    const size_t o = static_cast<size_t>(b) * p.K + i;
+    if (p.topk_ids != nullptr) p.topk_ids[o] = i < kk ? static_cast<int64_t>(packed_id(cand[i])) : -1;
+    if (p.keep != nullptr) p.keep[o] = (i <= r) ? 1 : 0;
+    if (p.renormed != nullptr) p.renormed[o] = (i <= r) ? prob[i] / zp : 0.0f;
+  }
+}
+
+// Block-wide tail for more than kWarpPathMax candidates: FP32 softmax over the top kk sorted
+// candidates, exclusive-prefix top-p cut, inverse-CDF draw. All NT threads call it.
 template <int DT>
-__device__ void sample_tail(const Params& p, int b, const uint64_t* cand, int kk, float pp,
-                            float* prob, float* cum, double* dscr, int* iscr) {
+__device__ void sample_tail_block(const Params& p, int b, const uint64_t* cand, int kk, float pp,
+                                  float* prob, float* cum, double* dscr, int* iscr) {
   const int t = threadIdx.x;
   const float m = key_to_float<DT>(packed_key(cand[0]));
   double part = 0.0;
@@ -167,7 +238,7 @@ __device__ void sample_tail(const Params& p, int b, const uint64_t* cand, int kk
   for (int i = t; i < kk; i += NT) prob[i] = prob[i] / z;
   __syncthreads();
 
-  // Inclusive cumulative sum accumulated in double and rounded once per element.
+  // inclusive cumulative sum accumulated in double and rounded once per element
   const int ipt = (kk + NT - 1) / NT;
   const int lo = min(kk, t * ipt), hi = min(kk, lo + ipt);
   double run = 0.0;
@@ -180,7 +251,7 @@ __device__ void sample_tail(const Params& p, int b, const uint64_t* cand, int kk
   }
   __syncthreads();
 
-  // r = (first i >= 1 with !((c_i - p_i) < p)) - 1, or kk - 1 when p >= 1.
+  // r = (first i >= 1 with !((c_i - p_i) < p)) - 1, or kk - 1 when p >= 1
   int fail = kk;
   if (pp < 1.0f) {
     for (int i = t; i < kk; i += NT)
@@ -198,17 +269,127 @@ __device__ void sample_tail(const Params& p, int b, const uint64_t* cand, int kk
   for (int i = t; i <= r; i += NT)
     if (cum[i] >= target) pick = min(pick, i);
   pick = block_min<NT>(pick, iscr);
-
   if (t == 0) {
     if (p.out != nullptr) p.out[b] = static_cast<int64_t>(packed_id(cand[pick]));
     if (p.status != nullptr) p.status[b] = FS_ROW_OK;
   }
-  for (int i = t; i < p.K; i += NT) {
-    const size_t o = static_cast<size_t>(b) * p.K + i;
-    if (p.topk_ids != nullptr) p.topk_ids[o] = i < kk ? static_cast<int64_t>(packed_id(cand[i])) : -1;
-    if (p.keep != nullptr) p.keep[o] = (i <= r) ? 1 : 0;
-    if (p.renormed != nullptr) p.renormed[o] = (i <= r) ? prob[i] / zp : 0.0f;
+  write_stages(p, b, cand, prob, kk, r, zp, NT);
+}
+
+// One-warp sort + tail for n <= 32 * R survivors (blocked layout: lane l owns ranks l*R..l*R+R-1).
+// Same arithmetic as the block tail; no __syncthreads, only shuffles.
+template <int DT, int R>
+__device__ void warp_finish(const Params& p, int b, uint64_t* surv, int n, int kk, float pp, float* prob) {
+  const int lane = threadIdx.x & 31;
+  uint64_t v[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int idx = lane * R + r;
+    v[r] = idx < n ? surv[idx] : 0ull;
   }
+  warp_sort_desc<R>(v);
+  if (p.stop == 5) {
+    if (lane == 0) p.out[b] = static_cast<int64_t>(packed_id(v[0]));
+    return;
+  }
+  const bool need_smem = p.mode != kModeSample || p.topk_ids != nullptr || p.keep != nullptr ||
+                         p.renormed != nullptr;
+  if (need_smem) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) surv[lane * R + r] = v[r];
+    __syncwarp();
+    if (write_selection(p, b, surv, kk, 32)) return;
+  }
+  const float m = key_to_float<DT>(packed_key(__shfl_sync(0xFFFFFFFFu, v[0], 0)));
+  float pr[R];
+  double part = 0.0;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int idx = lane * R + r;
+    const float w = idx < kk ? expf(key_to_float<DT>(packed_key(v[r])) - m) : 0.0f;
+    pr[r] = w;
+    part += static_cast<double>(w);
+  }
+  const float z = static_cast<float>(warp_sum(part));
+  double loc = 0.0, pre[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    pr[r] = pr[r] / z;
+    loc += static_cast<double>(pr[r]);
+    pre[r] = loc;
+  }
+  const double excl = warp_incl_scan(loc) - loc;
+  float cm[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) cm[r] = static_cast<float>(excl + pre[r]);
+  int fail = kk;
+  if (pp < 1.0f) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int idx = lane * R + r;
+      if (idx >= 1 && idx < kk && !((cm[r] - pr[r]) < pp)) fail = min(fail, idx);
+    }
+  }
+  fail = warp_min(fail);
+  const int rc = fail - 1;
+  if (p.stop == 6) {
+    if (lane == 0) p.out[b] = rc + 1;
+    return;
+  }
+  float csel = 0.0f;
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+    if (lane * R + r == rc) csel = cm[r];
+  const float zp = __shfl_sync(0xFFFFFFFFu, csel, rc / R);
+  const float target = row_uniform(p, b) * zp;
+  int pick = rc;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int idx = lane * R + r;
+    if (idx <= rc && cm[r] >= target) pick = min(pick, idx);
+  }
+  pick = warp_min(pick);
+  uint64_t vsel = 0ull;
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+    if (lane * R + r == pick) vsel = v[r];
+  const uint64_t win = __shfl_sync(0xFFFFFFFFu, vsel, pick / R);
+  if (lane == 0) {
+    if (p.out != nullptr) p.out[b] = static_cast<int64_t>(packed_id(win));
+    if (p.status != nullptr) p.status[b] = FS_ROW_OK;
+  }
+  if (need_smem) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) prob[lane * R + r] = pr[r];
+    __syncwarp();
+    write_stages(p, b, surv, prob, kk, rc, zp, 32);
+  }
+}
+
+// Sort + selection outputs + tail over n survivors in shared memory (leader CTA, all threads).
+template <int DT>
+__device__ void finish_row(const Params& p, int b, uint64_t* surv, int n, int kk, float pp, float* prob,
+                           float* cum, Shared& sh) {
+  const int t = threadIdx.x;
+  if (n <= kWarpPathMax) {
+    if (t >= 32) return;
+    if (n <= 32) warp_finish<DT, 1>(p, b, surv, n, kk, pp, prob);
+    else if (n <= 64) warp_finish<DT, 2>(p, b, surv, n, kk, pp, prob);
+    else if (n <= 128) warp_finish<DT, 4>(p, b, surv, n, kk, pp, prob);
+    else warp_finish<DT, 8>(p, b, surv, n, kk, pp, prob);
+    return;
+  }
+  int P = 32;
+  while (P < n) P <<= 1;
+  for (int i = n + t; i < P; i += NT) surv[i] = 0ull;
+  __syncthreads();
+  block_sort_desc<NT>(surv, P);
+  if (p.stop == 5) {
+    if (t == 0) p.out[b] = static_cast<int64_t>(packed_id(surv[0]));
+    return;
+  }
+  if (write_selection(p, b, surv, kk, NT)) return;
+  sample_tail_block<DT>(p, b, surv, kk, pp, prob, cum, sh.dscr, sh.iscr);
 }
 
 // Per-row k and p (a bad per-row value marks the row FS_ROW_BAD_PARAM).
@@ -389,6 +570,7 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
   return kk;
 }
 
+
 template <int DT, int C>
 __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
   cg::cluster_group cluster = cg::this_cluster();
@@ -416,17 +598,15 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
 #pragma unroll
   for (int c = 0; c < C; ++c) v[c] = load_chunk<DT>(row, (vbase + c * NT + t) * 8, V, p.vec);
 
-  // ---- shared-memory init, then the first cluster barrier ----
+  // ---- local shared-memory state (no other rank touches it before the first barrier) ----
+  for (int i = t; i < kHistBins; i += NT) sh.fine[i] = 0u;
+  sh.coarse[t] = 0u;
   if (leader) {
-    for (int i = t; i < kHistBins; i += NT) sh.hist[i] = 0u;
-    for (int i = t; i < 256; i += NT) {
-      sh.fh1[i] = 0u;
-      sh.fh2[i] = 0u;
-    }
+    sh.fh1[t] = 0u;
+    sh.fh2[t] = 0u;
   }
   if (t < 16) sh.ctl[t] = 0u;
-  if (t == 0) sh.ctl[kCtlBin] = 0xFFFFFFFFu;
-  cluster.sync();  // B1: every CTA of the cluster is running; leader state is zeroed
+  __syncthreads();
 
   // ---- phase 1: sub-chunk maxima ----
   uint32_t mx[4] = {Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2};
@@ -467,11 +647,10 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
   }
   if (p.stop == 1) {
     if (leader && t == 0) p.out[b] = static_cast<int64_t>(m16[0]);
-    return;  // no distributed shared memory access is pending
+    return;  // no distributed shared memory access has happened yet
   }
 
-  // ---- phase 2: maxima histogram in the leader + row flags ----
-  uint32_t* lhist = cluster.map_shared_rank(sh.hist, 0);
+  // ---- phase 2: this rank's maxima histograms and row flags ----
   uint32_t flags = 0u;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -483,77 +662,94 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
       if (bits == Fmt<DT>::kPosInf) flags |= kFlagPosInf;
       if (bits != Fmt<DT>::kNegInf) flags |= kFlagAboveNegInf;
     }
-    atomicAdd(lhist + (order_key(bits) >> 4), 1u);
+    const uint32_t key = order_key(bits);
+    atomicAdd(&sh.coarse[key >> 8], 1u);
+    atomicAdd(&sh.fine[key >> 4], 1u);
   }
   flags = __reduce_or_sync(0xFFFFFFFFu, flags);
-  if ((t & 31) == 0 && flags != 0u) atomicOr(&sh.ctl[kCtlLocalFlags], flags);
-  __syncthreads();
-  if (t == 0 && sh.ctl[kCtlLocalFlags] != 0u)
-    atomicOr(cluster.map_shared_rank(&sh.ctl[kCtlFlags], 0), sh.ctl[kCtlLocalFlags]);
-  cluster.sync();  // B2: leader histogram and flags are complete
+  if ((t & 31) == 0 && flags != 0u) atomicOr(&sh.ctl[kCtlFlags], flags);
+  cluster.sync();  // B2: every rank's histograms and flags are final (and every rank is running)
   if (p.stop == 2) {
     if (leader && t == 0) p.out[b] = static_cast<int64_t>(sh.ctl[kCtlFlags]);
-    return;
+    return;  // nothing was read remotely yet
   }
 
-  // ---- phase 3: threshold in the leader, broadcast to every rank ----
-  if (leader) {
-    const uint32_t f = sh.ctl[kCtlFlags];
-    int st = FS_ROW_OK;
-    if (bad) st = FS_ROW_BAD_PARAM;
-    else if (f & kFlagNaN) st = FS_ROW_NAN;
-    else if (f & kFlagPosInf) st = FS_ROW_POSINF;
-    else if (!(f & kFlagAboveNegInf)) st = FS_ROW_ALL_NEGINF;
-    uint32_t lkey = order_key(Fmt<DT>::kNegInf);
-    if (st == FS_ROW_OK) {
-      constexpr int BPT = kHistBins / NT;
-      const int hi = kHistBins - 1 - t * BPT;
-      uint32_t sum = 0u;
+  // ---- phase 3: the threshold, computed identically by every rank from pulled histograms ----
+  {
+    sh.gcoarse[t] = pull_sum(&sh.coarse[t], S);
+    if (t < S) {
+      const uint32_t f = ld_dsmem(dsmem_addr(&sh.ctl[kCtlFlags], static_cast<uint32_t>(t)));
+      if (f != 0u) atomicOr(&sh.ctl[kCtlGFlags], f);
+    }
+    __syncthreads();
+    if (t < 32) {
+      const int lane = t;
+      const uint32_t f = sh.ctl[kCtlGFlags];
+      int st = FS_ROW_OK;
+      if (bad) st = FS_ROW_BAD_PARAM;
+      else if (f & kFlagNaN) st = FS_ROW_NAN;
+      else if (f & kFlagPosInf) st = FS_ROW_POSINF;
+      else if (!(f & kFlagAboveNegInf)) st = FS_ROW_ALL_NEGINF;
+      uint32_t lkey = order_key(Fmt<DT>::kNegInf);
+      if (st == FS_ROW_OK) {
+        // coarse bins from the top: lane l owns bins 255-8l .. 248-8l
+        const uint32_t want = static_cast<uint32_t>(kk);
+        uint32_t cv[8], lsum = 0u;
 #pragma unroll
-      for (int j = 0; j < BPT; ++j) sum += sh.hist[hi - j];
-      uint32_t total;
-      const uint32_t inc = block_incl_scan<uint32_t, NT>(sum, sh.uscr, &total);
-      const uint32_t want = static_cast<uint32_t>(kk);
-      if (inc >= want && inc - sum < want) {
-        uint32_t acc = inc - sum;
-        for (int j = 0; j < BPT; ++j) {
-          acc += sh.hist[hi - j];
-          if (acc >= want) {
-            sh.ctl[kCtlBin] = static_cast<uint32_t>(hi - j);
-            break;
+        for (int j = 0; j < 8; ++j) {
+          cv[j] = sh.gcoarse[255 - 8 * lane - j];
+          lsum += cv[j];
+        }
+        const uint32_t inc = warp_incl_scan(lsum);
+        const unsigned ball = __ballot_sync(0xFFFFFFFFu, inc >= want);
+        if (ball != 0u) {
+          const int l0 = __ffs(ball) - 1;
+          uint32_t cbin = 0u, above = 0u;
+          if (lane == l0) {
+            uint32_t acc = inc - lsum;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              if (acc + cv[j] >= want) {
+                cbin = static_cast<uint32_t>(255 - 8 * lane - j);
+                above = acc;
+                break;
+              }
+              acc += cv[j];
+            }
           }
+          cbin = __shfl_sync(0xFFFFFFFFu, cbin, l0);
+          above = __shfl_sync(0xFFFFFFFFu, above, l0);
+          // the 16 fine bins of the boundary coarse bin, from the top
+          uint32_t fv = 0u;
+          if (lane < 16) fv = pull_sum(&sh.fine[cbin * 16u + 15u - static_cast<uint32_t>(lane)], S);
+          const uint32_t finc = warp_incl_scan(fv);
+          const unsigned fb = __ballot_sync(0xFFFFFFFFu, lane < 16 && above + finc >= want);
+          const uint32_t fbin = cbin * 16u + 15u - static_cast<uint32_t>(__ffs(fb) - 1);
+          lkey = max(fbin << 4, order_key(Fmt<DT>::kNegInf));
         }
       }
-      __syncthreads();
-      const uint32_t bin = sh.ctl[kCtlBin];
-      if (bin != 0xFFFFFFFFu) lkey = max(bin << 4, order_key(Fmt<DT>::kNegInf));
+      if (lane == 0) {
+        sh.ctl[kCtlLKey] = lkey;
+        sh.ctl[kCtlStatus] = static_cast<uint32_t>(st);
+      }
     }
-    for (int r = t; r < S; r += NT) {
-      uint32_t* rc = cluster.map_shared_rank(sh.ctl, r);
-      rc[kCtlLKey] = lkey;
-      rc[kCtlStatus] = static_cast<uint32_t>(st);
-    }
+    __syncthreads();
   }
-  cluster.sync();  // B3: threshold and row status visible in every rank
   const int st = static_cast<int>(sh.ctl[kCtlStatus]);
   const uint32_t lkey = sh.ctl[kCtlLKey];
-  if (st != FS_ROW_OK) {
-    if (leader) write_invalid_row(p, b, st);
-    return;
-  }
-  if (p.stop == 3) {
-    if (leader && t == 0) p.out[b] = static_cast<int64_t>(lkey);
+  if (st != FS_ROW_OK || p.stop == 3) {
+    cluster.sync();  // no rank leaves while another may still read its histograms
+    if (leader) {
+      if (st != FS_ROW_OK) write_invalid_row(p, b, st);
+      else if (t == 0) p.out[b] = static_cast<int64_t>(lkey);
+    }
     return;
   }
 
-  // ---- phase 4: survivors (every element >= L), staged locally, then placed in the leader ----
-  // Staging reuses this CTA's prob/cum region (cap packed words); the leader's surv[] is the
-  // destination of every rank. Order inside a rank's segment is arbitrary; the sort fixes it.
+  // ---- phase 4: survivors (every element >= L), staged locally, appended to the leader ----
   const uint32_t lbits = key_to_bits(lkey);
   const uint32_t l2 = lbits | (lbits << 16);
-  uint64_t* stage = reinterpret_cast<uint64_t*>(prob);
-  if (t == 0) sh.ctl[kCtlLocalFlags] = 0u;  // reused as the local survivor counter
-  __syncthreads();
+  uint64_t* stage = reinterpret_cast<uint64_t*>(prob);  // this rank's prob/cum region: cap words
 #pragma unroll
   for (int c = 0; c < C; ++c) {
 #pragma unroll
@@ -563,65 +759,42 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
       if (m != 0u) {
         const int e = (vbase + c * NT + t) * 8 + 2 * q;
         if ((m & 0xFFFFu) && e < V) {
-          const uint32_t slot = atomicAdd(&sh.ctl[kCtlLocalFlags], 1u);
+          const uint32_t slot = atomicAdd(&sh.ctl[kCtlLocal], 1u);
           if (slot < static_cast<uint32_t>(p.cap)) stage[slot] = pack(order_key(w & 0xFFFFu), p.id_base + e);
         }
         if ((m >> 16) && e + 1 < V) {
-          const uint32_t slot = atomicAdd(&sh.ctl[kCtlLocalFlags], 1u);
+          const uint32_t slot = atomicAdd(&sh.ctl[kCtlLocal], 1u);
           if (slot < static_cast<uint32_t>(p.cap)) stage[slot] = pack(order_key(w >> 16), p.id_base + e + 1);
         }
       }
     }
   }
   __syncthreads();
-  const uint32_t cta_total = sh.ctl[kCtlLocalFlags];
-  if (t < S) cluster.map_shared_rank(sh.cnt, t)[s] = cta_total;
-  cluster.sync();  // B4a: every rank knows every rank's survivor count
-  uint32_t n_surv = 0u, base = 0u;
-  for (int r = 0; r < S; ++r) {
-    const uint32_t cr = sh.cnt[r];
-    base += (r < s) ? cr : 0u;
-    n_surv += cr;
-  }
+  const uint32_t cta_total = sh.ctl[kCtlLocal];
   uint64_t* lsurv = cluster.map_shared_rank(surv, 0);
-  if (n_surv <= static_cast<uint32_t>(p.cap)) {
+  if (t == 0) sh.ctl[kCtlBase] = atomicAdd(cluster.map_shared_rank(&sh.ctl[kCtlCount], 0), cta_total);
+  __syncthreads();
+  const uint32_t base = sh.ctl[kCtlBase];
+  if (base + cta_total <= static_cast<uint32_t>(p.cap))
     for (uint32_t i = t; i < cta_total; i += NT) lsurv[base + i] = stage[i];
-  } else {
-    n_surv = static_cast<uint32_t>(
-        exact_select<DT, C>(sh, row, V, p.vec, p.id_base, vbase, kk, lsurv));
+  cluster.sync();  // B4: the leader's buffer and count are final
+  if (t == 0) sh.ctl[kCtlN] = ld_dsmem(dsmem_addr(&sh.ctl[kCtlCount], 0));
+  __syncthreads();
+  uint32_t n_surv = sh.ctl[kCtlN];
+  if (n_surv > static_cast<uint32_t>(p.cap)) {
+    n_surv = static_cast<uint32_t>(exact_select<DT, C>(sh, row, V, p.vec, p.id_base, vbase, kk, lsurv));
+    cluster.sync();  // F4: the leader holds exactly kk candidates
   }
-  cluster.sync();  // B4b: the leader holds every survivor
+  // Every rank has read the leader's count; ranks other than the leader are done. The leader
+  // waits for their arrival before it exits, so its shared memory outlives their last read.
+  cluster_arrive();
   if (!leader) return;
   if (p.stop == 4) {
     if (t == 0) p.out[b] = static_cast<int64_t>(n_surv);
-    return;
+  } else {
+    finish_row<DT>(p, b, surv, static_cast<int>(n_surv), kk, pp, prob, cum, sh);
   }
-
-  // ---- phase 5: sort the survivors (value desc, id asc) ----
-  const int n = static_cast<int>(n_surv);
-  int P = 32;
-  while (P < n) P <<= 1;
-  for (int i = n + t; i < P; i += NT) surv[i] = 0ull;
-  __syncthreads();
-  block_sort_desc<NT>(surv, P);
-  if (p.stop == 5) {
-    if (t == 0) p.out[b] = static_cast<int64_t>(packed_id(surv[0]));
-    return;
-  }
-  if (p.mode == kModeTopk) {
-    for (int i = t; i < p.K; i += NT)
-      p.topk_ids[static_cast<size_t>(b) * p.K + i] = i < kk ? static_cast<int64_t>(packed_id(surv[i])) : -1;
-    if (t == 0 && p.status != nullptr) p.status[b] = FS_ROW_OK;
-    return;
-  }
-  if (p.mode == kModeShard) {
-    uint64_t* co = p.cand_out + static_cast<size_t>(b) * (p.K + 1);
-    for (int i = t; i < p.K; i += NT) co[i] = i < kk ? surv[i] : 0ull;
-    if (t == 0) co[p.K] = FS_ROW_OK;
-    return;
-  }
-  // ---- phase 6/7: softmax, top-p cut, draw ----
-  sample_tail<DT>(p, b, surv, kk, pp, prob, cum, sh.dscr, sh.iscr);
+  cluster_wait();
 }
 
 // Merge of per-shard candidate blocks [parts, B, K + 1] for vocab-sharded tensor parallelism:
@@ -640,15 +813,9 @@ __global__ void __launch_bounds__(NT) fs_merge_kernel(const Params p, const uint
   bool bad;
   row_params(p, b, &kk, &pp, &bad);
   const int n = parts * p.K;
-  int P = 32;
-  while (P < n) P <<= 1;
-  for (int i = t; i < P; i += NT) {
-    uint64_t x = 0ull;
-    if (i < n) {
-      const int part = i / p.K, j = i - part * p.K;
-      x = cand[(static_cast<size_t>(part) * B + b) * (p.K + 1) + j];
-    }
-    surv[i] = x;
+  for (int i = t; i < n; i += NT) {
+    const int part = i / p.K, j = i - part * p.K;
+    surv[i] = cand[(static_cast<size_t>(part) * B + b) * (p.K + 1) + j];
   }
   // Combined row status: NaN or +inf in any shard; all -inf only if every shard is.
   if (t == 0) {
@@ -659,8 +826,8 @@ __global__ void __launch_bounds__(NT) fs_merge_kernel(const Params p, const uint
       inf |= w == FS_ROW_POSINF;
       neg += w == FS_ROW_ALL_NEGINF;
     }
-    int st = bad ? FS_ROW_BAD_PARAM
-                 : nan ? FS_ROW_NAN : inf ? FS_ROW_POSINF : (neg == parts ? FS_ROW_ALL_NEGINF : FS_ROW_OK);
+    const int st = bad ? FS_ROW_BAD_PARAM
+                       : nan ? FS_ROW_NAN : inf ? FS_ROW_POSINF : (neg == parts ? FS_ROW_ALL_NEGINF : FS_ROW_OK);
     sh.ctl[kCtlStatus] = static_cast<uint32_t>(st);
   }
   __syncthreads();
@@ -669,15 +836,9 @@ __global__ void __launch_bounds__(NT) fs_merge_kernel(const Params p, const uint
     write_invalid_row(p, b, st);
     return;
   }
-  block_sort_desc<NT>(surv, P);
-  // A shard that held fewer than K real values padded with 0; kk never exceeds the real count
-  // because the global row holds sum(V_shard) >= kk values.
-  if (p.mode == kModeTopk) {
-    for (int i = t; i < p.K; i += NT)
-      p.topk_ids[static_cast<size_t>(b) * p.K + i] = i < kk ? static_cast<int64_t>(packed_id(surv[i])) : -1;
-    return;
-  }
-  sample_tail<DT>(p, b, surv, kk, pp, prob, cum, sh.dscr, sh.iscr);
+  // A shard padded with 0 when it held fewer than K values; kk never exceeds the real count
+  // because every shard holds at least K values (checked on the host).
+  finish_row<DT>(p, b, surv, n, kk, pp, prob, cum, sh);
 }
 
 // ------------------------------------------------------------------------------------------
