@@ -17,6 +17,8 @@ struct PlanOut {
   int capacity;  // survivor buffer entries (power of two)
   int mpt;       // maxima per thread
   int mgroup;    // lanes per maximum
+  int mcta;      // maxima per CTA
+  int slot;      // survivor slots per rank in the leader's buffer
   int smem;      // dynamic shared memory bytes per CTA
 };
 

