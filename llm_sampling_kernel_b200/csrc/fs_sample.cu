@@ -721,13 +721,22 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
     else if (f & kFlagNaN) st = FS_ROW_NAN;
     else if (f & kFlagPosInf) st = FS_ROW_POSINF;
     else if (!(f & kFlagAboveNegInf)) st = FS_ROW_ALL_NEGINF;
-    uint32_t cb = 0xFFFFFFFFu, above = 0u;
-    if (st == FS_ROW_OK && !warp_boundary_256(sh.h1, static_cast<uint32_t>(kk), &cb, &above)) cb = 0xFFFFFFFFu;
+    uint32_t lkey = order_key(Fmt<DT>::kNegInf);
+    uint32_t cb = 0u, above = 0u;
+    if (st == FS_ROW_OK && warp_boundary_256(sh.h1, static_cast<uint32_t>(kk), &cb, &above)) {
+      // level 2 inside the boundary coarse bin, by this warp alone
+      for (int i = t; i < nmax; i += 32) {
+        const uint32_t k = sh.mkeys[i];
+        if ((k >> 8) == cb) atomicAdd(&sh.h2[k & 0xFFu], 1u);
+      }
+      __syncwarp();
+      uint32_t lb = 0u, dummy = 0u;
+      warp_boundary_256(sh.h2, static_cast<uint32_t>(kk) - above, &lb, &dummy);
+      lkey = max((cb << 8) | lb, lkey);
+    }
     if (t == 0) {
       sh.ctl[kCtlStatus] = static_cast<uint32_t>(st);
-      sh.ctl[kCtlCb] = cb;
-      sh.ctl[kCtlAboveC] = above;
-      sh.ctl[kCtlLKey] = order_key(Fmt<DT>::kNegInf);
+      sh.ctl[kCtlLKey] = lkey;
     }
   }
   __syncthreads();
@@ -736,20 +745,6 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
     // every remote access of this launch is complete (B2), so ranks may leave independently
     if (leader) write_invalid_row(p, b, st);
     return;
-  }
-  const uint32_t cb = sh.ctl[kCtlCb];
-  if (cb != 0xFFFFFFFFu) {
-    for (int i = t; i < nmax; i += NT) {
-      const uint32_t k = sh.mkeys[i];
-      if ((k >> 8) == cb) atomicAdd(&sh.h2[k & 0xFFu], 1u);
-    }
-    __syncthreads();
-    if (t < 32) {
-      uint32_t lb = 0u, dummy = 0u;
-      warp_boundary_256(sh.h2, static_cast<uint32_t>(kk) - sh.ctl[kCtlAboveC], &lb, &dummy);
-      if (t == 0) sh.ctl[kCtlLKey] = max((cb << 8) | lb, order_key(Fmt<DT>::kNegInf));
-    }
-    __syncthreads();
   }
   const uint32_t lkey = sh.ctl[kCtlLKey];
   if (p.stop == 3) {
@@ -760,6 +755,8 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
   // ---- phase 4: survivors (every element >= L) into this rank's slots of the leader ----
   const uint32_t lbits = key_to_bits(lkey);
   const uint32_t l2 = lbits | (lbits << 16);
+  const uint32_t M = static_cast<uint32_t>(p.slot);
+  const uint32_t slot0 = dsmem_addr(&surv[s * M], 0);
 #pragma unroll
   for (int c = 0; c < C; ++c) {
 #pragma unroll
@@ -770,29 +767,31 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
         const int e = (vbase + c * NT + t) * 8 + 2 * q;
         if ((m & 0xFFFFu) && e < V) {
           const uint32_t slot = atomicAdd(&sh.ctl[kCtlLocal], 1u);
-          if (slot < static_cast<uint32_t>(p.cap)) tmp[slot] = pack(order_key(w & 0xFFFFu), p.id_base + e);
+          if (slot < M) st_dsmem64(slot0 + 8u * slot, pack(order_key(w & 0xFFFFu), p.id_base + e));
         }
         if ((m >> 16) && e + 1 < V) {
           const uint32_t slot = atomicAdd(&sh.ctl[kCtlLocal], 1u);
-          if (slot < static_cast<uint32_t>(p.cap)) tmp[slot] = pack(order_key(w >> 16), p.id_base + e + 1);
+          if (slot < M) st_dsmem64(slot0 + 8u * slot, pack(order_key(w >> 16), p.id_base + e + 1));
         }
       }
     }
   }
   __syncthreads();
-  const uint32_t M = static_cast<uint32_t>(p.slot);
-  {
-    const uint32_t mine = sh.ctl[kCtlLocal];
-    const uint32_t wcount = min(mine, M);
-    for (uint32_t i = t; i < wcount; i += NT) st_dsmem64(dsmem_addr(&surv[s * M + i], 0), tmp[i]);
-    if (t == 0) st_dsmem(dsmem_addr(&sh.scnt[s], 0), mine);
-  }
+  if (t == 0) st_dsmem(dsmem_addr(&sh.scnt[s], 0), sh.ctl[kCtlLocal]);
   cluster.sync();  // B4: the leader's slots and counts are final
-  if (t < S) {
-    const uint32_t c = leader ? sh.scnt[t] : ld_dsmem(dsmem_addr(&sh.scnt[t], 0));
-    if (c > M) atomicOr(&sh.ctl[kCtlOverflow], 1u);
-    atomicAdd(&sh.ctl[kCtlN], c);
-    sh.cnt[t] = c;
+  if (t < 32) {
+    uint32_t c = 0u;
+    if (t < S) c = leader ? sh.scnt[t] : ld_dsmem(dsmem_addr(&sh.scnt[t], 0));
+    const uint32_t inc = warp_incl_scan(c);
+    const unsigned over = __ballot_sync(0xFFFFFFFFu, c > M);
+    if (t < S) {
+      sh.cnt[t] = c;
+      sh.cnt2[t] = inc - c;  // exclusive prefix: first compact index of rank t
+    }
+    if (t == 31) {
+      sh.ctl[kCtlN] = inc;
+      sh.ctl[kCtlOverflow] = over != 0u ? 1u : 0u;
+    }
   }
   __syncthreads();
   int n = static_cast<int>(sh.ctl[kCtlN]);
@@ -811,12 +810,11 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
   if (overflow) {
     for (int i = t; i < n; i += NT) tmp[i] = surv[i];
   } else {
-    // gather rank r's slots [r*M, r*M + cnt[r]) to [sum of earlier counts, ...)
-    int pre = 0;
-    for (int r = 0; r < S; ++r) {
-      const int cr = static_cast<int>(sh.cnt[r]);
-      for (int j = t; j < cr; j += NT) tmp[pre + j] = surv[r * M + j];
-      pre += cr;
+    // slot i = r * M + j of rank r goes to compact index prefix[r] + j
+    for (int i = t; i < S * static_cast<int>(M); i += NT) {
+      const int r = i / static_cast<int>(M);
+      const int j = i - r * static_cast<int>(M);
+      if (j < static_cast<int>(sh.cnt[r])) tmp[sh.cnt2[r] + j] = surv[i];
     }
   }
   __syncthreads();
