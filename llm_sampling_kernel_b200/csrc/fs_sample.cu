@@ -587,8 +587,11 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
 
 
 
+// Resident CTAs per SM the register budget must allow: the row slice lives in 4*C registers.
+constexpr int min_ctas_for(int C) { return C <= 10 ? 4 : (C <= 12 ? 3 : 2); }
+
 template <int DT, int C>
-__global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
+__global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const Params p) {
   cg::cluster_group cluster = cg::this_cluster();
   const int S = static_cast<int>(cluster.num_blocks());
   const int s = static_cast<int>(cluster.block_rank());
@@ -614,8 +617,15 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
   const uint16_t* row = p.logits + static_cast<int64_t>(b) * p.row_stride;
   const int vbase = s * C * NT;
   uint4 v[C];
+  if (p.vec && (vbase + C * NT) * 8 <= V) {
+    // whole slice in bounds and 16-byte aligned: one straight run of vector loads
+    const uint4* rv = reinterpret_cast<const uint4*>(row) + vbase + t;
 #pragma unroll
-  for (int c = 0; c < C; ++c) v[c] = load_chunk<DT>(row, (vbase + c * NT + t) * 8, V, p.vec);
+    for (int c = 0; c < C; ++c) v[c] = __ldg(rv + c * NT);
+  } else {
+#pragma unroll
+    for (int c = 0; c < C; ++c) v[c] = load_chunk<DT>(row, (vbase + c * NT + t) * 8, V, p.vec);
+  }
 
   sh.h1[t] = 0u;
   sh.h2[t] = 0u;
@@ -711,7 +721,10 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
 
   // ---- phase 3: the k-th largest maximum, by a local two-level radix select ----
   const int nmax = S * p.mcta;
-  for (int i = t; i < nmax; i += NT) atomicAdd(&sh.h1[sh.mkeys[i] >> 8], 1u);
+  for (int i0 = 0; i0 < nmax; i0 += NT) {  // uniform trip count: hist_add_warp needs full warps
+    const int i = i0 + t;
+    hist_add_warp(sh.h1, i < nmax ? sh.mkeys[i] >> 8 : 0u, i < nmax);
+  }
   __syncthreads();
   if (t < 32) {
     uint32_t f = t < S ? sh.flags[t] : 0u;
@@ -725,9 +738,10 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
     uint32_t cb = 0u, above = 0u;
     if (st == FS_ROW_OK && warp_boundary_256(sh.h1, static_cast<uint32_t>(kk), &cb, &above)) {
       // level 2 inside the boundary coarse bin, by this warp alone
-      for (int i = t; i < nmax; i += 32) {
-        const uint32_t k = sh.mkeys[i];
-        if ((k >> 8) == cb) atomicAdd(&sh.h2[k & 0xFFu], 1u);
+      for (int i0 = 0; i0 < nmax; i0 += 32) {
+        const int i = i0 + t;
+        const uint32_t k = i < nmax ? sh.mkeys[i] : 0u;
+        hist_add_warp(sh.h2, k & 0xFFu, i < nmax && (k >> 8) == cb);
       }
       __syncwarp();
       uint32_t lb = 0u, dummy = 0u;
@@ -757,22 +771,33 @@ __global__ void __launch_bounds__(NT) fs_cluster_kernel(const Params p) {
   const uint32_t l2 = lbits | (lbits << 16);
   const uint32_t M = static_cast<uint32_t>(p.slot);
   const uint32_t slot0 = dsmem_addr(&surv[s * M], 0);
+  // bit 8c+2q+h of the mask: element (chunk c, word q, half h) of this thread is >= L
+  constexpr int MW = (C * 8 + 31) / 32;
+  uint32_t mask[MW];
+#pragma unroll
+  for (int i = 0; i < MW; ++i) mask[i] = 0u;
 #pragma unroll
   for (int c = 0; c < C; ++c) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const uint32_t w = word_of(v[c], q);
-      const uint32_t m = pair_ge_mask<DT>(w, l2);
-      if (m != 0u) {
-        const int e = (vbase + c * NT + t) * 8 + 2 * q;
-        if ((m & 0xFFFFu) && e < V) {
-          const uint32_t slot = atomicAdd(&sh.ctl[kCtlLocal], 1u);
-          if (slot < M) st_dsmem64(slot0 + 8u * slot, pack(order_key(w & 0xFFFFu), p.id_base + e));
-        }
-        if ((m >> 16) && e + 1 < V) {
-          const uint32_t slot = atomicAdd(&sh.ctl[kCtlLocal], 1u);
-          if (slot < M) st_dsmem64(slot0 + 8u * slot, pack(order_key(w >> 16), p.id_base + e + 1));
-        }
+      const uint32_t m = pair_ge_mask<DT>(word_of(v[c], q), l2);
+      const uint32_t bits2 = (m & 1u) | ((m >> 15) & 2u);
+      const int bit = 8 * c + 2 * q;
+      mask[bit >> 5] |= bits2 << (bit & 31);
+    }
+  }
+  // rare: one rolled loop over the set bits; the value is re-read (an L1 hit)
+#pragma unroll
+  for (int i = 0; i < MW; ++i) {
+    uint32_t w = mask[i];
+    while (w != 0u) {
+      const int bit = 32 * i + __ffs(w) - 1;
+      w &= w - 1;
+      const int c = bit >> 3, j = bit & 7;
+      const int e = (vbase + c * NT + t) * 8 + j;
+      if (e < V) {
+        const uint32_t slot = atomicAdd(&sh.ctl[kCtlLocal], 1u);
+        if (slot < M) st_dsmem64(slot0 + 8u * slot, pack(order_key(row[e]), p.id_base + e));
       }
     }
   }
