@@ -90,8 +90,6 @@ constexpr int kCtlStatus = 1;   // row status
 constexpr int kCtlLocal = 2;    // this rank's staged survivors
 constexpr int kCtlN = 3;        // survivors of the row
 constexpr int kCtlOverflow = 4; // some rank overflowed its slots
-constexpr int kCtlCb = 5;       // threshold scratch: coarse bin and count above it
-constexpr int kCtlAboveC = 6;
 constexpr int kCtlHb = 8;       // fallback scratch
 constexpr int kCtlAbove = 9;
 constexpr int kCtlT = 10;
@@ -105,8 +103,6 @@ struct alignas(16) Shared {
   uint32_t scnt[kMaxSplits];  // leader: every rank's survivor count
   uint32_t cnt[kMaxSplits];   // fallback: per-rank counts above T
   uint32_t cnt2[kMaxSplits];  // fallback: per-rank tie counts
-  uint32_t h1[256];           // local radix histograms
-  uint32_t h2[256];
   uint32_t fh1[256];          // leader: fallback level-1 histogram (key >> 8)
   uint32_t fh2[256];          // leader: fallback level-2 histogram (key & 0xFF inside hb)
   uint32_t lh[256];           // fallback: local histogram before it is pushed
@@ -129,6 +125,10 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int q) {
 // Split cluster barrier: arrive (release) now, wait (acquire) later.
 __device__ __forceinline__ void cluster_arrive() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+}
+// Arrive without ordering earlier memory accesses (they are reads whose values were consumed).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait() {
   asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
@@ -162,34 +162,54 @@ __device__ __forceinline__ void hist_add_warp(uint32_t* h, uint32_t bin, bool va
   if (valid && (threadIdx.x & 31) == (__ffs(peers) - 1)) atomicAdd(&h[bin], __popc(peers));
 }
 
-// One warp finds, in a 256-bin histogram, the bin where the count from the top reaches `want`,
-// and the count strictly above that bin. Returns false when the total is below `want`.
-__device__ __forceinline__ bool warp_boundary_256(const uint32_t* h, uint32_t want, uint32_t* bin,
-                                                  uint32_t* above) {
-  const int lane = threadIdx.x & 31;
-  uint32_t lsum = 0u;
+// The kk-th largest of the n 16-bit keys keys[0..n) (0 when n < kk), decided bit by bit from the
+// top: a bit stays set when at least kk keys reach the candidate value. Warp 0 searches alone
+// (8 keys per lane, one warp reduction per bit) for n <= 256; above that every thread counts up
+// to 16 keys and the warps' counts meet in shared memory. The result is in every thread.
+__device__ uint32_t kth_largest_key(const uint32_t* keys, int n, int kk, uint32_t* scratch) {
+  const int t = threadIdx.x;
+  if (n <= 256) {
+    if (t < 32) {
+      uint32_t k8[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) lsum += h[255 - 8 * lane - j];
-  const uint32_t inc = warp_incl_scan(lsum);
-  const unsigned ball = __ballot_sync(0xFFFFFFFFu, inc >= want);
-  if (ball == 0u) return false;
-  const int l0 = __ffs(ball) - 1;
-  uint32_t b = 0u, a = 0u;
-  if (lane == l0) {
-    uint32_t acc = inc - lsum;
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t c = h[255 - 8 * lane - j];
-      if (acc + c >= want) {
-        b = static_cast<uint32_t>(255 - 8 * lane - j);
-        a = acc;
-        break;
+      for (int j = 0; j < 8; ++j) k8[j] = (32 * j + t < n) ? keys[32 * j + t] : 0u;
+      uint32_t L = 0u;
+#pragma unroll 1
+      for (int bit = 15; bit >= 0; --bit) {
+        const uint32_t cand = L | (1u << bit);
+        uint32_t c = 0u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) c += k8[j] >= cand;
+        if (__reduce_add_sync(0xFFFFFFFFu, c) >= static_cast<uint32_t>(kk)) L = cand;
       }
-      acc += c;
+      if (t == 0) scratch[0] = L;
     }
+    __syncthreads();
+    const uint32_t L = scratch[0];
+    __syncthreads();
+    return L;
   }
-  *bin = __shfl_sync(0xFFFFFFFFu, b, l0);
-  *above = __shfl_sync(0xFFFFFFFFu, a, l0);
-  return true;
+  uint32_t k16[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) k16[j] = (NT * j + t < n) ? keys[NT * j + t] : 0u;
+  uint32_t L = 0u;
+#pragma unroll 1
+  for (int bit = 15; bit >= 0; --bit) {
+    const uint32_t cand = L | (1u << bit);
+    uint32_t c = 0u;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) c += k16[j] >= cand;
+    c = __reduce_add_sync(0xFFFFFFFFu, c);
+    uint32_t* slot = scratch + (bit & 1) * 8;  // alternate halves: one barrier per bit
+    if ((t & 31) == 0) slot[t >> 5] = c;
+    __syncthreads();
+    uint32_t total = 0u;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) total += slot[w];
+    if (total >= static_cast<uint32_t>(kk)) L = cand;
+  }
+  __syncthreads();
+  return L;
 }
 
 __device__ __forceinline__ float row_uniform(const Params& p, int b) {
@@ -627,8 +647,6 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
     for (int c = 0; c < C; ++c) v[c] = load_chunk<DT>(row, (vbase + c * NT + t) * 8, V, p.vec);
   }
 
-  sh.h1[t] = 0u;
-  sh.h2[t] = 0u;
   if (leader) {
     sh.fh1[t] = 0u;
     sh.fh2[t] = 0u;
@@ -719,13 +737,8 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
     return;
   }
 
-  // ---- phase 3: the k-th largest maximum, by a local two-level radix select ----
+  // ---- phase 3: the k-th largest maximum, searched locally by every rank ----
   const int nmax = S * p.mcta;
-  for (int i0 = 0; i0 < nmax; i0 += NT) {  // uniform trip count: hist_add_warp needs full warps
-    const int i = i0 + t;
-    hist_add_warp(sh.h1, i < nmax ? sh.mkeys[i] >> 8 : 0u, i < nmax);
-  }
-  __syncthreads();
   if (t < 32) {
     uint32_t f = t < S ? sh.flags[t] : 0u;
     f = __reduce_or_sync(0xFFFFFFFFu, f);
@@ -734,24 +747,11 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
     else if (f & kFlagNaN) st = FS_ROW_NAN;
     else if (f & kFlagPosInf) st = FS_ROW_POSINF;
     else if (!(f & kFlagAboveNegInf)) st = FS_ROW_ALL_NEGINF;
-    uint32_t lkey = order_key(Fmt<DT>::kNegInf);
-    uint32_t cb = 0u, above = 0u;
-    if (st == FS_ROW_OK && warp_boundary_256(sh.h1, static_cast<uint32_t>(kk), &cb, &above)) {
-      // level 2 inside the boundary coarse bin, by this warp alone
-      for (int i0 = 0; i0 < nmax; i0 += 32) {
-        const int i = i0 + t;
-        const uint32_t k = i < nmax ? sh.mkeys[i] : 0u;
-        hist_add_warp(sh.h2, k & 0xFFu, i < nmax && (k >> 8) == cb);
-      }
-      __syncwarp();
-      uint32_t lb = 0u, dummy = 0u;
-      warp_boundary_256(sh.h2, static_cast<uint32_t>(kk) - above, &lb, &dummy);
-      lkey = max((cb << 8) | lb, lkey);
-    }
-    if (t == 0) {
-      sh.ctl[kCtlStatus] = static_cast<uint32_t>(st);
-      sh.ctl[kCtlLKey] = lkey;
-    }
+    if (t == 0) sh.ctl[kCtlStatus] = static_cast<uint32_t>(st);
+  }
+  {
+    const uint32_t kth = kth_largest_key(sh.mkeys, nmax, kk, sh.uscr);
+    if (t == 0) sh.ctl[kCtlLKey] = max(kth, order_key(Fmt<DT>::kNegInf));
   }
   __syncthreads();
   const int st = static_cast<int>(sh.ctl[kCtlStatus]);
@@ -828,7 +828,7 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
   }
   // Ranks other than the leader are done. The leader waits for their arrival before it exits,
   // so its shared memory outlives their last read of it.
-  cluster_arrive();
+  cluster_arrive_relaxed();
   if (!leader) return;
 
   // ---- phases 5-7 in the leader: compact, sort, tail ----
