@@ -47,7 +47,6 @@ namespace fsb {
 constexpr int NT = 256;  // threads per CTA (the 8-bit histograms map one thread per bin)
 static_assert(NT == 256, "the 8-bit histogram passes map one thread per bin");
 constexpr int kMaxMaxima = 4096;   // maxima exchanged per row, all ranks together
-constexpr int kRankSortMax = NT;   // survivors sorted by rank counting up to this count
 
 struct Params {
   const uint16_t* logits;
@@ -85,11 +84,13 @@ constexpr int kModeTopk = 1;
 constexpr int kModeShard = 2;
 
 // ctl[] slots (per CTA)
+constexpr int kCtlFlags = 14;   // this rank's row flags
 constexpr int kCtlLKey = 0;     // threshold key
 constexpr int kCtlStatus = 1;   // row status
 constexpr int kCtlLocal = 2;    // this rank's staged survivors
 constexpr int kCtlN = 3;        // survivors of the row
 constexpr int kCtlOverflow = 4; // some rank overflowed its slots
+constexpr int kCtlScr0 = 5;     // two words of block-search results
 constexpr int kCtlHb = 8;       // fallback scratch
 constexpr int kCtlAbove = 9;
 constexpr int kCtlT = 10;
@@ -103,6 +104,8 @@ struct alignas(16) Shared {
   uint32_t scnt[kMaxSplits];  // leader: every rank's survivor count
   uint32_t cnt[kMaxSplits];   // fallback: per-rank counts above T
   uint32_t cnt2[kMaxSplits];  // fallback: per-rank tie counts
+  uint32_t h1[256];           // threshold radix histograms
+  uint32_t h2[256];
   uint32_t fh1[256];          // leader: fallback level-1 histogram (key >> 8)
   uint32_t fh2[256];          // leader: fallback level-2 histogram (key & 0xFF inside hb)
   uint32_t lh[256];           // fallback: local histogram before it is pushed
@@ -162,54 +165,44 @@ __device__ __forceinline__ void hist_add_warp(uint32_t* h, uint32_t bin, bool va
   if (valid && (threadIdx.x & 31) == (__ffs(peers) - 1)) atomicAdd(&h[bin], __popc(peers));
 }
 
-// The kk-th largest of the n 16-bit keys keys[0..n) (0 when n < kk), decided bit by bit from the
-// top: a bit stays set when at least kk keys reach the candidate value. Warp 0 searches alone
-// (8 keys per lane, one warp reduction per bit) for n <= 256; above that every thread counts up
-// to 16 keys and the warps' counts meet in shared memory. The result is in every thread.
-__device__ uint32_t kth_largest_key(const uint32_t* keys, int n, int kk, uint32_t* scratch) {
+// Block-wide: the 256-bin histogram h (one bin per thread, bin 255 - t at thread t) has its
+// count from the top reach `want` in bin *bin, with *above counted strictly above it. Returns
+// false (and leaves the outputs alone) when the total is below `want`. Every thread calls it.
+__device__ __forceinline__ bool block_boundary_256(const uint32_t* h, uint32_t want, uint32_t* bin,
+                                                   uint32_t* above, uint32_t* scratch, uint32_t* result) {
   const int t = threadIdx.x;
-  if (n <= 256) {
-    if (t < 32) {
-      uint32_t k8[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) k8[j] = (32 * j + t < n) ? keys[32 * j + t] : 0u;
-      uint32_t L = 0u;
-#pragma unroll 1
-      for (int bit = 15; bit >= 0; --bit) {
-        const uint32_t cand = L | (1u << bit);
-        uint32_t c = 0u;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) c += k8[j] >= cand;
-        if (__reduce_add_sync(0xFFFFFFFFu, c) >= static_cast<uint32_t>(kk)) L = cand;
-      }
-      if (t == 0) scratch[0] = L;
-    }
-    __syncthreads();
-    const uint32_t L = scratch[0];
-    __syncthreads();
-    return L;
-  }
-  uint32_t k16[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) k16[j] = (NT * j + t < n) ? keys[NT * j + t] : 0u;
-  uint32_t L = 0u;
-#pragma unroll 1
-  for (int bit = 15; bit >= 0; --bit) {
-    const uint32_t cand = L | (1u << bit);
-    uint32_t c = 0u;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) c += k16[j] >= cand;
-    c = __reduce_add_sync(0xFFFFFFFFu, c);
-    uint32_t* slot = scratch + (bit & 1) * 8;  // alternate halves: one barrier per bit
-    if ((t & 31) == 0) slot[t >> 5] = c;
-    __syncthreads();
-    uint32_t total = 0u;
-#pragma unroll
-    for (int w = 0; w < NT / 32; ++w) total += slot[w];
-    if (total >= static_cast<uint32_t>(kk)) L = cand;
+  const uint32_t v = h[255 - t];
+  uint32_t total;
+  const uint32_t inc = block_incl_scan<uint32_t, NT>(v, scratch, &total);
+  if (inc >= want && inc - v < want) {
+    result[0] = static_cast<uint32_t>(255 - t);
+    result[1] = inc - v;
   }
   __syncthreads();
-  return L;
+  if (total < want) return false;
+  *bin = result[0];
+  *above = result[1];
+  return true;
+}
+
+// The kk-th largest of the n 16-bit keys keys[0..n) (0 when n < kk): two 8-bit radix levels with
+// shared-memory histograms h1 (high byte) and h2 (low byte inside the boundary high bin), each
+// boundary found by a block scan. h1 and h2 must be zero on entry. Every thread calls it.
+__device__ uint32_t kth_largest_key(const uint32_t* keys, int n, int kk, uint32_t* h1, uint32_t* h2,
+                                    uint32_t* scratch, uint32_t* result) {
+  const int t = threadIdx.x;
+  for (int i = t; i < n; i += NT) atomicAdd(&h1[keys[i] >> 8], 1u);
+  __syncthreads();
+  uint32_t hb = 0u, above = 0u;
+  if (!block_boundary_256(h1, static_cast<uint32_t>(kk), &hb, &above, scratch, result)) return 0u;
+  for (int i = t; i < n; i += NT) {
+    const uint32_t k = keys[i];
+    if ((k >> 8) == hb) atomicAdd(&h2[k & 0xFFu], 1u);
+  }
+  __syncthreads();
+  uint32_t lb = 0u, dummy = 0u;
+  block_boundary_256(h2, static_cast<uint32_t>(kk) - above, &lb, &dummy, scratch, result);
+  return (hb << 8) | lb;
 }
 
 __device__ __forceinline__ float row_uniform(const Params& p, int b) {
@@ -330,80 +323,76 @@ __device__ void sample_tail_block(const Params& p, int b, const uint64_t* cand, 
 }
 
 
-// One-warp tail over kk sorted candidates (rolled 32-wide chunks; same arithmetic as the block
-// tail): FP32 softmax, cumulative sum in double rounded per element, exclusive-prefix cut,
-// inverse-CDF draw.
+// Block tail for kk <= NT sorted candidates, one candidate per thread: FP32 softmax, cumulative
+// sum accumulated in double and rounded per element, exclusive-prefix cut, inverse-CDF draw.
+// Every collective is one warp-level step plus one cheap block barrier.
 template <int DT>
-__device__ void sample_tail_warp(const Params& p, int b, const uint64_t* cand, int kk, float pp, float* prob,
-                                 float* cum) {
-  const int lane = threadIdx.x & 31;
+__device__ void sample_tail_small(const Params& p, int b, const uint64_t* cand, int kk, float pp, float* prob,
+                                  float* cum, Shared& sh) {
+  const int t = threadIdx.x;
+  const int lane = t & 31, warp = t >> 5;
+  const bool live = t < kk;
   const float m = key_to_float<DT>(packed_key(cand[0]));
-  double part = 0.0;
-  for (int i = lane; i < kk; i += 32) {
-    const float w = expf(key_to_float<DT>(packed_key(cand[i])) - m);
-    prob[i] = w;
-    part += static_cast<double>(w);
+  const float w = live ? expf(key_to_float<DT>(packed_key(cand[t])) - m) : 0.0f;
+  const float z = static_cast<float>(block_sum<double, NT>(static_cast<double>(w), sh.dscr));
+  const float pr = w / z;
+  double total;
+  const float c = static_cast<float>(block_incl_scan<double, NT>(static_cast<double>(pr), sh.dscr, &total));
+  if (live) {
+    prob[t] = pr;
+    cum[t] = c;
   }
-  const float z = static_cast<float>(warp_sum(part));
-  double carry = 0.0;
+  // first failing index of the exclusive-prefix test (kk when none)
+  const bool fails = live && pp < 1.0f && t >= 1 && !((c - pr) < pp);
+  const unsigned fb = __ballot_sync(0xFFFFFFFFu, fails);
+  if (lane == 0) sh.iscr[warp] = fb ? 32 * warp + __ffs(fb) - 1 : kk;
+  __syncthreads();
   int fail = kk;
-  for (int base = 0; base < kk; base += 32) {
-    const int i = base + lane;
-    float pr = 0.0f;
-    if (i < kk) {
-      pr = prob[i] / z;
-      prob[i] = pr;
-    }
-    const double inc = warp_incl_scan(static_cast<double>(pr));
-    const float c = static_cast<float>(carry + inc);
-    if (i < kk) {
-      cum[i] = c;
-      if (pp < 1.0f && i >= 1 && !((c - pr) < pp)) fail = min(fail, i);
-    }
-    carry += __shfl_sync(0xFFFFFFFFu, inc, 31);
-  }
-  fail = warp_min(fail);
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) fail = min(fail, sh.iscr[i]);
   const int r = fail - 1;
-  __syncwarp();
   if (p.stop == 6) {
-    if (lane == 0) p.out[b] = r + 1;
+    if (t == 0) p.out[b] = r + 1;
     return;
   }
   const float zp = cum[r];
   const float target = row_uniform(p, b) * zp;
+  const unsigned hb = __ballot_sync(0xFFFFFFFFu, t <= r && c >= target);
+  __syncthreads();  // every thread has read iscr
+  if (lane == 0) sh.iscr[warp] = hb ? 32 * warp + __ffs(hb) - 1 : r;
+  __syncthreads();
   int pick = r;
-  for (int base = 0; base <= r; base += 32) {
-    const int i = base + lane;
-    const unsigned hit = __ballot_sync(0xFFFFFFFFu, i <= r && cum[i] >= target);
-    if (hit != 0u) {
-      pick = base + __ffs(hit) - 1;
-      break;
-    }
-  }
-  if (lane == 0) {
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) pick = min(pick, sh.iscr[i]);
+  if (t == 0) {
     if (p.out != nullptr) p.out[b] = static_cast<int64_t>(packed_id(cand[pick]));
     if (p.status != nullptr) p.status[b] = FS_ROW_OK;
   }
-  write_stages(p, b, cand, prob, kk, r, zp, 32);
+  write_stages(p, b, cand, prob, kk, r, zp, NT);
 }
 
 // Sorts n packed candidates (value desc, id asc) from `src` into the top kk of `dst`, then
 // writes the selection outputs or runs the tail. All NT threads of the CTA call it.
-// n <= NT: every thread ranks one candidate by counting the larger ones (packed values are
-// distinct). Larger n: bitonic sort in place in `src` (capacity >= next power of two of n).
-// `src` may alias prob/cum (it is dead once `dst` holds the sorted candidates); `dst` may not.
+// n <= NT: every candidate is ranked by counting the larger ones (packed values are distinct),
+// with NT / next_pow2(n) threads sharing each count. Larger n: bitonic sort in place in `src`
+// (capacity >= next power of two of n). `src` may alias prob/cum (it is dead once `dst` holds
+// the sorted candidates); `dst` may not.
 template <int DT>
 __device__ void finish_row(const Params& p, int b, uint64_t* src, int n, uint64_t* dst, int kk, float pp,
                            float* prob, float* cum, Shared& sh) {
   const int t = threadIdx.x;
-  const uint64_t* sorted = dst;
-  if (n <= kRankSortMax) {
-    if (t < n) {
-      const uint64_t mine = src[t];
-      int rank = 0;
-      for (int j = 0; j < n; ++j) rank += src[j] > mine;
-      if (rank < kk) dst[rank] = mine;
-    }
+  if (n <= NT) {
+    int P = 1;
+    while (P < n) P <<= 1;
+    const int g = NT / P;  // threads per candidate, a power of two <= NT
+    const int e = t / g, part = t - e * g;
+    const uint64_t mine = e < n ? src[e] : 0ull;
+    int rank = 0;
+#pragma unroll 4
+    for (int j = part; j < n; j += g) rank += src[j] > mine;
+    // a group wider than a warp means n <= 4: only its first n parts counted, all in one warp
+    for (int off = 1; off < min(g, 32); off <<= 1) rank += __shfl_xor_sync(0xFFFFFFFFu, rank, off);
+    if (part == 0 && e < n && rank < kk) dst[rank] = mine;
     __syncthreads();
   } else {
     int P = 32;
@@ -415,17 +404,16 @@ __device__ void finish_row(const Params& p, int b, uint64_t* src, int n, uint64_
     __syncthreads();
   }
   if (p.stop == 5) {
-    if (t == 0) p.out[b] = static_cast<int64_t>(packed_id(sorted[0]));
+    if (t == 0) p.out[b] = static_cast<int64_t>(packed_id(dst[0]));
     return;
   }
-  if (write_selection(p, b, sorted, kk, NT)) return;
-  if (kk <= kRankSortMax) {
-    if (t < 32) sample_tail_warp<DT>(p, b, sorted, kk, pp, prob, cum);
+  if (write_selection(p, b, dst, kk, NT)) return;
+  if (kk <= NT) {
+    sample_tail_small<DT>(p, b, dst, kk, pp, prob, cum, sh);
   } else {
-    sample_tail_block<DT>(p, b, sorted, kk, pp, prob, cum, sh.dscr, sh.iscr);
+    sample_tail_block<DT>(p, b, dst, kk, pp, prob, cum, sh.dscr, sh.iscr);
   }
 }
-
 
 // Per-row k and p (a bad per-row value marks the row FS_ROW_BAD_PARAM).
 __device__ __forceinline__ void row_params(const Params& p, int b, int* kk, float* pp, bool* bad) {
@@ -647,6 +635,8 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
     for (int c = 0; c < C; ++c) v[c] = load_chunk<DT>(row, (vbase + c * NT + t) * 8, V, p.vec);
   }
 
+  sh.h1[t] = 0u;
+  sh.h2[t] = 0u;
   if (leader) {
     sh.fh1[t] = 0u;
     sh.fh2[t] = 0u;
@@ -711,8 +701,7 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
     }
     sh.mkeys[mbase + i] = order_key(bits);
   }
-  flags = __reduce_or_sync(0xFFFFFFFFu, flags);
-  if ((t & 31) == 0) sh.iscr[t >> 5] = static_cast<int>(flags);
+  if (flags != 0u) atomicOr(&sh.ctl[kCtlFlags], flags);
   __syncthreads();
   cluster_wait();  // B1: every rank of the cluster is running
   {
@@ -724,12 +713,7 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
       const int r = ro < s ? ro : ro + 1;
       st_dsmem(dsmem_addr(&sh.mkeys[own + j], static_cast<uint32_t>(r)), sh.mkeys[own + j]);
     }
-    if (t < S) {
-      uint32_t f = 0u;
-#pragma unroll
-      for (int w = 0; w < NT / 32; ++w) f |= static_cast<uint32_t>(sh.iscr[w]);
-      st_dsmem(dsmem_addr(&sh.flags[s], static_cast<uint32_t>(t)), f);
-    }
+    if (t < S) st_dsmem(dsmem_addr(&sh.flags[s], static_cast<uint32_t>(t)), sh.ctl[kCtlFlags]);
   }
   cluster.sync();  // B2: every rank holds every rank's maxima and flags
   if (p.stop == 2) {
@@ -750,7 +734,7 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
     if (t == 0) sh.ctl[kCtlStatus] = static_cast<uint32_t>(st);
   }
   {
-    const uint32_t kth = kth_largest_key(sh.mkeys, nmax, kk, sh.uscr);
+    const uint32_t kth = kth_largest_key(sh.mkeys, nmax, kk, sh.h1, sh.h2, sh.uscr, &sh.ctl[kCtlScr0]);
     if (t == 0) sh.ctl[kCtlLKey] = max(kth, order_key(Fmt<DT>::kNegInf));
   }
   __syncthreads();
