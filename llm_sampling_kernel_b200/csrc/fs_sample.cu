@@ -165,44 +165,62 @@ __device__ __forceinline__ void hist_add_warp(uint32_t* h, uint32_t bin, bool va
   if (valid && (threadIdx.x & 31) == (__ffs(peers) - 1)) atomicAdd(&h[bin], __popc(peers));
 }
 
-// Block-wide: the 256-bin histogram h (one bin per thread, bin 255 - t at thread t) has its
-// count from the top reach `want` in bin *bin, with *above counted strictly above it. Returns
-// false (and leaves the outputs alone) when the total is below `want`. Every thread calls it.
-__device__ __forceinline__ bool block_boundary_256(const uint32_t* h, uint32_t want, uint32_t* bin,
-                                                   uint32_t* above, uint32_t* scratch, uint32_t* result) {
-  const int t = threadIdx.x;
-  const uint32_t v = h[255 - t];
-  uint32_t total;
-  const uint32_t inc = block_incl_scan<uint32_t, NT>(v, scratch, &total);
-  if (inc >= want && inc - v < want) {
-    result[0] = static_cast<uint32_t>(255 - t);
-    result[1] = inc - v;
+// One warp: in the 256-bin histogram h, the bin where the count from the top reaches `want`
+// and the count strictly above it (lane l owns bins 255-8l .. 248-8l). Returns false when the
+// total is below `want`. Results are valid in every lane.
+__device__ __forceinline__ bool warp_boundary_256(const uint32_t* h, uint32_t want, uint32_t* bin,
+                                                  uint32_t* above) {
+  const int lane = threadIdx.x & 31;
+  uint32_t pre[8], acc = 0u;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    acc += h[255 - 8 * lane - j];
+    pre[j] = acc;  // inclusive count of this lane's first j+1 bins (from the top)
   }
-  __syncthreads();
-  if (total < want) return false;
-  *bin = result[0];
-  *above = result[1];
+  const uint32_t inc = warp_incl_scan(acc);
+  const uint32_t before = inc - acc;
+  const unsigned ball = __ballot_sync(0xFFFFFFFFu, inc >= want);
+  if (ball == 0u) return false;
+  const int l0 = __ffs(ball) - 1;
+  unsigned hit = 0u;
+#pragma unroll
+  for (int j = 7; j >= 0; --j) hit = (hit << 1) | (before + pre[j] >= want ? 1u : 0u);
+  const int j0 = __ffs(hit) - 1;  // first of this lane's bins reaching `want` (valid in lane l0)
+  uint32_t ab = before;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (j < j0) ab = before + pre[j];
+  const uint32_t b = static_cast<uint32_t>(255 - 8 * lane - j0);
+  *bin = __shfl_sync(0xFFFFFFFFu, b, l0);
+  *above = __shfl_sync(0xFFFFFFFFu, ab, l0);
   return true;
 }
 
 // The kk-th largest of the n 16-bit keys keys[0..n) (0 when n < kk): two 8-bit radix levels with
-// shared-memory histograms h1 (high byte) and h2 (low byte inside the boundary high bin), each
-// boundary found by a block scan. h1 and h2 must be zero on entry. Every thread calls it.
+// shared-memory histograms h1 (high byte, filled by every thread) and h2 (low byte inside the
+// boundary high bin, filled by warp 0), each boundary found by one warp scan. h1 and h2 must be
+// zero on entry. Every thread calls it.
 __device__ uint32_t kth_largest_key(const uint32_t* keys, int n, int kk, uint32_t* h1, uint32_t* h2,
-                                    uint32_t* scratch, uint32_t* result) {
+                                    uint32_t* result) {
   const int t = threadIdx.x;
   for (int i = t; i < n; i += NT) atomicAdd(&h1[keys[i] >> 8], 1u);
   __syncthreads();
-  uint32_t hb = 0u, above = 0u;
-  if (!block_boundary_256(h1, static_cast<uint32_t>(kk), &hb, &above, scratch, result)) return 0u;
-  for (int i = t; i < n; i += NT) {
-    const uint32_t k = keys[i];
-    if ((k >> 8) == hb) atomicAdd(&h2[k & 0xFFu], 1u);
+  if (t < 32) {
+    uint32_t hb = 0u, above = 0u, L = 0u;
+    if (warp_boundary_256(h1, static_cast<uint32_t>(kk), &hb, &above)) {
+      for (int i = t; i < n; i += 32) {
+        const uint32_t k = keys[i];
+        if ((k >> 8) == hb) atomicAdd(&h2[k & 0xFFu], 1u);
+      }
+      __syncwarp();
+      uint32_t lb = 0u, dummy = 0u;
+      warp_boundary_256(h2, static_cast<uint32_t>(kk) - above, &lb, &dummy);
+      L = (hb << 8) | lb;
+    }
+    if (t == 0) result[0] = L;
   }
   __syncthreads();
-  uint32_t lb = 0u, dummy = 0u;
-  block_boundary_256(h2, static_cast<uint32_t>(kk) - above, &lb, &dummy, scratch, result);
-  return (hb << 8) | lb;
+  return result[0];
 }
 
 __device__ __forceinline__ float row_uniform(const Params& p, int b) {
@@ -323,76 +341,111 @@ __device__ void sample_tail_block(const Params& p, int b, const uint64_t* cand, 
 }
 
 
-// Block tail for kk <= NT sorted candidates, one candidate per thread: FP32 softmax, cumulative
-// sum accumulated in double and rounded per element, exclusive-prefix cut, inverse-CDF draw.
-// Every collective is one warp-level step plus one cheap block barrier.
-template <int DT>
-__device__ void sample_tail_small(const Params& p, int b, const uint64_t* cand, int kk, float pp, float* prob,
-                                  float* cum, Shared& sh) {
-  const int t = threadIdx.x;
-  const int lane = t & 31, warp = t >> 5;
-  const bool live = t < kk;
-  const float m = key_to_float<DT>(packed_key(cand[0]));
-  const float w = live ? expf(key_to_float<DT>(packed_key(cand[t])) - m) : 0.0f;
-  const float z = static_cast<float>(block_sum<double, NT>(static_cast<double>(w), sh.dscr));
-  const float pr = w / z;
-  double total;
-  const float c = static_cast<float>(block_incl_scan<double, NT>(static_cast<double>(pr), sh.dscr, &total));
-  if (live) {
-    prob[t] = pr;
-    cum[t] = c;
+// One-warp tail over kk <= 32 * R sorted candidates held in registers (blocked layout: lane l
+// owns ranks l*R .. l*R+R-1): FP32 softmax, cumulative sum accumulated in double and rounded per
+// element, exclusive-prefix cut, inverse-CDF draw against u * Z_p. One warp sum and one warp scan
+// are the only collectives; no block barrier.
+template <int DT, int R>
+__device__ void sample_tail_warp(const Params& p, int b, const uint64_t* cand, int kk, float pp, float u,
+                                 float* prob) {
+  const int lane = threadIdx.x & 31;
+  uint64_t v[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = lane * R + r;
+    v[r] = i < kk ? cand[i] : 0ull;
   }
-  // first failing index of the exclusive-prefix test (kk when none)
-  const bool fails = live && pp < 1.0f && t >= 1 && !((c - pr) < pp);
-  const unsigned fb = __ballot_sync(0xFFFFFFFFu, fails);
-  if (lane == 0) sh.iscr[warp] = fb ? 32 * warp + __ffs(fb) - 1 : kk;
-  __syncthreads();
+  const float m = key_to_float<DT>(packed_key(__shfl_sync(0xFFFFFFFFu, v[0], 0)));
+  float pr[R];
+  double part = 0.0;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    pr[r] = (lane * R + r < kk) ? expf(key_to_float<DT>(packed_key(v[r])) - m) : 0.0f;
+    part += static_cast<double>(pr[r]);
+  }
+  const float z = static_cast<float>(warp_sum(part));
+  double loc = 0.0, pre[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    pr[r] = pr[r] / z;
+    loc += static_cast<double>(pr[r]);
+    pre[r] = loc;
+  }
+  const double excl = warp_incl_scan(loc) - loc;
+  float cm[R];
   int fail = kk;
 #pragma unroll
-  for (int i = 0; i < NT / 32; ++i) fail = min(fail, sh.iscr[i]);
-  const int r = fail - 1;
+  for (int r = 0; r < R; ++r) {
+    cm[r] = static_cast<float>(excl + pre[r]);
+    const int i = lane * R + r;
+    if (pp < 1.0f && i >= 1 && i < kk && !((cm[r] - pr[r]) < pp)) fail = min(fail, i);
+  }
+  fail = __reduce_min_sync(0xFFFFFFFFu, static_cast<unsigned>(fail));
+  const int rc = fail - 1;
   if (p.stop == 6) {
-    if (t == 0) p.out[b] = r + 1;
+    if (lane == 0) p.out[b] = rc + 1;
     return;
   }
-  const float zp = cum[r];
-  const float target = row_uniform(p, b) * zp;
-  const unsigned hb = __ballot_sync(0xFFFFFFFFu, t <= r && c >= target);
-  __syncthreads();  // every thread has read iscr
-  if (lane == 0) sh.iscr[warp] = hb ? 32 * warp + __ffs(hb) - 1 : r;
-  __syncthreads();
-  int pick = r;
+  float csel = 0.0f;
 #pragma unroll
-  for (int i = 0; i < NT / 32; ++i) pick = min(pick, sh.iscr[i]);
-  if (t == 0) {
-    if (p.out != nullptr) p.out[b] = static_cast<int64_t>(packed_id(cand[pick]));
+  for (int r = 0; r < R; ++r)
+    if (lane * R + r == rc) csel = cm[r];
+  const float zp = __shfl_sync(0xFFFFFFFFu, csel, rc / R);
+  const float target = u * zp;
+  int pick = rc;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = lane * R + r;
+    if (i <= rc && cm[r] >= target) pick = min(pick, i);
+  }
+  pick = static_cast<int>(__reduce_min_sync(0xFFFFFFFFu, static_cast<unsigned>(pick)));
+  uint64_t vsel = 0ull;
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+    if (lane * R + r == pick) vsel = v[r];
+  const uint64_t win = __shfl_sync(0xFFFFFFFFu, vsel, pick / R);
+  if (lane == 0) {
+    if (p.out != nullptr) p.out[b] = static_cast<int64_t>(packed_id(win));
     if (p.status != nullptr) p.status[b] = FS_ROW_OK;
   }
-  write_stages(p, b, cand, prob, kk, r, zp, NT);
+  if (p.topk_ids != nullptr || p.keep != nullptr || p.renormed != nullptr) {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      if (lane * R + r < kk) prob[lane * R + r] = pr[r];
+    __syncwarp();
+    write_stages(p, b, cand, prob, kk, rc, zp, 32);
+  }
 }
 
 // Sorts n packed candidates (value desc, id asc) from `src` into the top kk of `dst`, then
-// writes the selection outputs or runs the tail. All NT threads of the CTA call it.
-// n <= NT: every candidate is ranked by counting the larger ones (packed values are distinct),
-// with NT / next_pow2(n) threads sharing each count. Larger n: bitonic sort in place in `src`
-// (capacity >= next power of two of n). `src` may alias prob/cum (it is dead once `dst` holds
-// the sorted candidates); `dst` may not.
+// writes the selection outputs or runs the tail. All NT threads of the CTA call it; `u` is the
+// row's uniform (valid in warp 0).
+// n <= NT: every candidate's rank is the count of larger ones (packed values are distinct),
+// counted by its own thread in unrolled chunks of 16 (src is zero-padded to a multiple of 16;
+// zeros are below every candidate). Larger n: bitonic sort in place in `src` (capacity >= next
+// power of two of n). `src` may alias prob/cum (it is dead once `dst` holds the sorted
+// candidates); `dst` may not.
 template <int DT>
 __device__ void finish_row(const Params& p, int b, uint64_t* src, int n, uint64_t* dst, int kk, float pp,
-                           float* prob, float* cum, Shared& sh) {
+                           float u, float* prob, float* cum, Shared& sh) {
   const int t = threadIdx.x;
   if (n <= NT) {
-    int P = 1;
-    while (P < n) P <<= 1;
-    const int g = NT / P;  // threads per candidate, a power of two <= NT
-    const int e = t / g, part = t - e * g;
-    const uint64_t mine = e < n ? src[e] : 0ull;
-    int rank = 0;
-#pragma unroll 4
-    for (int j = part; j < n; j += g) rank += src[j] > mine;
-    // a group wider than a warp means n <= 4: only its first n parts counted, all in one warp
-    for (int off = 1; off < min(g, 32); off <<= 1) rank += __shfl_xor_sync(0xFFFFFFFFu, rank, off);
-    if (part == 0 && e < n && rank < kk) dst[rank] = mine;
+    const int n16 = (n + 15) & ~15;
+    for (int i = n + t; i < n16; i += NT) src[i] = 0ull;
+    __syncthreads();
+    if (t < n) {
+      const uint64_t mine = src[t];
+      const ulonglong2* s2 = reinterpret_cast<const ulonglong2*>(src);
+      int rank = 0;
+      for (int base = 0; base < n16; base += 16) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const ulonglong2 w = s2[(base >> 1) + q];
+          rank += (w.x > mine) + (w.y > mine);
+        }
+      }
+      if (rank < kk) dst[rank] = mine;
+    }
     __syncthreads();
   } else {
     int P = 32;
@@ -408,8 +461,12 @@ __device__ void finish_row(const Params& p, int b, uint64_t* src, int n, uint64_
     return;
   }
   if (write_selection(p, b, dst, kk, NT)) return;
-  if (kk <= NT) {
-    sample_tail_small<DT>(p, b, dst, kk, pp, prob, cum, sh);
+  if (kk <= 256) {
+    if (t < 32) {
+      if (kk <= 32) sample_tail_warp<DT, 1>(p, b, dst, kk, pp, u, prob);
+      else if (kk <= 64) sample_tail_warp<DT, 2>(p, b, dst, kk, pp, u, prob);
+      else sample_tail_warp<DT, 8>(p, b, dst, kk, pp, u, prob);
+    }
   } else {
     sample_tail_block<DT>(p, b, dst, kk, pp, prob, cum, sh.dscr, sh.iscr);
   }
@@ -620,6 +677,8 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
   float pp;
   bool bad;
   row_params(p, b, &kk, &pp, &bad);
+  // the row's uniform, computed now so that it is off the leader's critical path later
+  const float u = (leader && t < 32) ? row_uniform(p, b) : 0.0f;
 
   // ---- issue every load of this thread's slice (one HBM read of the row) ----
   const uint16_t* row = p.logits + static_cast<int64_t>(b) * p.row_stride;
@@ -734,7 +793,7 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
     if (t == 0) sh.ctl[kCtlStatus] = static_cast<uint32_t>(st);
   }
   {
-    const uint32_t kth = kth_largest_key(sh.mkeys, nmax, kk, sh.h1, sh.h2, sh.uscr, &sh.ctl[kCtlScr0]);
+    const uint32_t kth = kth_largest_key(sh.mkeys, nmax, kk, sh.h1, sh.h2, &sh.ctl[kCtlScr0]);
     if (t == 0) sh.ctl[kCtlLKey] = max(kth, order_key(Fmt<DT>::kNegInf));
   }
   __syncthreads();
@@ -819,10 +878,11 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
   if (overflow) {
     for (int i = t; i < n; i += NT) tmp[i] = surv[i];
   } else {
-    // slot i = r * M + j of rank r goes to compact index prefix[r] + j
+    // slot i = r * M + j of rank r goes to compact index prefix[r] + j (M is a power of two)
+    const int mshift = __ffs(static_cast<int>(M)) - 1;
     for (int i = t; i < S * static_cast<int>(M); i += NT) {
-      const int r = i / static_cast<int>(M);
-      const int j = i - r * static_cast<int>(M);
+      const int r = i >> mshift;
+      const int j = i & (static_cast<int>(M) - 1);
       if (j < static_cast<int>(sh.cnt[r])) tmp[sh.cnt2[r] + j] = surv[i];
     }
   }
@@ -830,7 +890,7 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
   if (p.stop == 4) {
     if (t == 0) p.out[b] = static_cast<int64_t>(n);
   } else {
-    finish_row<DT>(p, b, tmp, n, surv, kk, pp, prob, cum, sh);
+    finish_row<DT>(p, b, tmp, n, surv, kk, pp, u, prob, cum, sh);
   }
   cluster_wait();
 }
@@ -851,6 +911,7 @@ __global__ void __launch_bounds__(NT) fs_merge_kernel(const Params p, const uint
   float pp;
   bool bad;
   row_params(p, b, &kk, &pp, &bad);
+  const float u = t < 32 ? row_uniform(p, b) : 0.0f;
   const int n = parts * p.K;
   for (int i = t; i < n; i += NT) {
     const int part = i / p.K, j = i - part * p.K;
@@ -877,7 +938,7 @@ __global__ void __launch_bounds__(NT) fs_merge_kernel(const Params p, const uint
   }
   // A shard padded with 0 when it held fewer than K values; kk never exceeds the real count
   // because every shard holds at least K values (checked on the host).
-  finish_row<DT>(p, b, tmp, n, surv, kk, pp, prob, cum, sh);
+  finish_row<DT>(p, b, tmp, n, surv, kk, pp, u, prob, cum, sh);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -927,12 +988,14 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, PlanOut* ou
   if (splits > 0) {
     // a requested split that cannot hold the row in registers is raised to the smallest that can
     S = static_cast<int>(std::min<int64_t>(kMaxSplits, std::max<int64_t>(splits, min_s)));
+    S = std::min(kMaxSplits, pow2_ceil(S));  // powers of two keep the slot arithmetic to shifts
   } else {
     S = (B <= 32) ? 16 : 8;
     // small rows need fewer CTAs
     const int64_t one_chunk = (V + per_cta_chunk - 1) / per_cta_chunk;
     S = static_cast<int>(std::min<int64_t>(S, std::max<int64_t>(1, one_chunk)));
     S = static_cast<int>(std::min<int64_t>(kMaxSplits, std::max<int64_t>(S, min_s)));
+    S = std::min(kMaxSplits, pow2_ceil(S));
   }
   // smallest chunk option that covers the row
   int C = 0;
