@@ -282,6 +282,24 @@ def run_ours(args):
         ms_hot = timed_steps(lambda i: ops.sample_fused(bufs[0], C1["k"], C1["p"], 0x5EED, i, 0),
                              args.steps, args.warmup, world)
         c1_hot_us = max_over_ranks(ms_hot * 1000.0 / args.steps, world)
+        # the same calls replayed from a CUDA graph (how a serving engine issues a decode step):
+        # 64 calls over 64 rotating buffers per graph; generator mode so replays advance the RNG
+        per_graph = 64
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for j in range(3):
+                ops.sample_fused(bufs[j], C1["k"], C1["p"], 0x5EED, -1, 0)
+        torch.cuda.current_stream().wait_stream(side)
+        with torch.cuda.graph(g):
+            for j in range(per_graph):
+                ops.sample_fused(bufs[j % nbuf], C1["k"], C1["p"], 0x5EED, -1, 0)
+        replays = max(3, args.steps // per_graph)
+        ms_graph = timed_steps(lambda i: g.replay(), replays, 3, world)
+        c1_graph_us = max_over_ranks(ms_graph * 1000.0 / (replays * per_graph), world)
+        launches += replays * per_graph
+        del g
 
         # ---- e2e through the public API with host buffers (pinned) ----
         host = [b.cpu().pin_memory() for b in bufs[:8]]
@@ -346,6 +364,7 @@ def run_ours(args):
             "parallelism": f"dp{world} (independent rows, no collective)",
         },
         "hot_l2_us": round(c1_hot_us, 3),
+        "graph_replay_us": round(c1_graph_us, 3),
         "e2e": {"value": round(e2e_us, 3), "unit": "µs/call", "h2d_bytes_per_step": per,
                 "d2h_bytes_per_step": C1["B"] * 8, "api": "llm_sampling_kernel_b200.fused.sample_fused"},
         "roofline": {
@@ -374,28 +393,30 @@ def run_ours(args):
 
 
 def run_tp(ops, world, rank, device, args):
-    """C4: vocab-sharded TP. Local shard top-k -> NCCL all-gather of packed candidates -> merge."""
+    """C4: vocab-sharded TP through llm_sampling_kernel_b200.sharded.VocabShardedSampler: local
+    shard top-k -> NCCL all-gather of packed candidates -> merge + sample on every rank."""
     import torch.distributed as dist
 
+    from llm_sampling_kernel_b200.sharded import VocabShardedSampler
+
     B, V, k, p = C4["B"], C4["V"], C4["k"], C4["p"]
-    vs = V // world
+    sampler = VocabShardedSampler(vocab=V, top_k=k, ops=ops)
+    lo, hi = sampler.cols
     full = tp_logits(B, V, device)
-    shard = full[:, rank * vs:(rank + 1) * vs].contiguous()
-    gathered = torch.empty(world, B, k + 1, dtype=torch.int64, device=device)
+    shard = full[:, lo:hi].contiguous()
+    del full
 
     def step(i):
-        cand = ops.shard_candidates(shard, k, rank * vs, 0)
-        dist.all_gather_into_tensor(gathered.view(world * B, k + 1), cand)
-        ops.merge_sample(gathered, True, k, p, None, None, None, 0x5EED, i, 0)
+        sampler.sample(shard, p, seed=0x5EED, offset=i)
 
     steps = max(3, min(args.steps, 200))
     ms = timed_steps(step, steps, max(3, args.warmup), world)
     us = max_over_ranks(ms * 1000.0 / steps, world)
-    ids, _ = ops.merge_sample(gathered, True, k, p, None, None, None, 0x5EED, 0, 0)
+    ids, _ = sampler.sample(shard, p, seed=0x5EED, offset=0)
     all_ids = [torch.empty_like(ids) for _ in range(world)]
     dist.all_gather(all_ids, ids)
     agree = all(torch.equal(all_ids[0], t) for t in all_ids)
-    return {"us_per_call": round(us, 3), "B": B, "V": V, "shard_vocab": vs, "top_k": k, "top_p": p,
+    return {"us_per_call": round(us, 3), "B": B, "V": V, "shard_vocab": hi - lo, "top_k": k, "top_p": p,
             "exchange_bytes_per_rank": B * (k + 1) * 8, "ranks_agree": agree, "launches": 2 * steps,
             "backend": "nccl all_gather_into_tensor"}
 

@@ -19,7 +19,6 @@ struct PlanOut {
   int mgroup;    // lanes per maximum
   int mcta;      // maxima per CTA
   int slot;      // survivor slots per rank in the leader's buffer
-  int local;     // 1: local-threshold kernel, 0: global-threshold kernel
   int smem;      // dynamic shared memory bytes per CTA
 };
 

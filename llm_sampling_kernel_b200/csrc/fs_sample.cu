@@ -91,7 +91,6 @@ constexpr int kCtlLocal = 2;    // this rank's staged survivors
 constexpr int kCtlN = 3;        // survivors of the row
 constexpr int kCtlOverflow = 4; // some rank overflowed its slots
 constexpr int kCtlScr0 = 5;     // two words of block-search results
-constexpr int kCtlLocal2 = 7;   // leader: candidates at or above the merged threshold
 constexpr int kCtlHb = 8;       // fallback scratch
 constexpr int kCtlAbove = 9;
 constexpr int kCtlT = 10;
@@ -211,31 +210,6 @@ __device__ uint32_t kth_largest_key(const uint32_t* keys, int n, int kk, uint32_
     if (warp_boundary_256(h1, static_cast<uint32_t>(kk), &hb, &above)) {
       for (int i = t; i < n; i += 32) {
         const uint32_t k = keys[i];
-        if ((k >> 8) == hb) atomicAdd(&h2[k & 0xFFu], 1u);
-      }
-      __syncwarp();
-      uint32_t lb = 0u, dummy = 0u;
-      warp_boundary_256(h2, static_cast<uint32_t>(kk) - above, &lb, &dummy);
-      L = (hb << 8) | lb;
-    }
-    if (t == 0) result[0] = L;
-  }
-  __syncthreads();
-  return result[0];
-}
-
-// The kk-th largest 16-bit key among n packed candidates c[0..n) (same method as
-// kth_largest_key). h1 and h2 must be zero on entry. Every thread calls it.
-__device__ uint32_t kth_largest_packed_key(const uint64_t* c, int n, int kk, uint32_t* h1, uint32_t* h2,
-                                           uint32_t* result) {
-  const int t = threadIdx.x;
-  for (int i = t; i < n; i += NT) atomicAdd(&h1[packed_key(c[i]) >> 8], 1u);
-  __syncthreads();
-  if (t < 32) {
-    uint32_t hb = 0u, above = 0u, L = 0u;
-    if (warp_boundary_256(h1, static_cast<uint32_t>(kk), &hb, &above)) {
-      for (int i = t; i < n; i += 32) {
-        const uint32_t k = packed_key(c[i]);
         if ((k >> 8) == hb) atomicAdd(&h2[k & 0xFFu], 1u);
       }
       __syncwarp();
@@ -678,106 +652,6 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
 
 
 
-// Exact top-kk of this CTA's slice alone, for the local-threshold kernel when the survivor
-// filter overflows its slots (heavy ties). Two 8-bit radix levels give the kk-th key T of the
-// slice; the elements above T and the lowest-id ties at T (ranked in id order: chunk, thread,
-// lane) are written as packed candidates to slot addresses slot0 + 8*i (distributed shared
-// memory). The slice is re-read chunk by chunk from global memory (L1/L2). h1 and h2 are
-// scratch. Returns the number written, min(kk, valid elements of the slice). Every thread of the
-// CTA calls it.
-template <int DT, int C>
-__device__ __noinline__ int local_exact_topk(Shared& sh, const uint16_t* __restrict__ row, int V, int vec,
-                                             uint32_t id_base, int vbase, int kk, uint32_t slot0) {
-  const int t = threadIdx.x;
-  const int valid = max(0, min(V - vbase * 8, C * NT * 8));
-  const int want = min(kk, valid);
-  if (want == 0) return 0;
-  sh.h1[t] = 0u;
-  sh.h2[t] = 0u;
-  if (t == 0) sh.ctl[kCtlLocal] = 0u;
-  __syncthreads();
-#pragma unroll 1
-  for (int c = 0; c < C; ++c) {
-    const int e0 = (vbase + c * NT + t) * 8;
-    const uint4 v = load_chunk<DT>(row, e0, V, vec);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t w = word_of(v, q);
-      if (e0 + 2 * q < V) atomicAdd(&sh.h1[order_key(w & 0xFFFFu) >> 8], 1u);
-      if (e0 + 2 * q + 1 < V) atomicAdd(&sh.h1[order_key(w >> 16) >> 8], 1u);
-    }
-  }
-  __syncthreads();
-  if (t < 32) {
-    uint32_t hb = 0u, above = 0u;
-    warp_boundary_256(sh.h1, static_cast<uint32_t>(want), &hb, &above);
-    if (t == 0) {
-      sh.ctl[kCtlHb] = hb;
-      sh.ctl[kCtlAbove] = above;
-    }
-  }
-  __syncthreads();
-  const uint32_t hb = sh.ctl[kCtlHb];
-  const uint32_t n_above = sh.ctl[kCtlAbove];
-#pragma unroll 1
-  for (int c = 0; c < C; ++c) {
-    const int e0 = (vbase + c * NT + t) * 8;
-    const uint4 v = load_chunk<DT>(row, e0, V, vec);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t w = word_of(v, q);
-      const uint32_t k0 = order_key(w & 0xFFFFu), k1 = order_key(w >> 16);
-      if (e0 + 2 * q < V && (k0 >> 8) == hb) atomicAdd(&sh.h2[k0 & 0xFFu], 1u);
-      if (e0 + 2 * q + 1 < V && (k1 >> 8) == hb) atomicAdd(&sh.h2[k1 & 0xFFu], 1u);
-    }
-  }
-  __syncthreads();
-  if (t < 32) {
-    uint32_t lb = 0u, above2 = 0u;
-    warp_boundary_256(sh.h2, static_cast<uint32_t>(want) - n_above, &lb, &above2);
-    if (t == 0) {
-      sh.ctl[kCtlT] = (hb << 8) | lb;
-      sh.ctl[kCtlNgt] = n_above + above2;
-    }
-  }
-  __syncthreads();
-  const uint32_t T = sh.ctl[kCtlT];
-  const uint32_t n_gt = sh.ctl[kCtlNgt];
-  const uint32_t need = static_cast<uint32_t>(want) - n_gt;
-  uint32_t chunk_base = 0u;
-#pragma unroll 1
-  for (int c = 0; c < C; ++c) {
-    const int e0 = (vbase + c * NT + t) * 8;
-    const uint4 v = load_chunk<DT>(row, e0, V, vec);
-    uint32_t mask = 0u;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t w = word_of(v, q);
-      const uint32_t k0 = order_key(w & 0xFFFFu), k1 = order_key(w >> 16);
-      if (e0 + 2 * q < V) {
-        if (k0 > T) st_dsmem64(slot0 + 8u * atomicAdd(&sh.ctl[kCtlLocal], 1u), pack(k0, id_base + e0 + 2 * q));
-        if (k0 == T) mask |= 1u << (2 * q);
-      }
-      if (e0 + 2 * q + 1 < V) {
-        if (k1 > T) st_dsmem64(slot0 + 8u * atomicAdd(&sh.ctl[kCtlLocal], 1u), pack(k1, id_base + e0 + 2 * q + 1));
-        if (k1 == T) mask |= 1u << (2 * q + 1);
-      }
-    }
-    const uint32_t cnt = __popc(mask);
-    uint32_t ctot;
-    const uint32_t excl = block_incl_scan<uint32_t, NT>(cnt, sh.uscr, &ctot) - cnt;
-    uint32_t rank = chunk_base + excl;
-    while (mask != 0u && rank < need) {
-      const int j = __ffs(mask) - 1;
-      mask &= mask - 1;
-      st_dsmem64(slot0 + 8u * (n_gt + rank), pack(T, id_base + e0 + j));
-      ++rank;
-    }
-    chunk_base += ctot;
-  }
-  return want;
-}
-
 // Resident CTAs per SM the register budget must allow: the row slice lives in 4*C registers.
 constexpr int min_ctas_for(int C) { return C <= 10 ? 4 : (C <= 12 ? 3 : 2); }
 
@@ -1021,234 +895,6 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
   cluster_wait();
 }
 
-// Local-threshold variant for small k (one cluster per row, no exchange before the filter).
-// Every rank keeps the top-kk of its own slice: L_s = the kk-th largest of its own maxima, the
-// survivors >= L_s (about 1.1 kk of them) go straight into the rank's slot range of the leader
-// (or, when more than half the range would be needed, the exact local top-kk does), then the
-// rank arrives at the cluster barrier and leaves. Only the leader waits; it merges the S slot
-// ranges - an exact radix select of the kk-th key over all of them, the candidates at or above
-// it ranked and sorted - and runs the tail. The union of the slices' top-kk holds the row's
-// top-kk, so the result is exact.
-template <int DT, int C>
-__global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_local_kernel(const Params p) {
-  cg::cluster_group cluster = cg::this_cluster();
-  const int S = static_cast<int>(cluster.num_blocks());
-  const int s = static_cast<int>(cluster.block_rank());
-  const int b = blockIdx.y;
-  const int t = threadIdx.x;
-  const bool leader = (s == 0);
-  const int V = p.vocab;
-  const uint32_t M = static_cast<uint32_t>(p.slot);  // slot range of one rank (power of two)
-
-  Shared& sh = *reinterpret_cast<Shared*>(g_smem);
-  uint64_t* surv = reinterpret_cast<uint64_t*>(g_smem + sizeof(Shared));  // S * M slots
-  float* prob = reinterpret_cast<float*>(surv + p.cap);
-  float* cum = prob + p.cap;
-  uint64_t* tmp = reinterpret_cast<uint64_t*>(prob);
-
-  cluster_arrive();  // B1 (split): waited for only before the first remote store
-
-  int kk;
-  float pp;
-  bool bad;
-  row_params(p, b, &kk, &pp, &bad);
-  const float u = (leader && t < 32) ? row_uniform(p, b) : 0.0f;
-
-  const uint16_t* row = p.logits + static_cast<int64_t>(b) * p.row_stride;
-  const int vbase = s * C * NT;
-  uint4 v[C];
-  if (p.vec && (vbase + C * NT) * 8 <= V) {
-    const uint4* rv = reinterpret_cast<const uint4*>(row) + vbase + t;
-#pragma unroll
-    for (int c = 0; c < C; ++c) v[c] = __ldg(rv + c * NT);
-  } else {
-#pragma unroll
-    for (int c = 0; c < C; ++c) v[c] = load_chunk<DT>(row, (vbase + c * NT + t) * 8, V, p.vec);
-  }
-  sh.h1[t] = 0u;
-  sh.h2[t] = 0u;
-  if (t < 16) sh.ctl[t] = 0u;
-
-  // ---- phase 1: maxima of this rank ----
-  uint32_t mx[4] = {Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2};
-#pragma unroll
-  for (int c = 0; c < C; ++c) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) mx[q] = pair_max_nan<DT>(mx[q], word_of(v[c], q));
-  }
-  uint32_t m16[8];
-  int nm;
-  if (p.mpt == 8) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      m16[2 * q] = mx[q] & 0xFFFFu;
-      m16[2 * q + 1] = mx[q] >> 16;
-    }
-    nm = 8;
-  } else if (p.mpt == 4) {
-    const uint32_t a = pair_max_nan<DT>(mx[0], mx[2]), c2 = pair_max_nan<DT>(mx[1], mx[3]);
-    m16[0] = a & 0xFFFFu;
-    m16[1] = a >> 16;
-    m16[2] = c2 & 0xFFFFu;
-    m16[3] = c2 >> 16;
-    nm = 4;
-  } else {
-    const uint32_t a = pair_max_nan<DT>(pair_max_nan<DT>(mx[0], mx[2]), pair_max_nan<DT>(mx[1], mx[3]));
-    if (p.mpt == 2) {
-      m16[0] = a & 0xFFFFu;
-      m16[1] = a >> 16;
-      nm = 2;
-    } else {
-      uint32_t m1 = half_max_nan<DT>(a & 0xFFFFu, a >> 16);
-      for (int off = 1; off < p.mgroup; off <<= 1)
-        m1 = half_max_nan<DT>(m1, __shfl_xor_sync(0xFFFFFFFFu, m1, off));
-      m16[0] = m1;
-      nm = ((t & (p.mgroup - 1)) == 0) ? 1 : 0;
-    }
-  }
-  uint32_t flags = 0u;
-  const int mbase = (t / p.mgroup) * p.mpt;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (i >= nm) break;
-    const uint32_t bits = m16[i];
-    if (Fmt<DT>::is_nan(bits)) {
-      flags |= kFlagNaN;
-    } else {
-      if (bits == Fmt<DT>::kPosInf) flags |= kFlagPosInf;
-      if (bits != Fmt<DT>::kNegInf) flags |= kFlagAboveNegInf;
-    }
-    sh.mkeys[mbase + i] = order_key(bits);
-  }
-  if (flags != 0u) atomicOr(&sh.ctl[kCtlFlags], flags);
-  __syncthreads();
-  if (p.stop == 1) {
-    cluster_wait();
-    if (leader && t == 0) p.out[b] = static_cast<int64_t>(m16[0]);
-    return;
-  }
-
-  // ---- phase 2/3: this rank's threshold L_s, the kk-th largest of its own maxima ----
-  const uint32_t kth = kth_largest_key(sh.mkeys, p.mcta, kk, sh.h1, sh.h2, &sh.ctl[kCtlScr0]);
-  const uint32_t lkey = max(kth, order_key(Fmt<DT>::kNegInf));
-
-  // ---- phase 4: survivors >= L_s into this rank's slots of the leader ----
-  const uint32_t lbits = key_to_bits(lkey);
-  const uint32_t l2 = lbits | (lbits << 16);
-  constexpr int MW = (C * 8 + 31) / 32;
-  uint32_t mask[MW];
-#pragma unroll
-  for (int i = 0; i < MW; ++i) mask[i] = 0u;
-  uint32_t mine = 0u;
-#pragma unroll
-  for (int c = 0; c < C; ++c) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t m = pair_ge_mask<DT>(word_of(v[c], q), l2);
-      const uint32_t bits2 = (m & 1u) | ((m >> 15) & 2u);
-      const int bit = 8 * c + 2 * q;
-      mask[bit >> 5] |= bits2 << (bit & 31);
-    }
-  }
-  // elements past the end of the row read as -inf and may pass an L_s of -inf: drop them
-  if (!(p.vec && (vbase + C * NT) * 8 <= V)) {
-#pragma unroll
-    for (int c = 0; c < C; ++c) {
-      const int e0 = (vbase + c * NT + t) * 8;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int bit = 8 * c + j;
-        if (e0 + j >= V) mask[bit >> 5] &= ~(1u << (bit & 31));
-      }
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < MW; ++i) mine += __popc(mask[i]);
-  const uint32_t total = block_sum<uint32_t, NT>(mine, sh.uscr);
-  cluster_wait();  // B1: the leader is running, its slots may be written
-  const uint32_t slot0 = dsmem_addr(&surv[s * M], 0);
-  uint32_t written;
-  if (total <= M / 2) {
-    written = total;
-#pragma unroll
-    for (int i = 0; i < MW; ++i) {
-      uint32_t w = mask[i];
-      while (w != 0u) {
-        const int bit = 32 * i + __ffs(w) - 1;
-        w &= w - 1;
-        const int c = bit >> 3, j = bit & 7;
-        const int e = (vbase + c * NT + t) * 8 + j;
-        const uint32_t slot = atomicAdd(&sh.ctl[kCtlLocal], 1u);
-        st_dsmem64(slot0 + 8u * slot, pack(order_key(row[e]), p.id_base + e));
-      }
-    }
-  } else {
-    written = static_cast<uint32_t>(local_exact_topk<DT, C>(sh, row, V, p.vec, p.id_base, vbase, kk, slot0));
-  }
-  if (t == 0) {
-    st_dsmem(dsmem_addr(&sh.scnt[s], 0), written);
-    st_dsmem(dsmem_addr(&sh.flags[s], 0), sh.ctl[kCtlFlags]);
-  }
-  __syncthreads();
-  cluster_arrive();  // B4: this rank's candidates are published
-  if (!leader) return;
-  cluster_wait();
-
-  // ---- leader: merge the slot ranges, then sort and tail ----
-  if (t < 32) {
-    const uint32_t c = t < S ? sh.scnt[t] : 0u;
-    const uint32_t inc = warp_incl_scan(c);
-    uint32_t f = t < S ? sh.flags[t] : 0u;
-    f = __reduce_or_sync(0xFFFFFFFFu, f);
-    if (t < S) {
-      sh.cnt[t] = c;
-      sh.cnt2[t] = inc - c;
-    }
-    if (t == 31) sh.ctl[kCtlN] = inc;
-    if (t == 0) {
-      int st = FS_ROW_OK;
-      if (bad) st = FS_ROW_BAD_PARAM;
-      else if (f & kFlagNaN) st = FS_ROW_NAN;
-      else if (f & kFlagPosInf) st = FS_ROW_POSINF;
-      else if (!(f & kFlagAboveNegInf)) st = FS_ROW_ALL_NEGINF;
-      sh.ctl[kCtlStatus] = static_cast<uint32_t>(st);
-    }
-  }
-  sh.h1[t] = 0u;
-  sh.h2[t] = 0u;
-  __syncthreads();
-  const int st = static_cast<int>(sh.ctl[kCtlStatus]);
-  if (st != FS_ROW_OK) {
-    write_invalid_row(p, b, st);
-    return;
-  }
-  const int n = static_cast<int>(sh.ctl[kCtlN]);
-  {
-    const int mshift = __ffs(static_cast<int>(M)) - 1;
-    for (int i = t; i < S * static_cast<int>(M); i += NT) {
-      const int r = i >> mshift;
-      const int j = i & (static_cast<int>(M) - 1);
-      if (j < static_cast<int>(sh.cnt[r])) tmp[sh.cnt2[r] + j] = surv[i];
-    }
-  }
-  __syncthreads();
-  if (p.stop == 2 || p.stop == 3 || p.stop == 4) {
-    if (t == 0) p.out[b] = p.stop == 4 ? static_cast<int64_t>(n) : static_cast<int64_t>(lkey);
-    return;
-  }
-  // exact kk-th key over the merged candidates, then every candidate at or above it
-  const uint32_t T = kth_largest_packed_key(tmp, n, kk, sh.h1, sh.h2, &sh.ctl[kCtlScr0]);
-  for (int i = t; i < n; i += NT) {
-    const uint64_t x = tmp[i];
-    if (packed_key(x) >= T) surv[atomicAdd(&sh.ctl[kCtlLocal2], 1u)] = x;
-  }
-  __syncthreads();
-  const int nsel = static_cast<int>(sh.ctl[kCtlLocal2]);
-  // sorted top-kk into the upper half of the slot region (the selection is at most half of it)
-  uint64_t* dst = surv + (S * static_cast<int>(M)) / 2;
-  finish_row<DT>(p, b, surv, nsel, dst, kk, pp, u, prob, cum, sh);
-}
-
 // Merge of per-shard candidate blocks [parts, B, K + 1] for vocab-sharded tensor parallelism:
 // one CTA per row, exact top-k over parts*K packed candidates, then the same tail.
 template <int DT>
@@ -1303,26 +949,21 @@ using KernelFn = void (*)(const Params);
 
 constexpr int kChunkOptions[] = {1, 2, 3, 4, 5, 6, 8, 10, 12, 16};
 
-// Kernel families: the global-threshold kernel (any k up to the capacity) and the
-// local-threshold kernel (k up to kLocalMaxK, lower latency).
-template <int DT, bool LOCAL>
+template <int DT>
 KernelFn cluster_kernel_for(int C) {
-#define FS_CASE(CC) \
-  case CC: return LOCAL ? fs_local_kernel<DT, CC> : fs_cluster_kernel<DT, CC>;
   switch (C) {
-    FS_CASE(1)
-    FS_CASE(2)
-    FS_CASE(3)
-    FS_CASE(4)
-    FS_CASE(5)
-    FS_CASE(6)
-    FS_CASE(8)
-    FS_CASE(10)
-    FS_CASE(12)
-    FS_CASE(16)
+    case 1: return fs_cluster_kernel<DT, 1>;
+    case 2: return fs_cluster_kernel<DT, 2>;
+    case 3: return fs_cluster_kernel<DT, 3>;
+    case 4: return fs_cluster_kernel<DT, 4>;
+    case 5: return fs_cluster_kernel<DT, 5>;
+    case 6: return fs_cluster_kernel<DT, 6>;
+    case 8: return fs_cluster_kernel<DT, 8>;
+    case 10: return fs_cluster_kernel<DT, 10>;
+    case 12: return fs_cluster_kernel<DT, 12>;
+    case 16: return fs_cluster_kernel<DT, 16>;
     default: return nullptr;
   }
-#undef FS_CASE
 }
 
 static int pow2_ceil(int64_t x) {
@@ -1337,7 +978,6 @@ static int pow2_floor(int64_t x) {
 }
 
 constexpr int kMaxCap = 8192;
-constexpr int64_t kLocalMaxK = 128;
 
 // Plan of one call: cluster size, chunks per thread, survivor capacity, maxima granularity.
 fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, PlanOut* out) {
@@ -1382,31 +1022,20 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, PlanOut* ou
     if (mpt > 1) mpt /= 2;
     else mgroup *= 2;
   }
+  int cap = std::max(1024, pow2_ceil(4 * K));
+  cap = std::min(cap, kMaxCap);
+  if (cap < K) {
+    set_error("top_k of %lld exceeds the %d-candidate capacity of this build",
+              static_cast<long long>(K), kMaxCap);
+    return FS_EUNSUPPORTED;
+  }
   out->splits = S;
   out->chunks = C;
   out->threads = NT;
-  if (K <= kLocalMaxK) {
-    // local threshold: each rank keeps its own top-K from about 4K of its own maxima; its
-    // slot range holds twice K so that the typical ~1.1K survivors fit in half of it
-    out->local = 1;
-    out->mpt = static_cast<int>(std::min<int64_t>(8, pow2_ceil((4 * K + NT - 1) / NT)));
-    out->mgroup = 1;
-    out->slot = std::max(64, pow2_ceil(2 * K));
-    out->capacity = S * out->slot;
-  } else {
-    int cap = std::max(1024, pow2_ceil(4 * K));
-    cap = std::min(cap, kMaxCap);
-    if (cap < K) {
-      set_error("top_k of %lld exceeds the %d-candidate capacity of this build",
-                static_cast<long long>(K), kMaxCap);
-      return FS_EUNSUPPORTED;
-    }
-    out->local = 0;
-    out->mpt = mpt;
-    out->mgroup = mgroup;
-    out->capacity = cap;
-    out->slot = cap / S;
-  }
+  out->mpt = mpt;
+  out->mgroup = mgroup;
+  out->capacity = cap;
+  out->slot = cap / S;
   out->mcta = NT * out->mpt / out->mgroup;
   out->smem = static_cast<int>(shared_bytes(out->capacity));
   return FS_OK;
@@ -1467,10 +1096,7 @@ static fs_status prepare_kernel(KernelFn fn, int S, int smem) {
 
 static fs_status launch_cluster(int dtype, const PlanOut& plan, int64_t B, const Params& prm,
                                 cudaStream_t stream) {
-  KernelFn fn = plan.local ? (dtype == FS_BF16 ? cluster_kernel_for<1, true>(plan.chunks)
-                                               : cluster_kernel_for<0, true>(plan.chunks))
-                           : (dtype == FS_BF16 ? cluster_kernel_for<1, false>(plan.chunks)
-                                               : cluster_kernel_for<0, false>(plan.chunks));
+  KernelFn fn = dtype == FS_BF16 ? cluster_kernel_for<1>(plan.chunks) : cluster_kernel_for<0>(plan.chunks);
   if (fn == nullptr) {
     set_error("no kernel for %d chunks", plan.chunks);
     return FS_EUNSUPPORTED;
@@ -1621,18 +1247,14 @@ fs_status run_merge(const fs_sample_args* a, const uint64_t* cand, int parts, cu
 
 void append_cluster_attrs(std::vector<fs_kernel_attr>& rows) {
   for (int dt = 0; dt < 2; ++dt) {
-    for (int local = 0; local < 2; ++local) {
-      for (int C : kChunkOptions) {
-        KernelFn fn = local ? (dt ? cluster_kernel_for<1, true>(C) : cluster_kernel_for<0, true>(C))
-                            : (dt ? cluster_kernel_for<1, false>(C) : cluster_kernel_for<0, false>(C));
-        fs_kernel_attr r = {};
-        std::snprintf(r.name, sizeof(r.name), "%s<%s>", local ? "fs_local_kernel" : "fs_cluster_kernel",
-                      dt ? "bf16" : "fp16");
-        r.param = C;
-        r.block = NT;
-        fill_attr(reinterpret_cast<const void*>(fn), NT, static_cast<int>(shared_bytes(1024)), &r);
-        rows.push_back(r);
-      }
+    for (int C : kChunkOptions) {
+      KernelFn fn = dt ? cluster_kernel_for<1>(C) : cluster_kernel_for<0>(C);
+      fs_kernel_attr r = {};
+      std::snprintf(r.name, sizeof(r.name), "fs_cluster_kernel<%s>", dt ? "bf16" : "fp16");
+      r.param = C;
+      r.block = NT;
+      fill_attr(reinterpret_cast<const void*>(fn), NT, static_cast<int>(shared_bytes(1024)), &r);
+      rows.push_back(r);
     }
     fs_kernel_attr r = {};
     std::snprintf(r.name, sizeof(r.name), "fs_merge_kernel<%s>", dt ? "bf16" : "fp16");
