@@ -458,6 +458,26 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_profile_case(args):
+    """A few launches of one configuration, untimed: the target of the ncu captures in profiles/.
+    c1 = the anchor (B=1), c3 = the B=1024 HBM-bound launch."""
+    sys.path.insert(0, str(ROOT))
+    import llm_sampling_kernel_b200 as pkg
+
+    ops = pkg.ops()
+    device = torch.device("cuda", 0)
+    if args.profile_case == "c1":
+        x = anchor_buffers(1, C1["B"], C1["V"], device)[0]
+        k, p = C1["k"], C1["p"]
+    else:
+        x = zipf_buffers(1, C3["B"], C3["V"], device)[0]
+        k, p = C3["k"], C3["p"]
+    for i in range(3):
+        ops.sample_fused(x, k, p, 0x5EED, i, 0)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": args.profile_case, "launches": 3}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -466,7 +486,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--profile-case", choices=["c1", "c3"], default=None,
+                    help="run three untimed launches of one configuration (ncu target) and exit")
     args = ap.parse_args()
+    if args.profile_case:
+        run_profile_case(args)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
