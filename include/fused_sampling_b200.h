@@ -89,11 +89,25 @@ typedef struct fs_sample_args {
   uint8_t* keep;             /* optional device [B, K]: nucleus mask                     */
   float* renormed;           /* optional device [B, K]: p_i / Z_p inside the nucleus     */
   int32_t* row_status;       /* optional device [B]: FS_ROW_*                            */
-  int32_t splits;            /* 0 = auto; else CTAs per row (cluster size 1..16)         */
+  int32_t splits;            /* 0 = auto; else CTAs per row (1..16, rounded up to 2^n)    */
   int32_t stop_phase;        /* 0 = full pipeline; 1..FS_NUM_PHASES ablation stop point  */
+  int32_t path;              /* FS_PATH_AUTO / FS_PATH_CLUSTER / FS_PATH_STREAM          */
+  void* workspace;           /* device scratch for the streaming path (see below)        */
+  uint64_t workspace_bytes;  /* its size; >= fs_workspace_size(args)                     */
 } fs_sample_args;
 
+/* Execution paths. CLUSTER: one launch, one thread-block cluster per row, no workspace (the
+ * latency path). STREAM: two launches - independent CTAs per row slice write candidate lists to
+ * the workspace, one CTA per row merges them (the throughput path for large batches). AUTO
+ * picks by batch size and k. Both compute the same result. */
+enum { FS_PATH_AUTO = 0, FS_PATH_CLUSTER = 1, FS_PATH_STREAM = 2 };
+
 #define FS_NUM_PHASES 7
+
+/* Bytes of device workspace the call described by args needs (0 when its path needs none).
+ * The workspace holds per-call candidate lists only: no state persists between calls, and it
+ * needs no initialisation. Calls that may run concurrently need separate workspaces. */
+FS_API uint64_t fs_workspace_size(const fs_sample_args* args);
 
 /* Fused top-k + top-p + sample, [B, V] -> [B].
  * Replaces: sample_fused / stages_fused / run_fused  (csrc/fused_sampling.cu:426-458,503-513)
@@ -156,8 +170,9 @@ FS_API int32_t fs_kernel_attrs(fs_kernel_attr* rows, int32_t cap);
 /* Human-readable message of the last error raised on the calling host thread. */
 FS_API const char* fs_last_error(void);
 
-/* Plan of a call, for logging and tests: CTAs per row (cluster size), uint4 chunks per
- * thread, threads per CTA, survivor capacity, and maxima per thread / lanes per maximum. */
+/* Plan of a call (automatic path), for logging and tests: CTAs per row, 16-byte chunks per
+ * thread, threads per CTA, survivor capacity, maxima per thread / lanes per maximum, path,
+ * workspace. */
 typedef struct fs_plan_info {
   int32_t splits;
   int32_t chunks;
@@ -166,6 +181,8 @@ typedef struct fs_plan_info {
   int32_t maxima_per_thread;
   int32_t lanes_per_max;
   int32_t smem_bytes;
+  int32_t path;              /* FS_PATH_CLUSTER or FS_PATH_STREAM */
+  uint64_t workspace_bytes;  /* 0 for the cluster path */
 } fs_plan_info;
 FS_API fs_status fs_plan(int64_t batch, int64_t vocab, int64_t top_k, int32_t splits, fs_plan_info* out);
 

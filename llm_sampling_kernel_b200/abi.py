@@ -38,7 +38,9 @@ EXPORTED = (
     "fs_last_error",
     "fs_plan",
     "fs_version",
+    "fs_workspace_size",
 )
+FS_PATH_AUTO, FS_PATH_CLUSTER, FS_PATH_STREAM = 0, 1, 2
 
 
 class FsRng(ctypes.Structure):
@@ -73,6 +75,9 @@ class FsSampleArgs(ctypes.Structure):
         ("row_status", ctypes.c_void_p),
         ("splits", ctypes.c_int32),
         ("stop_phase", ctypes.c_int32),
+        ("path", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_uint64),
     ]
 
 
@@ -97,6 +102,8 @@ class FsPlanInfo(ctypes.Structure):
         ("maxima_per_thread", ctypes.c_int32),
         ("lanes_per_max", ctypes.c_int32),
         ("smem_bytes", ctypes.c_int32),
+        ("path", ctypes.c_int32),
+        ("workspace_bytes", ctypes.c_uint64),
     ]
 
 
@@ -123,6 +130,8 @@ def lib() -> ctypes.CDLL:
         L.fs_last_error.restype = ctypes.c_char_p
         L.fs_version.restype = ctypes.c_char_p
         L.fs_plan.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, P(FsPlanInfo)]
+        L.fs_workspace_size.argtypes = [P(FsSampleArgs)]
+        L.fs_workspace_size.restype = ctypes.c_uint64
         for name in ("fs_sample", "fs_topk", "fs_probe_phase", "fs_shard_candidates", "fs_merge_sample",
                      "fs_probe_noop", "fs_probe_scan_rowblock", "fs_probe_scan_split", "fs_plan"):
             getattr(L, name).restype = ctypes.c_int
@@ -155,13 +164,15 @@ class Plan:
     maxima_per_thread: int
     lanes_per_max: int
     smem_bytes: int
+    path: int
+    workspace_bytes: int
 
 
 def plan(batch: int, vocab: int, top_k: int, splits: int = 0) -> Plan:
     info = FsPlanInfo()
     check(lib().fs_plan(batch, vocab, top_k, splits, ctypes.byref(info)), "fs_plan")
     return Plan(info.splits, info.chunks, info.threads, info.capacity, info.maxima_per_thread,
-                info.lanes_per_max, info.smem_bytes)
+                info.lanes_per_max, info.smem_bytes, info.path, info.workspace_bytes)
 
 
 def kernel_attrs() -> list[tuple]:
@@ -189,7 +200,7 @@ def _stream(stream=None):
 def make_args(logits, top_k: int, top_p: float = 1.0, *, seed: int = 0, offset: int = 0, uniforms=None,
               top_k_rows=None, top_p_rows=None, id_base: int = 0, row_base: int = 0, splits: int = 0,
               out_ids=None, topk_ids=None, keep=None, renormed=None, row_status=None,
-              stop_phase: int = 0) -> FsSampleArgs:
+              stop_phase: int = 0, path: int = FS_PATH_AUTO) -> FsSampleArgs:
     import torch
 
     a = FsSampleArgs()
@@ -217,12 +228,27 @@ def make_args(logits, top_k: int, top_p: float = 1.0, *, seed: int = 0, offset: 
     a.row_status = None if row_status is None else row_status.data_ptr()
     a.splits = splits
     a.stop_phase = stop_phase
+    a.path = path
     return a
+
+
+def attach_workspace(a: FsSampleArgs, device):
+    """Allocates the workspace the call needs (None when it needs none) and records it in `a`.
+    Keep the returned tensor alive until the call's work has run (stream order)."""
+    import torch
+
+    n = lib().fs_workspace_size(ctypes.byref(a))
+    if n == 0:
+        return None
+    ws = torch.empty(n, dtype=torch.uint8, device=device)
+    a.workspace = ws.data_ptr()
+    a.workspace_bytes = n
+    return ws
 
 
 def sample(logits, top_k: int, top_p: float, *, seed: int = 0, offset: int = 0, uniforms=None,
            top_k_rows=None, top_p_rows=None, splits: int = 0, id_base: int = 0, row_base: int = 0,
-           stages: bool = False, stream=None):
+           stages: bool = False, path: int = FS_PATH_AUTO, stream=None):
     """fs_sample through ctypes. Returns ids, or (ids, topk_ids, keep, renormed, status)."""
     import torch
 
@@ -238,20 +264,22 @@ def sample(logits, top_k: int, top_p: float, *, seed: int = 0, offset: int = 0, 
         ren = torch.empty(B, K, dtype=torch.float32, device=dev)
     a = make_args(logits, top_k, top_p, seed=seed, offset=offset, uniforms=uniforms, top_k_rows=top_k_rows,
                   top_p_rows=top_p_rows, id_base=id_base, row_base=row_base, splits=splits, out_ids=out,
-                  topk_ids=ids, keep=keep, renormed=ren, row_status=status)
+                  topk_ids=ids, keep=keep, renormed=ren, row_status=status, path=path)
+    ws = attach_workspace(a, dev)  # noqa: F841  (alive until the launches are enqueued)
     check(lib().fs_sample(ctypes.byref(a), _stream(stream)), "fs_sample")
     if stages:
         return out, ids, keep.bool(), ren, status
     return out
 
 
-def topk(logits, top_k: int, *, splits: int = 0, stream=None):
+def topk(logits, top_k: int, *, splits: int = 0, path: int = FS_PATH_AUTO, stream=None):
     import torch
 
     B, V = logits.shape
     K = min(top_k, V)
     ids = torch.empty(B, K, dtype=torch.int64, device=logits.device)
-    a = make_args(logits, top_k, 1.0, splits=splits, topk_ids=ids)
+    a = make_args(logits, top_k, 1.0, splits=splits, topk_ids=ids, path=path)
+    ws = attach_workspace(a, logits.device)  # noqa: F841
     check(lib().fs_topk(ctypes.byref(a), _stream(stream)), "fs_topk")
     return ids
 
@@ -262,6 +290,7 @@ def shard_candidates(logits, top_k: int, id_base: int, *, splits: int = 0, out=N
     B = logits.shape[0]
     cand = out if out is not None else torch.empty(B, top_k + 1, dtype=torch.int64, device=logits.device)
     a = make_args(logits, top_k, 1.0, id_base=id_base, splits=splits)
+    ws = attach_workspace(a, logits.device)  # noqa: F841
     check(lib().fs_shard_candidates(ctypes.byref(a), _ptr(cand), _stream(stream)), "fs_shard_candidates")
     return cand
 

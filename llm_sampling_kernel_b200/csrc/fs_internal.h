@@ -20,12 +20,16 @@ struct PlanOut {
   int mcta;      // maxima per CTA
   int slot;      // survivor slots per rank in the leader's buffer
   int smem;      // dynamic shared memory bytes per CTA
+  int stream;    // 1: streaming path (slice + row-merge launches), 0: cluster path
+  int merge_cap; // streaming: gathered-candidate capacity of the row merge (power of two)
+  int merge_smem;
+  uint64_t workspace;  // streaming: workspace bytes
 };
 
 // printf-style message for fs_last_error() on this host thread.
 void set_error(const char* fmt, ...);
 
-fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, PlanOut* out);
+fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t path, PlanOut* out);
 fs_status run_cluster(const fs_sample_args* a, int mode, uint64_t* cand_out, cudaStream_t stream);
 fs_status run_merge(const fs_sample_args* a, const uint64_t* cand, int parts, cudaStream_t stream);
 

@@ -223,6 +223,44 @@ __device__ uint32_t kth_largest_key(const uint32_t* keys, int n, int kk, uint32_
   return result[0];
 }
 
+// A lower bound L on the want-th largest of the n 16-bit keys in shared memory: one 256-bin
+// histogram anchored at the largest key (bin = (max - key) >> sh, clamped to the last bin), the
+// boundary found by one warp scan, L = the lower edge of the boundary bin. With sh == 0 and the
+// boundary below the last bin, L is exactly the want-th largest key. At least `want` keys are
+// >= L. Returns 0 when n < want. h: 256 zeroed shared words; scratch: >= 9 shared words. Every
+// thread of the CTA calls it.
+__device__ uint32_t anchored_threshold(const uint32_t* keys, int n, int want, int sh, uint32_t* h,
+                                       uint32_t* scratch) {
+  const int t = threadIdx.x;
+  uint32_t m = 0u;
+  for (int i = t; i < n; i += NT) m = max(m, keys[i]);
+  m = __reduce_max_sync(0xFFFFFFFFu, m);
+  if ((t & 31) == 0) scratch[t >> 5] = m;
+  __syncthreads();
+  uint32_t kmax = 0u;
+#pragma unroll
+  for (int w = 0; w < NT / 32; ++w) kmax = max(kmax, scratch[w]);
+  for (int i = t; i < n; i += NT) {
+    const uint32_t bin = min(255u, (kmax - keys[i]) >> sh);
+    atomicAdd(&h[255u - bin], 1u);  // reversed so that the top of the histogram is the largest key
+  }
+  __syncthreads();
+  if (t < 32) {
+    uint32_t idx = 0u, above = 0u, L = 0u;
+    if (warp_boundary_256(h, static_cast<uint32_t>(want), &idx, &above)) {
+      const uint32_t bin = 255u - idx;
+      if (bin < 255u) {
+        const uint32_t hi = kmax - (bin << sh);
+        const uint32_t width = (1u << sh) - 1u;
+        L = hi > width ? hi - width : 0u;
+      }
+    }
+    if (t == 0) scratch[8] = L;
+  }
+  __syncthreads();
+  return scratch[8];
+}
+
 __device__ __forceinline__ float row_uniform(const Params& p, int b) {
   if (p.uniforms != nullptr) return p.uniforms[b];
   uint64_t seed = p.seed, off = p.offset;
@@ -895,6 +933,326 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
   cluster_wait();
 }
 
+// ------------------------------------------------------------------------------------------
+// Streaming path for large batches: two launches, no cross-CTA waiting.
+//   fs_slice_kernel: one CTA per (slice, row). The slice is read once into registers; the CTA
+//     keeps every element >= L_s, a lower bound on its own kk-th largest element (the kk-th
+//     largest of about 4kk of its sub-chunk maxima, from one anchored histogram), and writes them
+//     as packed candidates to cand[b][s][0..n) with n | flags << 24 in cnt[b][s]. A slice whose
+//     survivors would not fit its M slots writes its exact top-kk instead. The union over the
+//     slices holds the row's top-kk.
+//   fs_rowmerge_kernel: one CTA per row. It gathers the slices' candidates (L2-resident), finds
+//     the boundary of the kk-th largest with the anchored histogram, ranks the candidates at or
+//     above it, and runs the same tail as the cluster kernel.
+// ------------------------------------------------------------------------------------------
+
+constexpr uint32_t kCountMask = 0xFFFFFFu;
+
+// Exact top-kk of this CTA's slice alone (heavy ties), written to slots[0..) in global memory:
+// two 8-bit radix levels over the slice (re-read from L1/L2) give the kk-th key T; the elements
+// above T and the lowest-id ties at T (ranked in id order: chunk, thread, lane) are written.
+// Returns min(kk, valid elements). Every thread of the CTA calls it.
+template <int DT, int C>
+__device__ __noinline__ int slice_exact_topk(Shared& sh, const uint16_t* __restrict__ row, int V, int vec,
+                                             uint32_t id_base, int vbase, int kk, uint64_t* slots) {
+  const int t = threadIdx.x;
+  const int valid = max(0, min(V - vbase * 8, C * NT * 8));
+  const int want = min(kk, valid);
+  if (want == 0) return 0;
+  sh.h1[t] = 0u;
+  sh.h2[t] = 0u;
+  if (t == 0) sh.ctl[kCtlLocal] = 0u;
+  __syncthreads();
+#pragma unroll 1
+  for (int c = 0; c < C; ++c) {
+    const int e0 = (vbase + c * NT + t) * 8;
+    const uint4 v = load_chunk<DT>(row, e0, V, vec);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t w = word_of(v, q);
+      if (e0 + 2 * q < V) atomicAdd(&sh.h1[order_key(w & 0xFFFFu) >> 8], 1u);
+      if (e0 + 2 * q + 1 < V) atomicAdd(&sh.h1[order_key(w >> 16) >> 8], 1u);
+    }
+  }
+  __syncthreads();
+  if (t < 32) {
+    uint32_t hb = 0u, above = 0u;
+    warp_boundary_256(sh.h1, static_cast<uint32_t>(want), &hb, &above);
+    if (t == 0) {
+      sh.ctl[kCtlHb] = hb;
+      sh.ctl[kCtlAbove] = above;
+    }
+  }
+  __syncthreads();
+  const uint32_t hb = sh.ctl[kCtlHb];
+  const uint32_t n_above = sh.ctl[kCtlAbove];
+#pragma unroll 1
+  for (int c = 0; c < C; ++c) {
+    const int e0 = (vbase + c * NT + t) * 8;
+    const uint4 v = load_chunk<DT>(row, e0, V, vec);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t w = word_of(v, q);
+      const uint32_t k0 = order_key(w & 0xFFFFu), k1 = order_key(w >> 16);
+      if (e0 + 2 * q < V && (k0 >> 8) == hb) atomicAdd(&sh.h2[k0 & 0xFFu], 1u);
+      if (e0 + 2 * q + 1 < V && (k1 >> 8) == hb) atomicAdd(&sh.h2[k1 & 0xFFu], 1u);
+    }
+  }
+  __syncthreads();
+  if (t < 32) {
+    uint32_t lb = 0u, above2 = 0u;
+    warp_boundary_256(sh.h2, static_cast<uint32_t>(want) - n_above, &lb, &above2);
+    if (t == 0) {
+      sh.ctl[kCtlT] = (hb << 8) | lb;
+      sh.ctl[kCtlNgt] = n_above + above2;
+    }
+  }
+  __syncthreads();
+  const uint32_t T = sh.ctl[kCtlT];
+  const uint32_t n_gt = sh.ctl[kCtlNgt];
+  const uint32_t need = static_cast<uint32_t>(want) - n_gt;
+  uint32_t chunk_base = 0u;
+#pragma unroll 1
+  for (int c = 0; c < C; ++c) {
+    const int e0 = (vbase + c * NT + t) * 8;
+    const uint4 v = load_chunk<DT>(row, e0, V, vec);
+    uint32_t mask = 0u;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t w = word_of(v, q);
+      const uint32_t k0 = order_key(w & 0xFFFFu), k1 = order_key(w >> 16);
+      if (e0 + 2 * q < V) {
+        if (k0 > T) slots[atomicAdd(&sh.ctl[kCtlLocal], 1u)] = pack(k0, id_base + e0 + 2 * q);
+        if (k0 == T) mask |= 1u << (2 * q);
+      }
+      if (e0 + 2 * q + 1 < V) {
+        if (k1 > T) slots[atomicAdd(&sh.ctl[kCtlLocal], 1u)] = pack(k1, id_base + e0 + 2 * q + 1);
+        if (k1 == T) mask |= 1u << (2 * q + 1);
+      }
+    }
+    const uint32_t cnt = __popc(mask);
+    uint32_t ctot;
+    const uint32_t excl = block_incl_scan<uint32_t, NT>(cnt, sh.uscr, &ctot) - cnt;
+    uint32_t rank = chunk_base + excl;
+    while (mask != 0u && rank < need) {
+      const int j = __ffs(mask) - 1;
+      mask &= mask - 1;
+      slots[n_gt + rank] = pack(T, id_base + e0 + j);
+      ++rank;
+    }
+    chunk_base += ctot;
+  }
+  return want;
+}
+
+template <int DT, int C>
+__global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_slice_kernel(const Params p, uint64_t* __restrict__ cand,
+                                                                      uint32_t* __restrict__ cnt) {
+  const int S = static_cast<int>(gridDim.x);
+  const int s = blockIdx.x;
+  const int b = blockIdx.y;
+  const int t = threadIdx.x;
+  const int V = p.vocab;
+  const uint32_t M = static_cast<uint32_t>(p.slot);
+  Shared& sh = *reinterpret_cast<Shared*>(g_smem);
+
+  int kk;
+  float pp;
+  bool bad;
+  row_params(p, b, &kk, &pp, &bad);
+
+  const uint16_t* row = p.logits + static_cast<int64_t>(b) * p.row_stride;
+  const int vbase = s * C * NT;
+  uint4 v[C];
+  const bool full = p.vec && (vbase + C * NT) * 8 <= V;
+  if (full) {
+    const uint4* rv = reinterpret_cast<const uint4*>(row) + vbase + t;
+#pragma unroll
+    for (int c = 0; c < C; ++c) v[c] = __ldg(rv + c * NT);
+  } else {
+#pragma unroll
+    for (int c = 0; c < C; ++c) v[c] = load_chunk<DT>(row, (vbase + c * NT + t) * 8, V, p.vec);
+  }
+  sh.h1[t] = 0u;
+  if (t < 16) sh.ctl[t] = 0u;
+
+  // sub-chunk maxima of this thread (mpt of them) and the row flags they carry
+  uint32_t mx[4] = {Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2};
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) mx[q] = pair_max_nan<DT>(mx[q], word_of(v[c], q));
+  }
+  uint32_t m16[8];
+  int nm;
+  if (p.mpt == 8) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      m16[2 * q] = mx[q] & 0xFFFFu;
+      m16[2 * q + 1] = mx[q] >> 16;
+    }
+    nm = 8;
+  } else if (p.mpt == 4) {
+    const uint32_t a = pair_max_nan<DT>(mx[0], mx[2]), c2 = pair_max_nan<DT>(mx[1], mx[3]);
+    m16[0] = a & 0xFFFFu;
+    m16[1] = a >> 16;
+    m16[2] = c2 & 0xFFFFu;
+    m16[3] = c2 >> 16;
+    nm = 4;
+  } else {
+    const uint32_t a = pair_max_nan<DT>(pair_max_nan<DT>(mx[0], mx[2]), pair_max_nan<DT>(mx[1], mx[3]));
+    if (p.mpt == 2) {
+      m16[0] = a & 0xFFFFu;
+      m16[1] = a >> 16;
+      nm = 2;
+    } else {
+      m16[0] = half_max_nan<DT>(a & 0xFFFFu, a >> 16);
+      nm = 1;
+    }
+  }
+  uint32_t flags = 0u;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (i >= nm) break;
+    const uint32_t bits = m16[i];
+    if (Fmt<DT>::is_nan(bits)) {
+      flags |= kFlagNaN;
+    } else {
+      if (bits == Fmt<DT>::kPosInf) flags |= kFlagPosInf;
+      if (bits != Fmt<DT>::kNegInf) flags |= kFlagAboveNegInf;
+    }
+    sh.mkeys[t * nm + i] = order_key(bits);
+  }
+  if (flags != 0u) atomicOr(&sh.ctl[kCtlFlags], flags);
+  __syncthreads();
+
+  // L_s: at most kk of this slice's elements lie above the kk-th largest of its maxima
+  constexpr int kSh = DT ? 0 : 2;  // bf16: one key per bin; fp16: four (same span in value)
+  const uint32_t kth = anchored_threshold(sh.mkeys, NT * nm, kk, kSh, sh.h1, sh.uscr);
+  const uint32_t lkey = max(kth, order_key(Fmt<DT>::kNegInf));
+  const uint32_t lbits = key_to_bits(lkey);
+  const uint32_t l2 = lbits | (lbits << 16);
+
+  constexpr int MW = (C * 8 + 31) / 32;
+  uint32_t mask[MW];
+#pragma unroll
+  for (int i = 0; i < MW; ++i) mask[i] = 0u;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t m = pair_ge_mask<DT>(word_of(v[c], q), l2);
+      const uint32_t bits2 = (m & 1u) | ((m >> 15) & 2u);
+      const int bit = 8 * c + 2 * q;
+      mask[bit >> 5] |= bits2 << (bit & 31);
+    }
+  }
+  if (!full) {  // elements past the end of the row read as -inf: never candidates
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const int e0 = (vbase + c * NT + t) * 8;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int bit = 8 * c + j;
+        if (e0 + j >= V) mask[bit >> 5] &= ~(1u << (bit & 31));
+      }
+    }
+  }
+  uint32_t mine = 0u;
+#pragma unroll
+  for (int i = 0; i < MW; ++i) mine += __popc(mask[i]);
+  const uint32_t total = block_sum<uint32_t, NT>(mine, sh.uscr);
+  uint64_t* slots = cand + (static_cast<size_t>(b) * S + s) * M;
+  uint32_t written;
+  if (total <= M) {
+    written = total;
+#pragma unroll
+    for (int i = 0; i < MW; ++i) {
+      uint32_t w = mask[i];
+      while (w != 0u) {
+        const int bit = 32 * i + __ffs(w) - 1;
+        w &= w - 1;
+        const int c = bit >> 3, j = bit & 7;
+        const int e = (vbase + c * NT + t) * 8 + j;
+        slots[atomicAdd(&sh.ctl[kCtlLocal], 1u)] = pack(order_key(row[e]), p.id_base + e);
+      }
+    }
+  } else {
+    written = static_cast<uint32_t>(slice_exact_topk<DT, C>(sh, row, V, p.vec, p.id_base, vbase, kk, slots));
+  }
+  if (t == 0) cnt[static_cast<size_t>(b) * S + s] = written | (sh.ctl[kCtlFlags] << 24);
+}
+
+template <int DT>
+__global__ void __launch_bounds__(NT) fs_rowmerge_kernel(const Params p, const uint64_t* __restrict__ cand,
+                                                         const uint32_t* __restrict__ cnt, int S) {
+  const int b = blockIdx.x;
+  const int t = threadIdx.x;
+  const uint32_t M = static_cast<uint32_t>(p.slot);
+  Shared& sh = *reinterpret_cast<Shared*>(g_smem);
+  uint64_t* gath = reinterpret_cast<uint64_t*>(g_smem + sizeof(Shared));  // cap words
+  uint64_t* sel = gath + p.cap;                                             // cap words
+  float* prob = reinterpret_cast<float*>(sel + p.cap);
+  float* cum = prob + p.cap;
+
+  int kk;
+  float pp;
+  bool bad;
+  row_params(p, b, &kk, &pp, &bad);
+  const float u = t < 32 ? row_uniform(p, b) : 0.0f;
+  sh.h1[t] = 0u;
+  if (t < 16) sh.ctl[t] = 0u;
+  if (t < 32) {
+    const uint32_t w = t < S ? __ldcg(cnt + static_cast<size_t>(b) * S + t) : 0u;
+    const uint32_t c = w & kCountMask;
+    const uint32_t inc = warp_incl_scan(c);
+    const uint32_t f = __reduce_or_sync(0xFFFFFFFFu, w >> 24);
+    if (t < S) {
+      sh.cnt[t] = c;
+      sh.cnt2[t] = inc - c;
+    }
+    if (t == 31) sh.ctl[kCtlN] = inc;
+    if (t == 0) {
+      int st = FS_ROW_OK;
+      if (bad) st = FS_ROW_BAD_PARAM;
+      else if (f & kFlagNaN) st = FS_ROW_NAN;
+      else if (f & kFlagPosInf) st = FS_ROW_POSINF;
+      else if (!(f & kFlagAboveNegInf)) st = FS_ROW_ALL_NEGINF;
+      sh.ctl[kCtlStatus] = static_cast<uint32_t>(st);
+    }
+  }
+  __syncthreads();
+  const int st = static_cast<int>(sh.ctl[kCtlStatus]);
+  if (st != FS_ROW_OK) {
+    write_invalid_row(p, b, st);
+    return;
+  }
+  const int n = static_cast<int>(sh.ctl[kCtlN]);
+  // gather: rank r's slots [0, cnt[r]) to [prefix[r], ...), keys alongside
+  {
+    const uint64_t* rowc = cand + static_cast<size_t>(b) * S * M;
+    const int mshift = __ffs(static_cast<int>(M)) - 1;
+    for (int i = t; i < S * static_cast<int>(M); i += NT) {
+      const int r = i >> mshift;
+      const int j = i & (static_cast<int>(M) - 1);
+      if (j < static_cast<int>(sh.cnt[r])) {
+        const uint64_t x = __ldcg(rowc + i);
+        const int d = static_cast<int>(sh.cnt2[r]) + j;
+        gath[d] = x;
+        sh.mkeys[d] = packed_key(x);
+      }
+    }
+  }
+  __syncthreads();
+  constexpr int kSh = DT ? 0 : 2;
+  const uint32_t E = anchored_threshold(sh.mkeys, n, kk, kSh, sh.h1, sh.uscr);
+  for (int i = t; i < n; i += NT) {
+    if (sh.mkeys[i] >= E) sel[atomicAdd(&sh.ctl[kCtlLocal], 1u)] = gath[i];
+  }
+  __syncthreads();
+  finish_row<DT>(p, b, sel, static_cast<int>(sh.ctl[kCtlLocal]), gath, kk, pp, u, prob, cum, sh);
+}
+
 // Merge of per-shard candidate blocks [parts, B, K + 1] for vocab-sharded tensor parallelism:
 // one CTA per row, exact top-k over parts*K packed candidates, then the same tail.
 template <int DT>
@@ -978,9 +1336,11 @@ static int pow2_floor(int64_t x) {
 }
 
 constexpr int kMaxCap = 8192;
+constexpr int64_t kStreamMaxK = 256;     // streaming path: top-K bound
+constexpr int64_t kStreamMinBatch = 128;  // AUTO: rows from which the streaming path is used
 
 // Plan of one call: cluster size, chunks per thread, survivor capacity, maxima granularity.
-fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, PlanOut* out) {
+fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t path, PlanOut* out) {
   const int64_t per_cta_chunk = static_cast<int64_t>(NT) * 8;  // elements per chunk per CTA
   constexpr int kMaxChunks = 16;
   const int64_t min_s = std::max<int64_t>(1, (V + per_cta_chunk * kMaxChunks - 1) / (per_cta_chunk * kMaxChunks));
@@ -1038,6 +1398,45 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, PlanOut* ou
   out->slot = cap / S;
   out->mcta = NT * out->mpt / out->mgroup;
   out->smem = static_cast<int>(shared_bytes(out->capacity));
+  out->stream = 0;
+  out->merge_cap = 0;
+  out->merge_smem = 0;
+  out->workspace = 0;
+
+  // streaming path: slices keep their own top-K in M slots; the row merge gathers S * M
+  const int M = std::max(64, pow2_ceil(2 * K));
+  // fewer, longer slices when S * M candidates would not fit the row merge's key buffer
+  int Ss = S;
+  while (Ss > 1 && static_cast<int64_t>(Ss) * M > kMaxMaxima) Ss /= 2;
+  int Cs = 0;
+  for (int opt : kChunkOptions) {
+    if (static_cast<int64_t>(opt) * per_cta_chunk * Ss >= V) {
+      Cs = opt;
+      break;
+    }
+  }
+  // (the slice launch puts rows on grid.y, at most 65535)
+  const bool stream_fits = K <= kStreamMaxK && static_cast<int64_t>(Ss) * M <= kMaxMaxima && Cs > 0 && B <= 65535;
+  const bool want_stream = path == FS_PATH_STREAM || (path == FS_PATH_AUTO && B >= kStreamMinBatch);
+  if (path == FS_PATH_STREAM && !stream_fits) {
+    set_error("the streaming path supports top_k <= %lld with splits * slots <= %d and batch <= 65535",
+              static_cast<long long>(kStreamMaxK), kMaxMaxima);
+    return FS_EUNSUPPORTED;
+  }
+  if (want_stream && stream_fits) {
+    S = Ss;
+    out->splits = Ss;
+    out->chunks = Cs;
+    out->stream = 1;
+    out->mpt = static_cast<int>(std::min<int64_t>(8, pow2_ceil((4 * K + NT - 1) / NT)));
+    out->mgroup = 1;
+    out->mcta = NT * out->mpt;
+    out->slot = M;
+    out->smem = static_cast<int>(sizeof(Shared));
+    out->merge_cap = std::max(256, pow2_ceil(static_cast<int64_t>(S) * M));
+    out->merge_smem = static_cast<int>(sizeof(Shared) + static_cast<size_t>(out->merge_cap) * 24);
+    out->workspace = static_cast<uint64_t>(B) * S * M * sizeof(uint64_t) + static_cast<uint64_t>(B) * S * 4 + 256;
+  }
   return FS_OK;
 }
 
@@ -1199,10 +1598,71 @@ static Params base_params(const fs_sample_args* a, int64_t K) {
   return prm;
 }
 
+template <int DT>
+KernelFn slice_kernel_for(int C) {
+  switch (C) {
+    case 1: return reinterpret_cast<KernelFn>(fs_slice_kernel<DT, 1>);
+    case 2: return reinterpret_cast<KernelFn>(fs_slice_kernel<DT, 2>);
+    case 3: return reinterpret_cast<KernelFn>(fs_slice_kernel<DT, 3>);
+    case 4: return reinterpret_cast<KernelFn>(fs_slice_kernel<DT, 4>);
+    case 5: return reinterpret_cast<KernelFn>(fs_slice_kernel<DT, 5>);
+    case 6: return reinterpret_cast<KernelFn>(fs_slice_kernel<DT, 6>);
+    case 8: return reinterpret_cast<KernelFn>(fs_slice_kernel<DT, 8>);
+    case 10: return reinterpret_cast<KernelFn>(fs_slice_kernel<DT, 10>);
+    case 12: return reinterpret_cast<KernelFn>(fs_slice_kernel<DT, 12>);
+    case 16: return reinterpret_cast<KernelFn>(fs_slice_kernel<DT, 16>);
+    default: return nullptr;
+  }
+}
+
+using SliceFn = void (*)(const Params, uint64_t*, uint32_t*);
+using RowMergeFn = void (*)(const Params, const uint64_t*, const uint32_t*, int);
+
+static fs_status launch_stream(const fs_sample_args* a, const PlanOut& plan, const Params& prm,
+                               cudaStream_t stream) {
+  if (a->workspace == nullptr || a->workspace_bytes < plan.workspace) {
+    set_error("the streaming path needs %llu bytes of workspace (got %llu)",
+              static_cast<unsigned long long>(plan.workspace),
+              static_cast<unsigned long long>(a->workspace == nullptr ? 0 : a->workspace_bytes));
+    return FS_EWORKSPACE;
+  }
+  const uintptr_t base = (reinterpret_cast<uintptr_t>(a->workspace) + 255) & ~static_cast<uintptr_t>(255);
+  uint64_t* cand = reinterpret_cast<uint64_t*>(base);
+  uint32_t* cnt = reinterpret_cast<uint32_t*>(cand + static_cast<size_t>(a->batch) * plan.splits * plan.slot);
+  SliceFn sfn = reinterpret_cast<SliceFn>(a->dtype == FS_BF16 ? slice_kernel_for<1>(plan.chunks)
+                                                               : slice_kernel_for<0>(plan.chunks));
+  RowMergeFn mfn = a->dtype == FS_BF16 ? fs_rowmerge_kernel<1> : fs_rowmerge_kernel<0>;
+  if (sfn == nullptr) {
+    set_error("no slice kernel for %d chunks", plan.chunks);
+    return FS_EUNSUPPORTED;
+  }
+  fs_status st = prepare_kernel(reinterpret_cast<KernelFn>(sfn), 1, plan.smem);
+  if (st != FS_OK) return st;
+  st = prepare_kernel(reinterpret_cast<KernelFn>(mfn), 1, plan.merge_smem);
+  if (st != FS_OK) return st;
+  sfn<<<dim3(plan.splits, static_cast<unsigned>(a->batch)), NT, plan.smem, stream>>>(prm, cand, cnt);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("slice launch: %s", cudaGetErrorString(e));
+    return FS_ELAUNCH;
+  }
+  Params mp = prm;
+  mp.cap = plan.merge_cap;
+  mfn<<<static_cast<unsigned>(a->batch), NT, plan.merge_smem, stream>>>(mp, cand, cnt, plan.splits);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("row-merge launch: %s", cudaGetErrorString(e));
+    return FS_ELAUNCH;
+  }
+  return FS_OK;
+}
+
 fs_status run_cluster(const fs_sample_args* a, int mode, uint64_t* cand_out, cudaStream_t stream) {
   const int64_t K = std::min<int64_t>(a->top_k, a->vocab);
   PlanOut plan;
-  fs_status st = make_plan(a->batch, a->vocab, K, a->splits, &plan);
+  // the ablation probe instruments the cluster kernel's phases
+  const int32_t path = a->stop_phase != 0 ? FS_PATH_CLUSTER : a->path;
+  fs_status st = make_plan(a->batch, a->vocab, K, a->splits, path, &plan);
   if (st != FS_OK) return st;
   Params prm = base_params(a, K);
   prm.cand_out = cand_out;
@@ -1213,7 +1673,17 @@ fs_status run_cluster(const fs_sample_args* a, int mode, uint64_t* cand_out, cud
   prm.slot = plan.slot;
   prm.stop = a->stop_phase;
   prm.mode = mode;
+  if (plan.stream) return launch_stream(a, plan, prm, stream);
   return launch_cluster(a->dtype, plan, a->batch, prm, stream);
+}
+
+uint64_t workspace_size(const fs_sample_args* a) {
+  if (a == nullptr || a->batch < 1 || a->vocab < 1 || a->top_k < 1) return 0;
+  PlanOut plan;
+  const int32_t path = a->stop_phase != 0 ? FS_PATH_CLUSTER : a->path;
+  if (make_plan(a->batch, a->vocab, std::min<int64_t>(a->top_k, a->vocab), a->splits, path, &plan) != FS_OK)
+    return 0;
+  return plan.stream ? plan.workspace : 0;
 }
 
 fs_status run_merge(const fs_sample_args* a, const uint64_t* cand, int parts, cudaStream_t stream) {
@@ -1254,6 +1724,24 @@ void append_cluster_attrs(std::vector<fs_kernel_attr>& rows) {
       r.param = C;
       r.block = NT;
       fill_attr(reinterpret_cast<const void*>(fn), NT, static_cast<int>(shared_bytes(1024)), &r);
+      rows.push_back(r);
+    }
+    for (int C : kChunkOptions) {
+      KernelFn fn = dt ? slice_kernel_for<1>(C) : slice_kernel_for<0>(C);
+      fs_kernel_attr r = {};
+      std::snprintf(r.name, sizeof(r.name), "fs_slice_kernel<%s>", dt ? "bf16" : "fp16");
+      r.param = C;
+      r.block = NT;
+      fill_attr(reinterpret_cast<const void*>(fn), NT, static_cast<int>(sizeof(Shared)), &r);
+      rows.push_back(r);
+    }
+    {
+      fs_kernel_attr r = {};
+      std::snprintf(r.name, sizeof(r.name), "fs_rowmerge_kernel<%s>", dt ? "bf16" : "fp16");
+      r.param = 0;
+      r.block = NT;
+      fill_attr(reinterpret_cast<const void*>(dt ? fs_rowmerge_kernel<1> : fs_rowmerge_kernel<0>), NT,
+                static_cast<int>(sizeof(Shared) + 1024 * 24), &r);
       rows.push_back(r);
     }
     fs_kernel_attr r = {};
@@ -1361,6 +1849,8 @@ extern "C" fs_status fs_merge_sample(const fs_sample_args* a, const uint64_t* ca
   return fsb::run_merge(a, cand, parts, reinterpret_cast<cudaStream_t>(stream));
 }
 
+extern "C" uint64_t fs_workspace_size(const fs_sample_args* a) { return fsb::workspace_size(a); }
+
 extern "C" fs_status fs_plan(int64_t batch, int64_t vocab, int64_t top_k, int32_t splits,
                              fs_plan_info* out) {
   if (out == nullptr || batch < 1 || vocab < 1 || top_k < 1) {
@@ -1368,7 +1858,7 @@ extern "C" fs_status fs_plan(int64_t batch, int64_t vocab, int64_t top_k, int32_
     return FS_EINVAL;
   }
   fsb::PlanOut p;
-  fs_status st = fsb::make_plan(batch, vocab, std::min(top_k, vocab), splits, &p);
+  fs_status st = fsb::make_plan(batch, vocab, std::min(top_k, vocab), splits, FS_PATH_AUTO, &p);
   if (st != FS_OK) return st;
   out->splits = p.splits;
   out->chunks = p.chunks;
@@ -1377,5 +1867,7 @@ extern "C" fs_status fs_plan(int64_t batch, int64_t vocab, int64_t top_k, int32_
   out->maxima_per_thread = p.mpt;
   out->lanes_per_max = p.mgroup;
   out->smem_bytes = p.smem;
+  out->path = p.stream ? FS_PATH_STREAM : FS_PATH_CLUSTER;
+  out->workspace_bytes = p.workspace;
   return FS_OK;
 }

@@ -86,6 +86,17 @@ void set_rng(fs_rng* rng, int64_t seed, int64_t offset) {
 
 int64_t clamp_k(const torch::Tensor& logits, int64_t top_k) { return std::min(top_k, logits.size(1)); }
 
+// Device workspace for the streaming path, from torch's caching allocator (stream-ordered, so it
+// may be released as soon as the launches are enqueued). Empty when the plan needs none.
+torch::Tensor attach_workspace(fs_sample_args* a, const torch::Tensor& like) {
+  const uint64_t bytes = fs_workspace_size(a);
+  if (bytes == 0) return torch::Tensor();
+  auto ws = torch::empty({static_cast<int64_t>(bytes)}, like.options().dtype(torch::kUInt8));
+  a->workspace = ws.data_ptr();
+  a->workspace_bytes = bytes;
+  return ws;
+}
+
 torch::Tensor empty_i64(const torch::Tensor& like, at::IntArrayRef shape) {
   return torch::empty(shape, like.options().dtype(torch::kInt64));
 }
@@ -102,6 +113,7 @@ torch::Tensor sample_fused(torch::Tensor logits, int64_t top_k, double top_p, in
   fs_sample_args a = base_args(logits, top_k, top_p, splits_override);
   set_rng(&a.rng, seed, offset);
   a.out_ids = out.data_ptr<int64_t>();
+  auto ws = attach_workspace(&a, logits);
   check(fs_sample(&a, current_stream()), "fs_sample");
   return out;
 }
@@ -114,6 +126,7 @@ torch::Tensor topk_fused(torch::Tensor logits, int64_t top_k, int64_t splits_ove
   auto ids = empty_i64(logits, {logits.size(0), K});
   fs_sample_args a = base_args(logits, top_k, 1.0, splits_override);
   a.topk_ids = ids.data_ptr<int64_t>();
+  auto ws = attach_workspace(&a, logits);
   check(fs_topk(&a, current_stream()), "fs_topk");
   return ids;
 }
@@ -134,6 +147,7 @@ std::vector<torch::Tensor> stages_fused(torch::Tensor logits, int64_t top_k, dou
   a.out_ids = out.data_ptr<int64_t>();
   a.keep = reinterpret_cast<uint8_t*>(keep.data_ptr<bool>());
   a.renormed = renormed.data_ptr<float>();
+  auto ws = attach_workspace(&a, logits);
   check(fs_sample(&a, current_stream()), "fs_sample");
   return {out, keep, renormed};
 }
@@ -237,7 +251,7 @@ void fill_rows(fs_sample_args* a, const torch::Tensor& logits,
 std::vector<std::optional<torch::Tensor>> sample_ex(
     torch::Tensor logits, int64_t top_k, double top_p, std::optional<torch::Tensor> top_k_rows,
     std::optional<torch::Tensor> top_p_rows, std::optional<torch::Tensor> uniforms, int64_t seed,
-    int64_t offset, int64_t splits, int64_t id_base, int64_t row_base, bool return_stages) {
+    int64_t offset, int64_t splits, int64_t id_base, int64_t row_base, bool return_stages, int64_t path) {
   check_logits(logits);
   check_top_k(top_k);
   if (!top_p_rows.has_value()) check_top_p(top_p);
@@ -261,6 +275,8 @@ std::vector<std::optional<torch::Tensor>> sample_ex(
     a.keep = reinterpret_cast<uint8_t*>(keep->data_ptr<bool>());
     a.renormed = ren->data_ptr<float>();
   }
+  a.path = static_cast<int32_t>(path);
+  auto ws = attach_workspace(&a, logits);
   check(fs_sample(&a, current_stream()), "fs_sample");
   return {out, ids, keep, ren, status};
 }
@@ -275,6 +291,7 @@ torch::Tensor shard_candidates(torch::Tensor logits, int64_t top_k, int64_t id_b
   auto cand = empty_i64(logits, {B, top_k + 1});
   fs_sample_args a = base_args(logits, top_k, 1.0, splits);
   a.id_base = id_base;
+  auto ws = attach_workspace(&a, logits);
   check(fs_shard_candidates(&a, reinterpret_cast<uint64_t*>(cand.data_ptr<int64_t>()), current_stream()),
         "fs_shard_candidates");
   return cand;
@@ -313,11 +330,12 @@ std::vector<torch::Tensor> merge_sample(torch::Tensor cand, bool bf16, int64_t t
   return {out, status};
 }
 
-std::tuple<int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t> plan(int64_t batch, int64_t vocab,
-                                                                               int64_t top_k, int64_t splits) {
+std::tuple<int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t> plan(
+    int64_t batch, int64_t vocab, int64_t top_k, int64_t splits) {
   fs_plan_info p = {};
   check(fs_plan(batch, vocab, top_k, static_cast<int32_t>(splits), &p), "fs_plan");
-  return {p.splits, p.chunks, p.threads, p.capacity, p.maxima_per_thread, p.lanes_per_max, p.smem_bytes};
+  return {p.splits, p.chunks, p.threads, p.capacity, p.maxima_per_thread, p.lanes_per_max, p.smem_bytes,
+          p.path, static_cast<int64_t>(p.workspace_bytes)};
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -333,7 +351,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("logits"), py::arg("top_k"), py::arg("top_p"), py::arg("top_k_rows") = py::none(),
         py::arg("top_p_rows") = py::none(), py::arg("uniforms") = py::none(), py::arg("seed") = 0,
         py::arg("offset") = -1, py::arg("splits") = 0, py::arg("id_base") = 0,
-        py::arg("row_base") = 0, py::arg("return_stages") = false);
+        py::arg("row_base") = 0, py::arg("return_stages") = false, py::arg("path") = 0);
   m.def("shard_candidates", &shard_candidates, "vocab-shard local top-k as packed candidates",
         py::arg("logits"), py::arg("top_k"), py::arg("id_base"), py::arg("splits") = 0);
   m.def("merge_sample", &merge_sample, "merge gathered shard candidates and sample",
@@ -341,6 +359,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("top_k_rows") = py::none(), py::arg("top_p_rows") = py::none(),
         py::arg("uniforms") = py::none(), py::arg("seed") = 0, py::arg("offset") = -1,
         py::arg("row_base") = 0);
-  m.def("plan", &plan, "launch plan (splits, chunks, threads, capacity, maxima/thread, lanes/max, smem)");
+  m.def("plan", &plan,
+        "launch plan (splits, chunks, threads, capacity, maxima/thread, lanes/max, smem, path, workspace)");
   m.attr("NUM_PHASES") = FS_NUM_PHASES;
 }

@@ -108,3 +108,40 @@ def test_invalid_arguments_are_rejected_before_any_launch():
     assert lib.fs_sample(None, None) == abi.FS_EINVAL
     assert lib.fs_probe_noop(None, 4, None) == abi.FS_EINVAL
     assert lib.fs_merge_sample(ctypes.byref(a), None, 2, None) == abi.FS_EINVAL
+
+
+def test_large_batches_plan_the_streaming_path_with_a_workspace():
+    big = abi.plan(1024, 151936, 50)
+    assert big.path == abi.FS_PATH_STREAM
+    # [B, S, M] packed candidates + [B, S] counts + alignment slack
+    assert big.workspace_bytes >= 1024 * big.splits * (2 * 50 * 8 + 4)
+    assert abi.plan(1, 151936, 50).path == abi.FS_PATH_CLUSTER
+    assert abi.plan(1, 151936, 50).workspace_bytes == 0
+    # beyond the streaming slots the cluster path serves every batch size
+    assert abi.plan(1024, 151936, 1024).path == abi.FS_PATH_CLUSTER
+
+
+def test_workspace_size_follows_the_plan_and_the_path_override():
+    lib = abi.lib()
+    a = abi.FsSampleArgs()
+    a.dtype, a.batch, a.vocab, a.row_stride, a.top_k, a.top_p = abi.FS_BF16, 1024, 151936, 151936, 50, 0.9
+    assert lib.fs_workspace_size(ctypes.byref(a)) == abi.plan(1024, 151936, 50).workspace_bytes
+    a.path = abi.FS_PATH_CLUSTER
+    assert lib.fs_workspace_size(ctypes.byref(a)) == 0
+    a.path, a.batch = abi.FS_PATH_STREAM, 1
+    assert lib.fs_workspace_size(ctypes.byref(a)) > 0
+    assert lib.fs_workspace_size(None) == 0
+
+
+def test_the_streaming_path_without_its_workspace_is_rejected_before_any_launch():
+    lib = abi.lib()
+    a = abi.FsSampleArgs()
+    a.dtype, a.batch, a.vocab, a.row_stride, a.top_k, a.top_p = abi.FS_BF16, 1024, 151936, 151936, 50, 0.9
+    a.logits = 0x1000
+    a.out_ids = 0x2000
+    assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EWORKSPACE
+    assert "workspace" in lib.fs_last_error().decode()
+    a.workspace, a.workspace_bytes = 0x3000, 64
+    assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EWORKSPACE
+    a.path, a.top_k = abi.FS_PATH_STREAM, 1024
+    assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EUNSUPPORTED
