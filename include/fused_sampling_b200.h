@@ -114,6 +114,16 @@ FS_API uint64_t fs_workspace_size(const fs_sample_args* args);
  * and the pybind entries sample_fused, stages_fused (csrc/bindings.cpp:20,22). */
 FS_API fs_status fs_sample(const fs_sample_args* args, fs_stream_t stream);
 
+/* fs_sample without a caller workspace (no counterpart in the reference). For callers that
+ * cannot allocate device memory at call time. The streaming path's scratch is one static device
+ * array of FS_STATIC_SCRATCH_BYTES per device; a call that needs more returns FS_EWORKSPACE.
+ * args->workspace is ignored. The first call on a device looks the array up
+ * (cudaGetSymbolAddress): make it before any stream capture. Nothing is allocated, freed or
+ * zeroed per call. Calls that overlap in time (other streams, other host threads) share the array
+ * and race: serialise them. */
+#define FS_STATIC_SCRATCH_BYTES (16ull << 20)
+FS_API fs_status fs_sample_noalloc(const fs_sample_args* args, fs_stream_t stream);
+
 /* Top-K candidate ids only ([B, K] into args->topk_ids; out_ids may be NULL).
  * Replaces: topk_fused (csrc/fused_sampling.cu:460-473, csrc/bindings.cpp:21). */
 FS_API fs_status fs_topk(const fs_sample_args* args, fs_stream_t stream);

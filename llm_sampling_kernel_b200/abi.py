@@ -39,6 +39,7 @@ EXPORTED = (
     "fs_plan",
     "fs_version",
     "fs_workspace_size",
+    "fs_sample_noalloc",
 )
 FS_PATH_AUTO, FS_PATH_CLUSTER, FS_PATH_STREAM = 0, 1, 2
 
@@ -132,7 +133,8 @@ def lib() -> ctypes.CDLL:
         L.fs_plan.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, P(FsPlanInfo)]
         L.fs_workspace_size.argtypes = [P(FsSampleArgs)]
         L.fs_workspace_size.restype = ctypes.c_uint64
-        for name in ("fs_sample", "fs_topk", "fs_probe_phase", "fs_shard_candidates", "fs_merge_sample",
+        L.fs_sample_noalloc.argtypes = [P(FsSampleArgs), ctypes.c_void_p]
+        for name in ("fs_sample", "fs_sample_noalloc", "fs_topk", "fs_probe_phase", "fs_shard_candidates", "fs_merge_sample",
                      "fs_probe_noop", "fs_probe_scan_rowblock", "fs_probe_scan_split", "fs_plan"):
             getattr(L, name).restype = ctypes.c_int
         _lib = L
