@@ -1338,6 +1338,7 @@ static int pow2_floor(int64_t x) {
 constexpr int kMaxCap = 8192;
 constexpr int64_t kStreamMaxK = 256;     // streaming path: top-K bound
 constexpr int64_t kStreamMinBatch = 128;  // AUTO: rows from which the streaming path is used
+constexpr int64_t kStreamAutoMaxK = 128;  // AUTO: largest k for which it is used
 
 // Plan of one call: cluster size, chunks per thread, survivor capacity, maxima granularity.
 fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t path, PlanOut* out) {
@@ -1417,7 +1418,8 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t pat
   }
   // (the slice launch puts rows on grid.y, at most 65535)
   const bool stream_fits = K <= kStreamMaxK && static_cast<int64_t>(Ss) * M <= kMaxMaxima && Cs > 0 && B <= 65535;
-  const bool want_stream = path == FS_PATH_STREAM || (path == FS_PATH_AUTO && B >= kStreamMinBatch);
+  const bool want_stream =
+      path == FS_PATH_STREAM || (path == FS_PATH_AUTO && B >= kStreamMinBatch && K <= kStreamAutoMaxK);
   if (path == FS_PATH_STREAM && !stream_fits) {
     set_error("the streaming path supports top_k <= %lld with splits * slots <= %d and batch <= 65535",
               static_cast<long long>(kStreamMaxK), kMaxMaxima);

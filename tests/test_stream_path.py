@@ -3,7 +3,8 @@
 The streaming path must give exactly what the cluster path gives: the same top-k set and order
 (checked against the oracle), and, because both end in the same row tail over the same
 candidates, the same ids, keep mask, renormed probabilities and row status, bit for bit.
-`path=2` forces it at any batch; batches of 128 rows and more take it by default when k <= 256.
+`path=2` forces it at any batch (k <= 256); batches of 128 rows and more take it by default when
+k <= 128.
 """
 
 import numpy as np
