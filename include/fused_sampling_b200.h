@@ -52,7 +52,8 @@ enum {
   FS_ROW_NAN = 1,         /* "logits contain NaN"                          */
   FS_ROW_POSINF = 2,      /* "logits contain +inf"                         */
   FS_ROW_ALL_NEGINF = 3,  /* "logits contain a row that is entirely -inf"  */
-  FS_ROW_BAD_PARAM = 4    /* per-row k < 1, or per-row p outside (0, 1]     */
+  FS_ROW_BAD_PARAM = 4,   /* per-row k < 1, or per-row p outside (0, 1]     */
+  FS_ROW_TIMEOUT = 5      /* a bounded device wait of the launch ran out: no result for the row */
 };
 
 /* Source of the per-row uniform u in [0, 1), in priority order:
@@ -91,16 +92,18 @@ typedef struct fs_sample_args {
   int32_t* row_status;       /* optional device [B]: FS_ROW_*                            */
   int32_t splits;            /* 0 = auto; else CTAs per row (1..16, rounded up to 2^n)    */
   int32_t stop_phase;        /* 0 = full pipeline; 1..FS_NUM_PHASES ablation stop point  */
-  int32_t path;              /* FS_PATH_AUTO / FS_PATH_CLUSTER / FS_PATH_STREAM          */
+  int32_t path;              /* FS_PATH_* (AUTO = 0 picks)                               */
   void* workspace;           /* device scratch for the streaming path (see below)        */
   uint64_t workspace_bytes;  /* its size; >= fs_workspace_size(args)                     */
 } fs_sample_args;
 
 /* Execution paths. CLUSTER: one launch, one thread-block cluster per row, no workspace (the
  * latency path). STREAM: two launches - independent CTAs per row slice write candidate lists to
- * the workspace, one CTA per row merges them (the throughput path for large batches). AUTO
- * picks by batch size and k. Both compute the same result. */
-enum { FS_PATH_AUTO = 0, FS_PATH_CLUSTER = 1, FS_PATH_STREAM = 2 };
+ * the workspace, one CTA per row merges them. PERSIST: one launch, one CTA per SM streaming
+ * whole rows through a ring of shared-memory stages filled by bulk copies, no workspace (the
+ * throughput path for large batches; needs 16-byte aligned rows and V % 8 == 0, otherwise AUTO
+ * falls back to CLUSTER). AUTO picks by batch size and k. All compute the same result. */
+enum { FS_PATH_AUTO = 0, FS_PATH_CLUSTER = 1, FS_PATH_STREAM = 2, FS_PATH_PERSIST = 3 };
 
 #define FS_NUM_PHASES 7
 
@@ -191,8 +194,8 @@ typedef struct fs_plan_info {
   int32_t maxima_per_thread;
   int32_t lanes_per_max;
   int32_t smem_bytes;
-  int32_t path;              /* FS_PATH_CLUSTER or FS_PATH_STREAM */
-  uint64_t workspace_bytes;  /* 0 for the cluster path */
+  int32_t path;              /* FS_PATH_CLUSTER, FS_PATH_STREAM or FS_PATH_PERSIST */
+  uint64_t workspace_bytes;  /* 0 unless the path is FS_PATH_STREAM */
 } fs_plan_info;
 FS_API fs_status fs_plan(int64_t batch, int64_t vocab, int64_t top_k, int32_t splits, fs_plan_info* out);
 

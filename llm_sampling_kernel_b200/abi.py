@@ -41,7 +41,7 @@ EXPORTED = (
     "fs_workspace_size",
     "fs_sample_noalloc",
 )
-FS_PATH_AUTO, FS_PATH_CLUSTER, FS_PATH_STREAM = 0, 1, 2
+FS_PATH_AUTO, FS_PATH_CLUSTER, FS_PATH_STREAM, FS_PATH_PERSIST = 0, 1, 2, 3
 
 
 class FsRng(ctypes.Structure):

@@ -24,6 +24,9 @@ struct PlanOut {
   int merge_cap; // streaming: gathered-candidate capacity of the row merge (power of two)
   int merge_smem;
   uint64_t workspace;  // streaming: workspace bytes
+  int persist;   // 1: persistent row-streaming kernel (one CTA per SM)
+  int ring;      // persistent: shared-memory stages
+  int nst;       // persistent: stages per row
 };
 
 // printf-style message for fs_last_error() on this host thread.

@@ -77,6 +77,9 @@ struct Params {
   int32_t vec;         // 16-byte vector loads allowed
   int32_t stop;        // 0 = full pipeline, else ablation phase
   int32_t mode;        // kModeSample / kModeTopk / kModeShard
+  int32_t batch;       // rows (the persistent kernel walks them)
+  int32_t ring;        // persistent kernel: shared-memory stages in the ring
+  int32_t nst;         // persistent kernel: stages per row
 };
 
 constexpr int kModeSample = 0;
@@ -94,6 +97,7 @@ constexpr int kCtlScr0 = 5;     // two words of block-search results
 constexpr int kCtlHb = 8;       // fallback scratch
 constexpr int kCtlAbove = 9;
 constexpr int kCtlT = 10;
+constexpr int kCtlTmo = 12;     // persistent kernel: some thread's wait ran out
 constexpr int kCtlNgt = 11;
 
 constexpr uint32_t kFlagNaN = 1u, kFlagPosInf = 2u, kFlagAboveNegInf = 4u;
@@ -272,14 +276,14 @@ __device__ __forceinline__ float row_uniform(const Params& p, int b) {
 }
 
 
-// Writes the outputs of a row that cannot be sampled (bad input or parameters).
-__device__ void write_invalid_row(const Params& p, int b, int st) {
-  const int t = threadIdx.x;
+// Writes the outputs of a row that cannot be sampled (bad input or parameters). Called by
+// `stride` threads numbered t = 0 .. stride-1 (the CTA, or one warp with t = lane).
+__device__ void write_invalid_row(const Params& p, int b, int st, int t, int stride) {
   if (t == 0) {
     if (p.out != nullptr) p.out[b] = -1;
     if (p.status != nullptr) p.status[b] = st;
   }
-  for (int i = t; i < p.K; i += blockDim.x) {
+  for (int i = t; i < p.K; i += stride) {
     const size_t o = static_cast<size_t>(b) * p.K + i;
     if (p.topk_ids != nullptr) p.topk_ids[o] = -1;
     if (p.keep != nullptr) p.keep[o] = 0;
@@ -287,15 +291,18 @@ __device__ void write_invalid_row(const Params& p, int b, int st) {
   }
   if (p.cand_out != nullptr) {
     uint64_t* co = p.cand_out + static_cast<size_t>(b) * (p.K + 1);
-    for (int i = t; i < p.K; i += blockDim.x) co[i] = 0ull;
+    for (int i = t; i < p.K; i += stride) co[i] = 0ull;
     if (t == 0) co[p.K] = static_cast<uint64_t>(st);
   }
 }
 
+__device__ __forceinline__ void write_invalid_row(const Params& p, int b, int st) {
+  write_invalid_row(p, b, st, static_cast<int>(threadIdx.x), static_cast<int>(blockDim.x));
+}
+
 // Writes the top-K ids or the shard candidates of a sorted candidate list (shared memory).
-// Returns true when the mode ends here. Called by `nthreads` threads starting at thread 0.
-__device__ bool write_selection(const Params& p, int b, const uint64_t* cand, int kk, int nthreads) {
-  const int t = threadIdx.x;
+// Returns true when the mode ends here. Called by `nthreads` threads numbered t = 0 .. nthreads-1.
+__device__ bool write_selection(const Params& p, int b, const uint64_t* cand, int kk, int t, int nthreads) {
   if (p.mode == kModeTopk) {
     for (int i = t; i < p.K; i += nthreads)
       p.topk_ids[static_cast<size_t>(b) * p.K + i] = i < kk ? static_cast<int64_t>(packed_id(cand[i])) : -1;
@@ -314,8 +321,8 @@ __device__ bool write_selection(const Params& p, int b, const uint64_t* cand, in
 // Stage outputs (top-K ids, keep, renormed) from the sorted candidates and the per-rank
 // probabilities / cumulative sums held in shared memory.
 __device__ void write_stages(const Params& p, int b, const uint64_t* cand, const float* prob, int kk, int r,
-                             float zp, int nthreads) {
-  for (int i = threadIdx.x; i < p.K; i += nthreads) {
+                             float zp, int t, int nthreads) {
+  for (int i = t; i < p.K; i += nthreads) {
     const size_t o = static_cast<size_t>(b) * p.K + i;
     if (p.topk_ids != nullptr) p.topk_ids[o] = i < kk ? static_cast<int64_t>(packed_id(cand[i])) : -1;
     if (p.keep != nullptr) p.keep[o] = (i <= r) ? 1 : 0;
@@ -375,7 +382,7 @@ __device__ void sample_tail_block(const Params& p, int b, const uint64_t* cand, 
     if (p.out != nullptr) p.out[b] = static_cast<int64_t>(packed_id(cand[pick]));
     if (p.status != nullptr) p.status[b] = FS_ROW_OK;
   }
-  write_stages(p, b, cand, prob, kk, r, zp, NT);
+  write_stages(p, b, cand, prob, kk, r, zp, t, NT);
 }
 
 
@@ -451,7 +458,7 @@ __device__ void sample_tail_warp(const Params& p, int b, const uint64_t* cand, i
     for (int r = 0; r < R; ++r)
       if (lane * R + r < kk) prob[lane * R + r] = pr[r];
     __syncwarp();
-    write_stages(p, b, cand, prob, kk, rc, zp, 32);
+    write_stages(p, b, cand, prob, kk, rc, zp, lane, 32);
   }
 }
 
@@ -498,7 +505,7 @@ __device__ void finish_row(const Params& p, int b, uint64_t* src, int n, uint64_
     if (t == 0) p.out[b] = static_cast<int64_t>(packed_id(dst[0]));
     return;
   }
-  if (write_selection(p, b, dst, kk, NT)) return;
+  if (write_selection(p, b, dst, kk, t, NT)) return;
   if (kk <= 256) {
     if (t < 32) {
       if (kk <= 32) sample_tail_warp<DT, 1>(p, b, dst, kk, pp, u, prob);
@@ -948,15 +955,16 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
 
 constexpr uint32_t kCountMask = 0xFFFFFFu;
 
-// Exact top-kk of this CTA's slice alone (heavy ties), written to slots[0..) in global memory:
-// two 8-bit radix levels over the slice (re-read from L1/L2) give the kk-th key T; the elements
-// above T and the lowest-id ties at T (ranked in id order: chunk, thread, lane) are written.
-// Returns min(kk, valid elements). Every thread of the CTA calls it.
-template <int DT, int C>
-__device__ __noinline__ int slice_exact_topk(Shared& sh, const uint16_t* __restrict__ row, int V, int vec,
-                                             uint32_t id_base, int vbase, int kk, uint64_t* slots) {
+// Exact top-kk of the span of `nchunks` CTA chunks starting at vector vbase (heavy ties), written
+// to slots[0..) (global or shared memory): two 8-bit radix levels over the span (re-read from
+// L1/L2) give the kk-th key T; the elements above T and the lowest-id ties at T (ranked in id
+// order: chunk, thread, lane) are written. Returns min(kk, valid elements). Every thread of the
+// CTA calls it.
+template <int DT>
+__device__ __noinline__ int span_exact_topk(Shared& sh, const uint16_t* __restrict__ row, int V, int vec,
+                                            uint32_t id_base, int vbase, int nchunks, int kk, uint64_t* slots) {
   const int t = threadIdx.x;
-  const int valid = max(0, min(V - vbase * 8, C * NT * 8));
+  const int valid = max(0, min(V - vbase * 8, nchunks * NT * 8));
   const int want = min(kk, valid);
   if (want == 0) return 0;
   sh.h1[t] = 0u;
@@ -964,7 +972,7 @@ __device__ __noinline__ int slice_exact_topk(Shared& sh, const uint16_t* __restr
   if (t == 0) sh.ctl[kCtlLocal] = 0u;
   __syncthreads();
 #pragma unroll 1
-  for (int c = 0; c < C; ++c) {
+  for (int c = 0; c < nchunks; ++c) {
     const int e0 = (vbase + c * NT + t) * 8;
     const uint4 v = load_chunk<DT>(row, e0, V, vec);
 #pragma unroll
@@ -987,7 +995,7 @@ __device__ __noinline__ int slice_exact_topk(Shared& sh, const uint16_t* __restr
   const uint32_t hb = sh.ctl[kCtlHb];
   const uint32_t n_above = sh.ctl[kCtlAbove];
 #pragma unroll 1
-  for (int c = 0; c < C; ++c) {
+  for (int c = 0; c < nchunks; ++c) {
     const int e0 = (vbase + c * NT + t) * 8;
     const uint4 v = load_chunk<DT>(row, e0, V, vec);
 #pragma unroll
@@ -1013,7 +1021,7 @@ __device__ __noinline__ int slice_exact_topk(Shared& sh, const uint16_t* __restr
   const uint32_t need = static_cast<uint32_t>(want) - n_gt;
   uint32_t chunk_base = 0u;
 #pragma unroll 1
-  for (int c = 0; c < C; ++c) {
+  for (int c = 0; c < nchunks; ++c) {
     const int e0 = (vbase + c * NT + t) * 8;
     const uint4 v = load_chunk<DT>(row, e0, V, vec);
     uint32_t mask = 0u;
@@ -1133,124 +1141,589 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_slice_kernel(const Par
   const uint32_t lbits = key_to_bits(lkey);
   const uint32_t l2 = lbits | (lbits << 16);
 
-  constexpr int MW = (C * 8 + 31) / 32;
-  uint32_t mask[MW];
-#pragma unroll
-  for (int i = 0; i < MW; ++i) mask[i] = 0u;
-#pragma unroll
-  for (int c = 0; c < C; ++c) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t m = pair_ge_mask<DT>(word_of(v[c], q), l2);
-      const uint32_t bits2 = (m & 1u) | ((m >> 15) & 2u);
-      const int bit = 8 * c + 2 * q;
-      mask[bit >> 5] |= bits2 << (bit & 31);
-    }
-  }
-  if (!full) {  // elements past the end of the row read as -inf: never candidates
-#pragma unroll
-    for (int c = 0; c < C; ++c) {
-      const int e0 = (vbase + c * NT + t) * 8;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int bit = 8 * c + j;
-        if (e0 + j >= V) mask[bit >> 5] &= ~(1u << (bit & 31));
-      }
-    }
-  }
-  uint32_t mine = 0u;
-#pragma unroll
-  for (int i = 0; i < MW; ++i) mine += __popc(mask[i]);
-  const uint32_t total = block_sum<uint32_t, NT>(mine, sh.uscr);
+  // Filter, warp-cooperative: a lane whose maximum reaches L marks its chunks that hold an
+  // element >= L; the warp lists the marked (lane, chunk) pairs, hands one pair to each lane,
+  // which re-reads that chunk (an L1 hit) and appends its hits with one shared atomic per warp.
   uint64_t* slots = cand + (static_cast<size_t>(b) * S + s) * M;
-  uint32_t written;
-  if (total <= M) {
-    written = total;
+  const uint32_t pmax = pair_max_nan<DT>(pair_max_nan<DT>(mx[0], mx[2]), pair_max_nan<DT>(mx[1], mx[3]));
+  const uint32_t tmax = half_max_nan<DT>(pmax & 0xFFFFu, pmax >> 16);
+  const bool hot = !Fmt<DT>::is_nan(tmax) && order_key(tmax) >= lkey;
+  if (__ballot_sync(0xFFFFFFFFu, hot) != 0u) {
+    const int lane = t & 31;
+    uint32_t cm = 0u;
+    if (hot) {
 #pragma unroll
-    for (int i = 0; i < MW; ++i) {
-      uint32_t w = mask[i];
-      while (w != 0u) {
-        const int bit = 32 * i + __ffs(w) - 1;
-        w &= w - 1;
-        const int c = bit >> 3, j = bit & 7;
-        const int e = (vbase + c * NT + t) * 8 + j;
-        slots[atomicAdd(&sh.ctl[kCtlLocal], 1u)] = pack(order_key(row[e]), p.id_base + e);
+      for (int c = 0; c < C; ++c) {
+        const uint32_t any = pair_ge_mask<DT>(v[c].x, l2) | pair_ge_mask<DT>(v[c].y, l2) |
+                             pair_ge_mask<DT>(v[c].z, l2) | pair_ge_mask<DT>(v[c].w, l2);
+        cm |= (any != 0u ? 1u : 0u) << c;
       }
     }
-  } else {
-    written = static_cast<uint32_t>(slice_exact_topk<DT, C>(sh, row, V, p.vec, p.id_base, vbase, kk, slots));
+    const int np = __popc(cm);
+    const int pincl = warp_incl_scan(np);
+    const int npairs = __shfl_sync(0xFFFFFFFFu, pincl, 31);
+    uint16_t* wp = reinterpret_cast<uint16_t*>(g_smem + sizeof(Shared)) + (t >> 5) * (32 * C);
+    int k = pincl - np;
+    while (cm != 0u) {
+      const int c = __ffs(cm) - 1;
+      cm &= cm - 1u;
+      wp[k++] = static_cast<uint16_t>((lane << 4) | c);
+    }
+    __syncwarp();
+    for (int base = 0; base < npairs; base += 32) {
+      const int pi = base + lane;
+      uint32_t hits = 0u;  // bit 2w + h: half h of word w of the chunk is >= L
+      uint4 x = make_uint4(0u, 0u, 0u, 0u);
+      int e0 = 0;
+      if (pi < npairs) {
+        const int pr = wp[pi];
+        const int owner = (t & ~31) + (pr >> 4);
+        e0 = (vbase + (pr & 15) * NT + owner) * 8;
+        x = load_chunk<DT>(row, e0, V, p.vec);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const uint32_t m = pair_ge_mask<DT>(word_of(x, w), l2);
+          hits |= ((m & 1u) | ((m >> 15) & 2u)) << (2 * w);
+        }
+        if (e0 + 8 > V) hits &= (e0 < V) ? ((1u << (V - e0)) - 1u) : 0u;  // past the row end
+      }
+      const int nh = __popc(hits);
+      const int hincl = warp_incl_scan(nh);
+      const int htot = __shfl_sync(0xFFFFFFFFu, hincl, 31);
+      uint32_t hbase = 0u;
+      if (lane == 31 && htot > 0) hbase = atomicAdd(&sh.ctl[kCtlLocal], static_cast<uint32_t>(htot));
+      hbase = __shfl_sync(0xFFFFFFFFu, hbase, 31);
+      uint32_t j = hbase + static_cast<uint32_t>(hincl - nh);
+      while (hits != 0u) {
+        const int bit = __ffs(hits) - 1;
+        hits &= hits - 1u;
+        const int w = bit >> 1;
+        const uint32_t word = w == 0 ? x.x : w == 1 ? x.y : w == 2 ? x.z : x.w;
+        if (j < M) slots[j] = pack(order_key((word >> (16 * (bit & 1))) & 0xFFFFu), p.id_base + e0 + bit);
+        ++j;
+      }
+    }
+  }
+  __syncthreads();
+  const uint32_t total = sh.ctl[kCtlLocal];
+  uint32_t written = total;
+  if (total > M) {
+    __syncthreads();  // every thread has read the count before the fallback resets it
+    written = static_cast<uint32_t>(span_exact_topk<DT>(sh, row, V, p.vec, p.id_base, vbase, C, kk, slots));
   }
   if (t == 0) cnt[static_cast<size_t>(b) * S + s] = written | (sh.ctl[kCtlFlags] << 24);
 }
 
+// Row merge, one warp per row (blockDim.x / 32 rows per CTA, no block barrier). Per-warp shared
+// memory: a 256-bin histogram, the slice counts and offsets, the row's gathered candidates, the
+// sorted top kk and the probabilities of the tail.
+constexpr int kMergeWarps = NT / 32;
+
+__host__ __device__ constexpr size_t merge_warp_bytes(int capn, int K) {
+  return (1024 + 128 + static_cast<size_t>(capn) * 8 + static_cast<size_t>(K) * 8 + static_cast<size_t>(K) * 4 +
+          15) & ~static_cast<size_t>(15);
+}
+
+// Warps per row-merge CTA that fit the shared memory budget.
+__host__ __device__ constexpr int merge_warps(int capn, int K) {
+  return static_cast<int>(std::min<size_t>(kMergeWarps, (200u * 1024u) / merge_warp_bytes(capn, K)));
+}
+
+// The need-th largest low word (0xFFFFFFFF - id: the need-th smallest id) among the n gathered
+// candidates whose key is E: four 8-bit radix levels (one warp).
+__device__ __noinline__ uint32_t warp_tie_cut(const uint64_t* g, uint32_t n, uint32_t E, uint32_t need,
+                                              uint32_t* hist) {
+  const int lane = threadIdx.x & 31;
+  uint32_t prefix = 0u;
+  for (int level = 3; level >= 0; --level) {
+    const int sh = 8 * level;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0u;
+    __syncwarp();
+    for (uint32_t d = lane; d < n; d += 32) {
+      const uint64_t x = g[d];
+      const uint32_t lo = static_cast<uint32_t>(x);
+      const bool match = packed_key(x) == E && (level == 3 || (lo >> (sh + 8)) == (prefix >> (sh + 8)));
+      if (match) atomicAdd(&hist[(lo >> sh) & 0xFFu], 1u);
+    }
+    __syncwarp();
+    uint32_t bin = 0u, above = 0u;
+    warp_boundary_256(hist, need, &bin, &above);
+    prefix |= bin << sh;
+    need -= above;
+    __syncwarp();
+  }
+  return prefix;
+}
+
 template <int DT>
 __global__ void __launch_bounds__(NT) fs_rowmerge_kernel(const Params p, const uint64_t* __restrict__ cand,
-                                                         const uint32_t* __restrict__ cnt, int S) {
-  const int b = blockIdx.x;
-  const int t = threadIdx.x;
+                                                         const uint32_t* __restrict__ cnt, int S, int B) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int b = blockIdx.x * static_cast<int>(blockDim.x >> 5) + warp;
+  if (b >= B) return;  // whole warp
   const uint32_t M = static_cast<uint32_t>(p.slot);
-  Shared& sh = *reinterpret_cast<Shared*>(g_smem);
-  uint64_t* gath = reinterpret_cast<uint64_t*>(g_smem + sizeof(Shared));  // cap words
-  uint64_t* sel = gath + p.cap;                                             // cap words
-  float* prob = reinterpret_cast<float*>(sel + p.cap);
-  float* cum = prob + p.cap;
+  const int capn = p.cap;
+  unsigned char* base = g_smem + merge_warp_bytes(capn, p.K) * warp;
+  uint32_t* hist = reinterpret_cast<uint32_t*>(base);
+  uint32_t* offs_cnt = hist + 256;  // [0, 16): counts; [16, 32): exclusive offsets
+  uint64_t* g = reinterpret_cast<uint64_t*>(offs_cnt + 32);
+  uint64_t* dst = g + capn;
+  float* prob = reinterpret_cast<float*>(dst + p.K);
 
   int kk;
   float pp;
   bool bad;
   row_params(p, b, &kk, &pp, &bad);
-  const float u = t < 32 ? row_uniform(p, b) : 0.0f;
-  sh.h1[t] = 0u;
-  if (t < 16) sh.ctl[t] = 0u;
-  if (t < 32) {
-    const uint32_t w = t < S ? __ldcg(cnt + static_cast<size_t>(b) * S + t) : 0u;
-    const uint32_t c = w & kCountMask;
-    const uint32_t inc = warp_incl_scan(c);
-    const uint32_t f = __reduce_or_sync(0xFFFFFFFFu, w >> 24);
-    if (t < S) {
-      sh.cnt[t] = c;
-      sh.cnt2[t] = inc - c;
-    }
-    if (t == 31) sh.ctl[kCtlN] = inc;
-    if (t == 0) {
-      int st = FS_ROW_OK;
-      if (bad) st = FS_ROW_BAD_PARAM;
-      else if (f & kFlagNaN) st = FS_ROW_NAN;
-      else if (f & kFlagPosInf) st = FS_ROW_POSINF;
-      else if (!(f & kFlagAboveNegInf)) st = FS_ROW_ALL_NEGINF;
-      sh.ctl[kCtlStatus] = static_cast<uint32_t>(st);
-    }
-  }
-  __syncthreads();
-  const int st = static_cast<int>(sh.ctl[kCtlStatus]);
+  const float u = row_uniform(p, b);
+  const uint32_t w = lane < S ? __ldcg(cnt + static_cast<size_t>(b) * S + lane) : 0u;
+  const uint32_t c = w & kCountMask;
+  const uint32_t inc = warp_incl_scan(c);
+  const uint32_t f = __reduce_or_sync(0xFFFFFFFFu, w >> 24);
+  const uint32_t n = __shfl_sync(0xFFFFFFFFu, inc, 31);
+  int st = FS_ROW_OK;
+  if (bad) st = FS_ROW_BAD_PARAM;
+  else if (f & kFlagNaN) st = FS_ROW_NAN;
+  else if (f & kFlagPosInf) st = FS_ROW_POSINF;
+  else if (!(f & kFlagAboveNegInf)) st = FS_ROW_ALL_NEGINF;
   if (st != FS_ROW_OK) {
-    write_invalid_row(p, b, st);
+    write_invalid_row(p, b, st, lane, 32);
     return;
   }
-  const int n = static_cast<int>(sh.ctl[kCtlN]);
-  // gather: rank r's slots [0, cnt[r]) to [prefix[r], ...), keys alongside
-  {
-    const uint64_t* rowc = cand + static_cast<size_t>(b) * S * M;
-    const int mshift = __ffs(static_cast<int>(M)) - 1;
-    for (int i = t; i < S * static_cast<int>(M); i += NT) {
-      const int r = i >> mshift;
-      const int j = i & (static_cast<int>(M) - 1);
-      if (j < static_cast<int>(sh.cnt[r])) {
-        const uint64_t x = __ldcg(rowc + i);
-        const int d = static_cast<int>(sh.cnt2[r]) + j;
-        gath[d] = x;
-        sh.mkeys[d] = packed_key(x);
-      }
+  if (lane < 16) {
+    offs_cnt[lane] = c;
+    offs_cnt[16 + lane] = inc - c;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0u;
+  __syncwarp();
+  // gather every slot in use (independent L2 loads) and the high-byte histogram of the keys
+  const uint64_t* rowc = cand + static_cast<size_t>(b) * S * M;
+  const int mshift = __ffs(static_cast<int>(M)) - 1;
+  const uint32_t slots = static_cast<uint32_t>(S) * M;
+#pragma unroll 4
+  for (uint32_t i = lane; i < slots; i += 32) {
+    const uint32_t r = i >> mshift, j = i & (M - 1u);
+    if (j < offs_cnt[r]) {
+      const uint64_t x = __ldcg(rowc + i);
+      g[offs_cnt[16 + r] + j] = x;
+      atomicAdd(&hist[packed_key(x) >> 8], 1u);
     }
   }
-  __syncthreads();
-  constexpr int kSh = DT ? 0 : 2;
-  const uint32_t E = anchored_threshold(sh.mkeys, n, kk, kSh, sh.h1, sh.uscr);
-  for (int i = t; i < n; i += NT) {
-    if (sh.mkeys[i] >= E) sel[atomicAdd(&sh.ctl[kCtlLocal], 1u)] = gath[i];
+  __syncwarp();
+  uint32_t hb = 0u, above = 0u;
+  warp_boundary_256(hist, static_cast<uint32_t>(kk), &hb, &above);
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0u;
+  __syncwarp();
+  // low byte inside the boundary bin
+  for (uint32_t d = lane; d < n; d += 32) {
+    const uint32_t key = packed_key(g[d]);
+    if ((key >> 8) == hb) atomicAdd(&hist[key & 0xFFu], 1u);
   }
+  __syncwarp();
+  uint32_t lb = 0u, above2 = 0u;
+  warp_boundary_256(hist, static_cast<uint32_t>(kk) - above, &lb, &above2);
+  const uint32_t E = (hb << 8) | lb;
+  const uint32_t need = static_cast<uint32_t>(kk) - (above + above2);  // ties to take at E
+  const uint32_t eq = hist[lb];
+  // more than 32 surplus ties at E: keep only the `need` lowest ids among them
+  const bool cut = eq > need + 32u;
+  const uint32_t tcut = cut ? warp_tie_cut(g, n, E, need, hist) : 0u;
+  // compact in place (a kept candidate never moves up): keys above E and the kept ties
+  uint32_t nsel = 0u;
+  for (uint32_t d0 = 0; d0 < n; d0 += 32) {
+    const uint32_t d = d0 + lane;
+    const uint64_t x = d < n ? g[d] : 0ull;
+    const uint32_t key = packed_key(x);
+    const bool take = d < n && (key > E || (key == E && (!cut || static_cast<uint32_t>(x) >= tcut)));
+    const unsigned ball = __ballot_sync(0xFFFFFFFFu, take);
+    if (take) g[nsel + __popc(ball & ((1u << lane) - 1u))] = x;
+    nsel += __popc(ball);
+  }
+  __syncwarp();
+  // rank sort (packed values are distinct; nsel <= kk + 32): the top kk in order
+  for (uint32_t i = lane; i < nsel; i += 32) {
+    const uint64_t x = g[i];
+    uint32_t rank = 0u;
+    for (uint32_t j = 0; j < nsel; ++j) rank += g[j] > x ? 1u : 0u;
+    if (rank < static_cast<uint32_t>(kk)) dst[rank] = x;
+  }
+  __syncwarp();
+  if (write_selection(p, b, dst, kk, lane, 32)) return;
+  if (kk <= 32) sample_tail_warp<DT, 1>(p, b, dst, kk, pp, u, prob);
+  else if (kk <= 64) sample_tail_warp<DT, 2>(p, b, dst, kk, pp, u, prob);
+  else sample_tail_warp<DT, 8>(p, b, dst, kk, pp, u, prob);
+}
+
+// ------------------------------------------------------------------------------------------
+// Persistent row-streaming path for large batches: one launch, one CTA per SM, no workspace.
+// CTA c takes rows c, c + G, c + 2G, ... (G = grid size) and streams each row through a ring of
+// `ring` shared-memory stages of kStageBytes. Thread 0 fills the stages with bulk copies
+// (cp.async.bulk, completion counted on one mbarrier per stage) up to `ring` stages ahead, across
+// row boundaries, so HBM keeps streaming while a stage is filtered and while a finished row is
+// sampled. Per row:
+//   stage 0: L = the kk-th largest of the stage's sub-chunk maxima (at least kk elements >= L);
+//   every stage: a thread whose maximum is >= L appends its elements >= L to the candidate
+//     buffer (shared memory); when the buffer passes half its capacity it is cut down to the
+//     elements >= its exact kk-th largest key, which also raises L;
+//   end: the exact kk-th key E of the candidates, the candidates >= E, and the common row tail.
+// L never exceeds the kk-th largest logit of the part of the row seen so far, so the candidates
+// always hold the row's top-kk. A row whose candidates overflow the buffer (heavy ties) is
+// re-read from L2/HBM by the exact radix select.
+// ------------------------------------------------------------------------------------------
+
+constexpr int kStageChunks = 8;                     // 16-byte vectors per thread per stage
+constexpr int kStageElems = kStageChunks * NT * 8;  // 16384 logits
+constexpr int kStageBytes = kStageElems * 2;        // 32 KiB
+constexpr int kMaxRing = 6;
+constexpr int kRingOffset = 128;                    // mbarriers, then the stages (128-byte aligned)
+constexpr long long kWaitLimit = 1LL << 22;         // try_wait polls before a stage wait gives up
+
+__device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+// One poll of the phase with the given parity; true once it has completed.
+__device__ __forceinline__ bool mbar_done(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0u;
+}
+
+// Bounded wait for a stage; false if it did not complete within kWaitLimit polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (long long i = 0; i < kWaitLimit; ++i) {
+    if (mbar_done(bar, parity)) return true;
+  }
+  return false;
+}
+
+// Orders this CTA's earlier generic-proxy accesses of shared memory before later bulk copies.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
+// Global -> shared bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned),
+// completion signalled on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+template <int DT>
+__global__ void __launch_bounds__(NT, 1) fs_rowstream_kernel(const Params p) {
+  Shared& sh = *reinterpret_cast<Shared*>(g_smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(g_smem + sizeof(Shared));
+  uint4* ring = reinterpret_cast<uint4*>(g_smem + sizeof(Shared) + kRingOffset);
+  uint64_t* cand = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(ring) +
+                                               static_cast<size_t>(p.ring) * kStageBytes);
+  uint64_t* spare = cand + p.cap;
+  float* prob = reinterpret_cast<float*>(spare + p.cap);
+  float* cum = prob + p.cap;
+  uint8_t* pairs = reinterpret_cast<uint8_t*>(cum + p.cap);  // per warp: 32 * kStageChunks pairs
+
+  const int t = threadIdx.x;
+  const int G = static_cast<int>(gridDim.x);
+  const int V = p.vocab;
+  const int R = p.ring;
+  const int nst = p.nst;
+  const uint32_t cap = static_cast<uint32_t>(p.cap);
+  // past `high` candidates the buffer is cut back to about kk (the row end ranks up to NT directly)
+  const uint32_t high = min(cap / 2u, max(static_cast<uint32_t>(NT), 4u * static_cast<uint32_t>(p.K)));
+  const int nrows = (p.batch - static_cast<int>(blockIdx.x) + G - 1) / G;
+  const int total = nrows * nst;
+
+  // thread 0: stage q of this CTA = stage q % nst of its row q / nst, into ring slot q % R
+  auto issue = [&](int q) {
+    const int i = q / nst;
+    const int st = q - i * nst;
+    const int64_t b = static_cast<int64_t>(blockIdx.x) + static_cast<int64_t>(i) * G;
+    const int off = st * kStageElems;
+    const uint32_t bytes = static_cast<uint32_t>(min(kStageElems, V - off)) * 2u;
+    uint64_t* bar = &bars[q % R];
+    mbar_expect_tx(bar, bytes);
+    bulk_load(ring + static_cast<size_t>(q % R) * (kStageBytes / 16), p.logits + b * p.row_stride + off, bytes,
+              bar);
+  };
+
+  if (t == 0) {
+    for (int r = 0; r < R; ++r) mbar_init(&bars[r], 1u);
+    mbar_init_fence();
+  }
+  sh.h1[t] = 0u;
+  sh.h2[t] = 0u;
+  if (t < 16) sh.ctl[t] = 0u;
   __syncthreads();
-  finish_row<DT>(p, b, sel, static_cast<int>(sh.ctl[kCtlLocal]), gath, kk, pp, u, prob, cum, sh);
+  if (t == 0) {
+    for (int q = 0; q < min(R, total); ++q) issue(q);
+  }
+
+  bool timed_out = false;
+  int q = 0;
+  int i = 0;
+  for (; i < nrows; ++i) {
+    const int b = static_cast<int>(blockIdx.x) + i * G;
+    int kk;
+    float pp;
+    bool bad;
+    row_params(p, b, &kk, &pp, &bad);
+    const float u = t < 32 ? row_uniform(p, b) : 0.0f;
+    uint32_t lkey = 0u;
+    uint32_t rflags = 0u;
+    bool overflow = false;
+    bool hit_high = false;  // one of this thread's appends went past `high`
+    uint64_t* cbuf = cand;
+    uint64_t* sbuf = spare;
+
+    for (int st = 0; st < nst; ++st, ++q) {
+      const int slot = q % R;
+      if (!timed_out) timed_out = !mbar_wait(&bars[slot], static_cast<uint32_t>((q / R) & 1));
+      const int off = st * kStageElems;
+      const uint4* stage = ring + static_cast<size_t>(slot) * (kStageBytes / 16);
+      uint4 v[kStageChunks];
+      uint32_t validm = 0u;
+#pragma unroll
+      for (int c = 0; c < kStageChunks; ++c) {
+        const bool valid = off + (c * NT + t) * 8 < V;
+        v[c] = valid ? stage[c * NT + t] : make_uint4(Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2,
+                                                      Fmt<DT>::kNegInf2);
+        validm |= static_cast<uint32_t>(valid) << c;
+      }
+      uint32_t mx[4] = {Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2};
+#pragma unroll
+      for (int c = 0; c < kStageChunks; ++c) {
+#pragma unroll
+        for (int w = 0; w < 4; ++w) mx[w] = pair_max_nan<DT>(mx[w], word_of(v[c], w));
+      }
+      const uint32_t m2 = pair_max_nan<DT>(pair_max_nan<DT>(mx[0], mx[2]), pair_max_nan<DT>(mx[1], mx[3]));
+      const uint32_t mbits = half_max_nan<DT>(m2 & 0xFFFFu, m2 >> 16);
+      if (Fmt<DT>::is_nan(mbits)) {
+        rflags |= kFlagNaN;
+      } else {
+        if (mbits == Fmt<DT>::kPosInf) rflags |= kFlagPosInf;
+        if (mbits != Fmt<DT>::kNegInf) rflags |= kFlagAboveNegInf;
+      }
+      if (st == 0) {  // sub-chunk maxima for the first threshold
+        const int mpt = p.mpt;
+        if (mpt == 8) {
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            sh.mkeys[t * 8 + 2 * w] = order_key(mx[w] & 0xFFFFu);
+            sh.mkeys[t * 8 + 2 * w + 1] = order_key(mx[w] >> 16);
+          }
+        } else if (mpt == 4) {
+          const uint32_t a = pair_max_nan<DT>(mx[0], mx[2]), c2 = pair_max_nan<DT>(mx[1], mx[3]);
+          sh.mkeys[t * 4 + 0] = order_key(a & 0xFFFFu);
+          sh.mkeys[t * 4 + 1] = order_key(a >> 16);
+          sh.mkeys[t * 4 + 2] = order_key(c2 & 0xFFFFu);
+          sh.mkeys[t * 4 + 3] = order_key(c2 >> 16);
+        } else if (mpt == 2) {
+          sh.mkeys[t * 2 + 0] = order_key(m2 & 0xFFFFu);
+          sh.mkeys[t * 2 + 1] = order_key(m2 >> 16);
+        } else {
+          sh.mkeys[t] = order_key(mbits);
+        }
+      }
+      // S1: the previous stage is finished by every thread (its slot may be refilled) and its
+      // appends are complete. A timeout or a candidate buffer past `high` asks for attention;
+      // otherwise nothing else synchronises the stage.
+      const int attention = __syncthreads_or((timed_out || hit_high) ? 1 : 0);
+      if (t == 0 && q >= 1 && q - 1 + R < total) {
+        fence_proxy_async_smem();
+        issue(q - 1 + R);
+      }
+      if (attention) {
+        if (timed_out) sh.ctl[kCtlTmo] = 1u;
+        __syncthreads();
+        if (sh.ctl[kCtlTmo] != 0u) {
+          timed_out = true;
+          break;
+        }
+        hit_high = false;
+        const uint32_t n = sh.ctl[kCtlN];  // stable: no thread appends before the next barrier
+        if (n > cap) {
+          overflow = true;
+        } else if (n > high) {
+          for (uint32_t j = t; j < n; j += NT) sh.mkeys[j] = packed_key(cbuf[j]);
+          __syncthreads();
+          const uint32_t e = kth_largest_key(sh.mkeys, static_cast<int>(n), kk, sh.h1, sh.h2, &sh.ctl[kCtlScr0]);
+          sh.h1[t] = 0u;
+          sh.h2[t] = 0u;
+          for (uint32_t j = t; j < n; j += NT) {
+            if (sh.mkeys[j] >= e) sbuf[atomicAdd(&sh.ctl[kCtlLocal], 1u)] = cbuf[j];
+          }
+          __syncthreads();
+          const uint32_t kept = sh.ctl[kCtlLocal];
+          __syncthreads();
+          if (t == 0) {
+            sh.ctl[kCtlN] = kept;
+            sh.ctl[kCtlLocal] = 0u;
+          }
+          uint64_t* tmp = cbuf;
+          cbuf = sbuf;
+          sbuf = tmp;
+          lkey = max(lkey, e);
+        }
+        __syncthreads();
+      }
+      if (st == 0) {
+        const uint32_t kth = kth_largest_key(sh.mkeys, NT * p.mpt, kk, sh.h1, sh.h2, &sh.ctl[kCtlScr0]);
+        lkey = max(kth, order_key(Fmt<DT>::kNegInf));
+        sh.h1[t] = 0u;
+        sh.h2[t] = 0u;
+      }
+      // Filter, warp-cooperative: a lane whose maximum reaches L marks its chunks that hold an
+      // element >= L; the warp lists the marked (lane, chunk) pairs, hands one pair to each
+      // lane, which re-reads that chunk from the stage (refilled only after the next S1), and
+      // appends every hit with one shared atomic per warp.
+      if (!overflow) {
+        const bool hot = !Fmt<DT>::is_nan(mbits) && order_key(mbits) >= lkey;
+        if (__ballot_sync(0xFFFFFFFFu, hot) != 0u) {
+          const int lane = t & 31;
+          const uint32_t lbits = key_to_bits(lkey);
+          const uint32_t l2 = lbits | (lbits << 16);
+          uint32_t cm = 0u;
+          if (hot) {
+#pragma unroll
+            for (int c = 0; c < kStageChunks; ++c) {
+              const uint32_t any = pair_ge_mask<DT>(v[c].x, l2) | pair_ge_mask<DT>(v[c].y, l2) |
+                                   pair_ge_mask<DT>(v[c].z, l2) | pair_ge_mask<DT>(v[c].w, l2);
+              cm |= (any != 0u ? 1u : 0u) << c;
+            }
+            cm &= validm;
+          }
+          const int np = __popc(cm);
+          const int pincl = warp_incl_scan(np);
+          const int npairs = __shfl_sync(0xFFFFFFFFu, pincl, 31);
+          uint8_t* wp = pairs + (t >> 5) * (32 * kStageChunks);
+          int k = pincl - np;
+          while (cm != 0u) {
+            const int c = __ffs(cm) - 1;
+            cm &= cm - 1u;
+            wp[k++] = static_cast<uint8_t>((lane << 3) | c);
+          }
+          __syncwarp();
+          for (int base = 0; base < npairs; base += 32) {
+            const int pi = base + lane;
+            uint32_t hits = 0u;  // bit 2w + h: half h of word w of the chunk is >= L
+            uint4 x = make_uint4(0u, 0u, 0u, 0u);
+            int e0 = 0;
+            if (pi < npairs) {
+              const int pr = wp[pi];
+              const int owner = (t & ~31) + (pr >> 3);
+              const int c = pr & 7;
+              x = stage[c * NT + owner];
+              e0 = off + (c * NT + owner) * 8;
+#pragma unroll
+              for (int w = 0; w < 4; ++w) {
+                const uint32_t m = pair_ge_mask<DT>(word_of(x, w), l2);
+                hits |= ((m & 1u) | ((m >> 15) & 2u)) << (2 * w);
+              }
+            }
+            const int nh = __popc(hits);
+            const int hincl = warp_incl_scan(nh);
+            const int htot = __shfl_sync(0xFFFFFFFFu, hincl, 31);
+            uint32_t hbase = 0u;
+            if (lane == 31 && htot > 0) hbase = atomicAdd(&sh.ctl[kCtlN], static_cast<uint32_t>(htot));
+            hbase = __shfl_sync(0xFFFFFFFFu, hbase, 31);
+            uint32_t j = hbase + static_cast<uint32_t>(hincl - nh);
+            while (hits != 0u) {
+              const int bit = __ffs(hits) - 1;
+              hits &= hits - 1u;
+              const int w = bit >> 1;
+              const uint32_t word = w == 0 ? x.x : w == 1 ? x.y : w == 2 ? x.z : x.w;
+              const uint32_t h16 = (word >> (16 * (bit & 1))) & 0xFFFFu;
+              if (j < cap) cbuf[j] = pack(order_key(h16), p.id_base + e0 + bit);
+              hit_high |= j >= high;
+              ++j;
+            }
+          }
+        }
+      }
+    }
+    if (timed_out) break;
+
+    // ---- end of row ----
+    rflags = __reduce_or_sync(0xFFFFFFFFu, rflags);
+    if ((t & 31) == 0 && rflags != 0u) atomicOr(&sh.ctl[kCtlFlags], rflags);
+    __syncthreads();
+    const uint32_t n = sh.ctl[kCtlN];
+    const uint32_t f = sh.ctl[kCtlFlags];
+    __syncthreads();
+    if (t == 0) {
+      sh.ctl[kCtlN] = 0u;
+      sh.ctl[kCtlFlags] = 0u;
+    }
+    int status = FS_ROW_OK;
+    if (bad) status = FS_ROW_BAD_PARAM;
+    else if (f & kFlagNaN) status = FS_ROW_NAN;
+    else if (f & kFlagPosInf) status = FS_ROW_POSINF;
+    else if (!(f & kFlagAboveNegInf)) status = FS_ROW_ALL_NEGINF;
+    if (status != FS_ROW_OK) {
+      write_invalid_row(p, b, status);
+    } else if (overflow || n > cap) {
+      const uint16_t* row = p.logits + static_cast<int64_t>(b) * p.row_stride;
+      const int nchunks = (V + NT * 8 - 1) / (NT * 8);
+      const int got = span_exact_topk<DT>(sh, row, V, p.vec, p.id_base, 0, nchunks, kk, sbuf);
+      __syncthreads();
+      sh.ctl[kCtlLocal] = 0u;  // (every thread writes the same value; read only after a barrier)
+      finish_row<DT>(p, b, sbuf, got, cbuf, kk, pp, u, prob, cum, sh);
+    } else if (n <= static_cast<uint32_t>(NT)) {
+      // every candidate is ranked against all others: the top kk come out sorted
+      finish_row<DT>(p, b, cbuf, static_cast<int>(n), sbuf, kk, pp, u, prob, cum, sh);
+    } else {
+      for (uint32_t j = t; j < n; j += NT) sh.mkeys[j] = packed_key(cbuf[j]);
+      __syncthreads();
+      const uint32_t e = kth_largest_key(sh.mkeys, static_cast<int>(n), kk, sh.h1, sh.h2, &sh.ctl[kCtlScr0]);
+      sh.h1[t] = 0u;
+      sh.h2[t] = 0u;
+      for (uint32_t j = t; j < n; j += NT) {
+        if (sh.mkeys[j] >= e) sbuf[atomicAdd(&sh.ctl[kCtlLocal], 1u)] = cbuf[j];
+      }
+      __syncthreads();
+      const int nsel = static_cast<int>(sh.ctl[kCtlLocal]);
+      __syncthreads();
+      if (t == 0) sh.ctl[kCtlLocal] = 0u;
+      finish_row<DT>(p, b, sbuf, nsel, cbuf, kk, pp, u, prob, cum, sh);
+    }
+    // the next row reuses the buffers and histograms
+    __syncthreads();
+    sh.h1[t] = 0u;
+    sh.h2[t] = 0u;
+  }
+
+  if (timed_out) {
+    // rows this CTA did not finish get no result; then give the copies in flight a bounded
+    // chance to land before the CTA's shared memory is released
+    for (int r = i; r < nrows; ++r) write_invalid_row(p, static_cast<int>(blockIdx.x) + r * G, FS_ROW_TIMEOUT);
+    if (t == 0) {
+      const int last = min(total, q + R + 1);
+      for (int qq = q; qq < last; ++qq) (void)mbar_wait(&bars[qq % R], static_cast<uint32_t>((qq / R) & 1));
+    }
+  }
 }
 
 // Merge of per-shard candidate blocks [parts, B, K + 1] for vocab-sharded tensor parallelism:
@@ -1339,9 +1812,14 @@ constexpr int kMaxCap = 8192;
 constexpr int64_t kStreamMaxK = 256;     // streaming path: top-K bound
 constexpr int64_t kStreamMinBatch = 128;  // AUTO: rows from which the streaming path is used
 constexpr int64_t kStreamAutoMaxK = 128;  // AUTO: largest k for which it is used
+constexpr size_t kPersistSmemBudget = 227 * 1024;  // opt-in dynamic shared memory per CTA
 
 // Plan of one call: cluster size, chunks per thread, survivor capacity, maxima granularity.
 fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t path, PlanOut* out) {
+  if (path < FS_PATH_AUTO || path > FS_PATH_PERSIST) {
+    set_error("path must be one of FS_PATH_AUTO, FS_PATH_CLUSTER, FS_PATH_STREAM, FS_PATH_PERSIST; got %d", path);
+    return FS_EINVAL;
+  }
   const int64_t per_cta_chunk = static_cast<int64_t>(NT) * 8;  // elements per chunk per CTA
   constexpr int kMaxChunks = 16;
   const int64_t min_s = std::max<int64_t>(1, (V + per_cta_chunk * kMaxChunks - 1) / (per_cta_chunk * kMaxChunks));
@@ -1403,6 +1881,34 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t pat
   out->merge_cap = 0;
   out->merge_smem = 0;
   out->workspace = 0;
+  out->persist = 0;
+  out->ring = 0;
+  out->nst = 0;
+
+  // persistent row-streaming path: whole rows through a ring of shared-memory stages
+  const bool want_persist = path == FS_PATH_PERSIST;
+  if (path == FS_PATH_PERSIST && K > kStreamMaxK) {
+    set_error("the persistent path supports top_k <= %lld", static_cast<long long>(kStreamMaxK));
+    return FS_EUNSUPPORTED;
+  }
+  if (want_persist) {
+    const int pcap = std::max(1024, pow2_ceil(8 * K));
+    const size_t fixed = sizeof(Shared) + kRingOffset + static_cast<size_t>(pcap) * 24 + NT * kStageChunks;
+    const int ring = static_cast<int>(
+        std::min<size_t>(kMaxRing, (kPersistSmemBudget - fixed) / static_cast<size_t>(kStageBytes)));
+    out->persist = 1;
+    out->ring = ring;
+    out->nst = static_cast<int>((V + kStageElems - 1) / kStageElems);
+    out->splits = 1;
+    out->chunks = kStageChunks;
+    out->capacity = pcap;
+    out->mpt = static_cast<int>(std::min<int64_t>(8, pow2_ceil((4 * K + NT - 1) / NT)));
+    out->mgroup = 1;
+    out->mcta = NT * out->mpt;
+    out->slot = 0;
+    out->smem = static_cast<int>(fixed + static_cast<size_t>(ring) * kStageBytes);
+    return FS_OK;
+  }
 
   // streaming path: slices keep their own top-K in M slots; the row merge gathers S * M
   const int M = std::max(64, pow2_ceil(2 * K));
@@ -1434,9 +1940,10 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t pat
     out->mgroup = 1;
     out->mcta = NT * out->mpt;
     out->slot = M;
-    out->smem = static_cast<int>(sizeof(Shared));
+    out->smem = static_cast<int>(sizeof(Shared) + static_cast<size_t>(NT) * Cs * sizeof(uint16_t));
     out->merge_cap = std::max(256, pow2_ceil(static_cast<int64_t>(S) * M));
-    out->merge_smem = static_cast<int>(sizeof(Shared) + static_cast<size_t>(out->merge_cap) * 24);
+    out->merge_smem = static_cast<int>(merge_warps(out->merge_cap, static_cast<int>(K)) *
+                                       merge_warp_bytes(out->merge_cap, static_cast<int>(K)));
     out->workspace = static_cast<uint64_t>(B) * S * M * sizeof(uint64_t) + static_cast<uint64_t>(B) * S * 4 + 256;
   }
   return FS_OK;
@@ -1618,7 +2125,7 @@ KernelFn slice_kernel_for(int C) {
 }
 
 using SliceFn = void (*)(const Params, uint64_t*, uint32_t*);
-using RowMergeFn = void (*)(const Params, const uint64_t*, const uint32_t*, int);
+using RowMergeFn = void (*)(const Params, const uint64_t*, const uint32_t*, int, int);
 
 static fs_status launch_stream(const fs_sample_args* a, const PlanOut& plan, const Params& prm,
                                cudaStream_t stream) {
@@ -1640,20 +2147,59 @@ static fs_status launch_stream(const fs_sample_args* a, const PlanOut& plan, con
   }
   fs_status st = prepare_kernel(reinterpret_cast<KernelFn>(sfn), 1, plan.smem);
   if (st != FS_OK) return st;
-  st = prepare_kernel(reinterpret_cast<KernelFn>(mfn), 1, plan.merge_smem);
-  if (st != FS_OK) return st;
   sfn<<<dim3(plan.splits, static_cast<unsigned>(a->batch)), NT, plan.smem, stream>>>(prm, cand, cnt);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error("slice launch: %s", cudaGetErrorString(e));
     return FS_ELAUNCH;
   }
+  st = prepare_kernel(reinterpret_cast<KernelFn>(mfn), 1, plan.merge_smem);
+  if (st != FS_OK) return st;
   Params mp = prm;
   mp.cap = plan.merge_cap;
-  mfn<<<static_cast<unsigned>(a->batch), NT, plan.merge_smem, stream>>>(mp, cand, cnt, plan.splits);
+  const int mw = merge_warps(plan.merge_cap, static_cast<int>(prm.K));
+  const unsigned mgrid = static_cast<unsigned>((a->batch + mw - 1) / mw);
+  mfn<<<mgrid, 32 * mw, plan.merge_smem, stream>>>(mp, cand, cnt, plan.splits, static_cast<int>(a->batch));
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error("row-merge launch: %s", cudaGetErrorString(e));
+    return FS_ELAUNCH;
+  }
+  return FS_OK;
+}
+
+// SMs of the current device (cached per device).
+static int sm_count() {
+  static int counts[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (counts[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    counts[dev] = n;
+  }
+  return counts[dev];
+}
+
+static fs_status launch_persist(int dtype, const PlanOut& plan, int64_t B, Params prm, cudaStream_t stream) {
+  KernelFn fn = dtype == FS_BF16 ? reinterpret_cast<KernelFn>(fs_rowstream_kernel<1>)
+                                 : reinterpret_cast<KernelFn>(fs_rowstream_kernel<0>);
+  fs_status st = prepare_kernel(fn, 1, plan.smem);
+  if (st != FS_OK) return st;
+  const int nsm = sm_count();
+  if (nsm <= 0) {
+    set_error("could not read the SM count of the current device");
+    return FS_ELAUNCH;
+  }
+  prm.batch = static_cast<int32_t>(B);
+  prm.ring = plan.ring;
+  prm.nst = plan.nst;
+  const int grid = static_cast<int>(std::min<int64_t>(B, nsm));
+  using PersistFn = void (*)(const Params);
+  reinterpret_cast<PersistFn>(fn)<<<grid, NT, plan.smem, stream>>>(prm);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("persistent launch: %s", cudaGetErrorString(e));
     return FS_ELAUNCH;
   }
   return FS_OK;
@@ -1667,6 +2213,15 @@ fs_status run_cluster(const fs_sample_args* a, int mode, uint64_t* cand_out, cud
   fs_status st = make_plan(a->batch, a->vocab, K, a->splits, path, &plan);
   if (st != FS_OK) return st;
   Params prm = base_params(a, K);
+  if (plan.persist && !(prm.vec && a->vocab % 8 == 0)) {
+    // bulk copies need 16-byte aligned rows of whole 16-byte vectors
+    if (path == FS_PATH_PERSIST) {
+      set_error("the persistent path needs 16-byte aligned rows and a vocabulary that is a multiple of 8");
+      return FS_EUNSUPPORTED;
+    }
+    st = make_plan(a->batch, a->vocab, K, a->splits, FS_PATH_CLUSTER, &plan);
+    if (st != FS_OK) return st;
+  }
   prm.cand_out = cand_out;
   prm.cap = plan.capacity;
   prm.mpt = plan.mpt;
@@ -1675,6 +2230,7 @@ fs_status run_cluster(const fs_sample_args* a, int mode, uint64_t* cand_out, cud
   prm.slot = plan.slot;
   prm.stop = a->stop_phase;
   prm.mode = mode;
+  if (plan.persist) return launch_persist(a->dtype, plan, a->batch, prm, stream);
   if (plan.stream) return launch_stream(a, plan, prm, stream);
   return launch_cluster(a->dtype, plan, a->batch, prm, stream);
 }
@@ -1734,7 +2290,7 @@ void append_cluster_attrs(std::vector<fs_kernel_attr>& rows) {
       std::snprintf(r.name, sizeof(r.name), "fs_slice_kernel<%s>", dt ? "bf16" : "fp16");
       r.param = C;
       r.block = NT;
-      fill_attr(reinterpret_cast<const void*>(fn), NT, static_cast<int>(sizeof(Shared)), &r);
+      fill_attr(reinterpret_cast<const void*>(fn), NT, static_cast<int>(sizeof(Shared) + NT * C * 2), &r);
       rows.push_back(r);
     }
     {
@@ -1743,7 +2299,17 @@ void append_cluster_attrs(std::vector<fs_kernel_attr>& rows) {
       r.param = 0;
       r.block = NT;
       fill_attr(reinterpret_cast<const void*>(dt ? fs_rowmerge_kernel<1> : fs_rowmerge_kernel<0>), NT,
-                static_cast<int>(sizeof(Shared) + 1024 * 24), &r);
+                static_cast<int>(kMergeWarps * merge_warp_bytes(1024, 64)), &r);
+      rows.push_back(r);
+    }
+    {
+      fs_kernel_attr r = {};
+      std::snprintf(r.name, sizeof(r.name), "fs_rowstream_kernel<%s>", dt ? "bf16" : "fp16");
+      r.param = 0;
+      r.block = NT;
+      fill_attr(reinterpret_cast<const void*>(dt ? fs_rowstream_kernel<1> : fs_rowstream_kernel<0>), NT,
+                static_cast<int>(sizeof(Shared) + kRingOffset + 5 * kStageBytes + 1024 * 24 + NT * kStageChunks),
+                &r);
       rows.push_back(r);
     }
     fs_kernel_attr r = {};
@@ -1869,7 +2435,7 @@ extern "C" fs_status fs_plan(int64_t batch, int64_t vocab, int64_t top_k, int32_
   out->maxima_per_thread = p.mpt;
   out->lanes_per_max = p.mgroup;
   out->smem_bytes = p.smem;
-  out->path = p.stream ? FS_PATH_STREAM : FS_PATH_CLUSTER;
+  out->path = p.persist ? FS_PATH_PERSIST : p.stream ? FS_PATH_STREAM : FS_PATH_CLUSTER;
   out->workspace_bytes = p.workspace;
   return FS_OK;
 }

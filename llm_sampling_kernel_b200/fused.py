@@ -19,7 +19,7 @@ from . import ops
 
 DEFAULT_SEED = 0x5EED
 
-ROW_OK, ROW_NAN, ROW_POSINF, ROW_ALL_NEGINF, ROW_BAD_PARAM = 0, 1, 2, 3, 4
+ROW_OK, ROW_NAN, ROW_POSINF, ROW_ALL_NEGINF, ROW_BAD_PARAM, ROW_TIMEOUT = 0, 1, 2, 3, 4, 5
 _ROW_MESSAGES = {
     ROW_NAN: "logits contain NaN",
     ROW_POSINF: "logits contain +inf",
@@ -93,5 +93,7 @@ def sample(
         bad = status[status != ROW_OK]
         if bad.numel():
             code = int(bad.min().item())
+            if code == ROW_TIMEOUT:
+                raise RuntimeError("a bounded device wait of the sampling launch ran out")
             raise ValueError(_ROW_MESSAGES.get(code, f"row status {code}"))
     return SampleResult(ids, status, tk, keep, ren)

@@ -65,7 +65,9 @@ def test_plan_table():
     assert (p.splits, p.chunks, p.threads) == (16, 5, 256)
     assert p.splits * p.chunks * p.threads * 8 >= 151936
     q = abi.plan(1024, 151936, 50)
+    assert q.path == abi.FS_PATH_STREAM and q.workspace_bytes > 0
     assert q.splits * q.chunks * q.threads * 8 >= 151936
+    assert q.smem_bytes <= 227 * 1024
     r = abi.plan(8, 151936, 1024)
     assert r.capacity >= 4 * 1024
     assert r.splits * r.threads * r.maxima_per_thread // r.lanes_per_max >= 4 * 1024
@@ -75,8 +77,12 @@ def test_plan_table():
         for V in (2000, 4001, 32000, 128256, 151936, 256000):
             for k in (1, 50, 256, 1024):
                 pl = abi.plan(B, V, k)
-                assert pl.splits * pl.chunks * pl.threads * 8 >= V
-                assert 1 <= pl.splits <= 16
+                if pl.path == abi.FS_PATH_PERSIST:  # rows stream through 32 KiB stages
+                    assert pl.chunks * pl.threads * 8 == 16384 and pl.splits == 1
+                    assert pl.capacity >= 4 * min(k, V) and pl.smem_bytes <= 227 * 1024
+                else:
+                    assert pl.splits * pl.chunks * pl.threads * 8 >= V
+                    assert 1 <= pl.splits <= 16
                 assert pl.capacity >= min(k, V)
 
 
@@ -113,20 +119,32 @@ def test_invalid_arguments_are_rejected_before_any_launch():
 def test_large_batches_plan_the_streaming_path_with_a_workspace():
     big = abi.plan(1024, 151936, 50)
     assert big.path == abi.FS_PATH_STREAM
-    # [B, S, M] packed candidates + [B, S] counts + alignment slack
+    # [B, S, M] packed candidates (M >= 2k) + [B, S] counts + alignment slack
     assert big.workspace_bytes >= 1024 * big.splits * (2 * 50 * 8 + 4)
     assert abi.plan(1, 151936, 50).path == abi.FS_PATH_CLUSTER
     assert abi.plan(1, 151936, 50).workspace_bytes == 0
-    # beyond the streaming slots the cluster path serves every batch size
+    # beyond the streaming path's k the cluster path serves every batch size
     assert abi.plan(1024, 151936, 1024).path == abi.FS_PATH_CLUSTER
+    assert abi.plan(1024, 151936, 256).path == abi.FS_PATH_CLUSTER
+
+
+def test_the_forced_streaming_path_plans_a_workspace():
+    lib = abi.lib()
+    a = abi.FsSampleArgs()
+    a.dtype, a.batch, a.vocab, a.row_stride, a.top_k, a.top_p = abi.FS_BF16, 1024, 151936, 151936, 50, 0.9
+    a.path = abi.FS_PATH_STREAM
+    # [B, S, M] packed candidates (M >= 2k) + [B, S] counts + alignment slack, S >= 8 slices
+    assert lib.fs_workspace_size(ctypes.byref(a)) >= 1024 * 8 * (2 * 50 * 8 + 4)
 
 
 def test_workspace_size_follows_the_plan_and_the_path_override():
     lib = abi.lib()
     a = abi.FsSampleArgs()
     a.dtype, a.batch, a.vocab, a.row_stride, a.top_k, a.top_p = abi.FS_BF16, 1024, 151936, 151936, 50, 0.9
-    assert lib.fs_workspace_size(ctypes.byref(a)) == abi.plan(1024, 151936, 50).workspace_bytes
+    assert lib.fs_workspace_size(ctypes.byref(a)) == abi.plan(1024, 151936, 50).workspace_bytes > 0
     a.path = abi.FS_PATH_CLUSTER
+    assert lib.fs_workspace_size(ctypes.byref(a)) == 0
+    a.path = abi.FS_PATH_PERSIST
     assert lib.fs_workspace_size(ctypes.byref(a)) == 0
     a.path, a.batch = abi.FS_PATH_STREAM, 1
     assert lib.fs_workspace_size(ctypes.byref(a)) > 0
@@ -139,9 +157,26 @@ def test_the_streaming_path_without_its_workspace_is_rejected_before_any_launch(
     a.dtype, a.batch, a.vocab, a.row_stride, a.top_k, a.top_p = abi.FS_BF16, 1024, 151936, 151936, 50, 0.9
     a.logits = 0x1000
     a.out_ids = 0x2000
+    a.path = abi.FS_PATH_STREAM
     assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EWORKSPACE
     assert "workspace" in lib.fs_last_error().decode()
     a.workspace, a.workspace_bytes = 0x3000, 64
     assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EWORKSPACE
     a.path, a.top_k = abi.FS_PATH_STREAM, 1024
     assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EUNSUPPORTED
+
+
+def test_unknown_paths_and_unsupported_forced_paths_are_rejected():
+    lib = abi.lib()
+    a = abi.FsSampleArgs()
+    a.dtype, a.batch, a.vocab, a.row_stride, a.top_k, a.top_p = abi.FS_BF16, 4, 151936, 151936, 50, 0.9
+    a.logits, a.out_ids = 0x1000, 0x2000
+    a.path = 9
+    assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EINVAL
+    assert "path" in lib.fs_last_error().decode()
+    a.path, a.top_k = abi.FS_PATH_PERSIST, 1024
+    assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EUNSUPPORTED
+    # rows that bulk copies cannot move (odd vocabulary) are refused by the forced path
+    a.top_k, a.vocab, a.row_stride = 50, 151935, 151935
+    assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EUNSUPPORTED
+    assert "multiple of 8" in lib.fs_last_error().decode()

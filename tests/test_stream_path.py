@@ -1,10 +1,10 @@
-"""CUDA parity tests of the large-batch streaming path (slice launch + row-merge launch).
+"""CUDA parity tests of the large-batch paths: STREAM (slice launch + row-merge launch) and
+PERSIST (one CTA per SM streaming whole rows through bulk-copied shared-memory stages).
 
-The streaming path must give exactly what the cluster path gives: the same top-k set and order
-(checked against the oracle), and, because both end in the same row tail over the same
-candidates, the same ids, keep mask, renormed probabilities and row status, bit for bit.
-`path=2` forces it at any batch (k <= 256); batches of 128 rows and more take it by default when
-k <= 128.
+Each must give exactly what the cluster path gives: the same top-k set and order (checked against
+the oracle), and, because all end in the same row tail over the same candidates, the same ids,
+keep mask, renormed probabilities and row status, bit for bit. `path=` forces a path at any batch
+(k <= 256); batches of 128 rows and more take STREAM by default when k <= 128.
 """
 
 import numpy as np
@@ -18,7 +18,8 @@ from oracle import sampler_oracle as orc
 pytestmark = pytest.mark.gpu
 
 DTYPES = [torch.float16, torch.bfloat16]
-CLUSTER, STREAM = abi.FS_PATH_CLUSTER, abi.FS_PATH_STREAM
+CLUSTER, STREAM, PERSIST = abi.FS_PATH_CLUSTER, abi.FS_PATH_STREAM, abi.FS_PATH_PERSIST
+PATHS = [STREAM, PERSIST]
 
 
 def dev_randn(B, V, scale, dtype, seed=0):
@@ -35,9 +36,9 @@ def run(x, top_k, top_p, path, **kw):
     return out, ids, keep, ren, status
 
 
-def assert_paths_agree(x, top_k, top_p, **kw):
+def assert_paths_agree(x, top_k, top_p, path=STREAM, **kw):
     a = run(x, top_k, top_p, CLUSTER, **kw)
-    b = run(x, top_k, top_p, STREAM, **kw)
+    b = run(x, top_k, top_p, path, **kw)
     for name, p, q in zip(("ids", "topk", "keep", "renormed", "status"), a, b):
         assert torch.equal(p, q), name
     return b
@@ -46,32 +47,40 @@ def assert_paths_agree(x, top_k, top_p, **kw):
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("top_k", [1, 20, 50, 100, 256])
 @pytest.mark.parametrize("vocab", [2000, 4001, 32000, 128256, 151936])
-def test_streaming_candidate_set_matches_the_oracle_exactly(vocab, top_k, dtype):
+@pytest.mark.parametrize("path", PATHS)
+def test_streaming_candidate_set_matches_the_oracle_exactly(vocab, top_k, dtype, path):
     x = dev_randn(24, vocab, 4.0, dtype, seed=vocab + top_k)
-    got = abi.topk(x, top_k, path=STREAM).cpu()
+    if path == PERSIST and vocab % 8:  # bulk copies move whole 16-byte vectors only
+        with pytest.raises(abi.FsError):
+            abi.topk(x, top_k, path=path)
+        return
+    got = abi.topk(x, top_k, path=path).cpu()
     assert torch.equal(got, oracle_topk(x, top_k))
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("top_k", [1, 50, 256])
-def test_all_equal_rows_take_the_exact_slice_fallback(top_k, dtype):
+@pytest.mark.parametrize("path", PATHS)
+def test_all_equal_rows_take_the_exact_slice_fallback(top_k, dtype, path):
     # every slice overflows its slots: each writes its exact top-k (lowest ids first)
     x = torch.zeros(3, 151936, device="cuda", dtype=dtype)
-    assert torch.equal(abi.topk(x, top_k, path=STREAM).cpu(), torch.arange(top_k).expand(3, top_k))
+    assert torch.equal(abi.topk(x, top_k, path=path).cpu(), torch.arange(top_k).expand(3, top_k))
 
 
 @pytest.mark.parametrize("vocab", [20000, 151936])
-def test_dense_ties_and_grid_rounded_values(vocab):
+@pytest.mark.parametrize("path", PATHS)
+def test_dense_ties_and_grid_rounded_values(vocab, path):
     x = dev_randn(16, vocab, 0.05, torch.bfloat16, seed=3)
     for top_k in (20, 50, 100, 256):
-        assert torch.equal(abi.topk(x, top_k, path=STREAM).cpu(), oracle_topk(x, top_k))
+        assert torch.equal(abi.topk(x, top_k, path=path).cpu(), oracle_topk(x, top_k))
     for dtype in DTYPES:
         g = orc.grid_logits(16, vocab, 1.0, dtype, seed=vocab).cuda()
         for top_k in (1, 50, 256):
-            assert torch.equal(abi.topk(g, top_k, path=STREAM).cpu(), oracle_topk(g, top_k))
+            assert torch.equal(abi.topk(g, top_k, path=path).cpu(), oracle_topk(g, top_k))
 
 
-def test_ties_straddling_slice_boundaries_keep_the_lowest_ids():
+@pytest.mark.parametrize("path", PATHS)
+def test_ties_straddling_slice_boundaries_keep_the_lowest_ids(path):
     # a block of equal maxima across a slice boundary, plus heavy ties at the k-th value
     x = torch.full((4, 151936), -5.0)
     x[0, 10000:12000] = 3.0
@@ -83,10 +92,11 @@ def test_ties_straddling_slice_boundaries_keep_the_lowest_ids():
     for dtype in DTYPES:
         xd = x.to(dtype).cuda()
         for k in (1, 7, 50, 256):
-            assert torch.equal(abi.topk(xd, k, path=STREAM).cpu(), oracle_topk(xd, k))
+            assert torch.equal(abi.topk(xd, k, path=path).cpu(), oracle_topk(xd, k))
 
 
-def test_signed_zeros_tie_across_slices():
+@pytest.mark.parametrize("path", PATHS)
+def test_signed_zeros_tie_across_slices(path):
     x = torch.full((2, 40000), -1.0)
     x[0, ::3] = 0.0
     x[0, 1::3] = -0.0
@@ -95,16 +105,17 @@ def test_signed_zeros_tie_across_slices():
     for dtype in DTYPES:
         xd = x.to(dtype).cuda()
         for k in (5, 150, 256):
-            assert torch.equal(abi.topk(xd, k, path=STREAM).cpu(), oracle_topk(xd, k))
+            assert torch.equal(abi.topk(xd, k, path=path).cpu(), oracle_topk(xd, k))
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("top_k,top_p", [(1, 1.0), (50, 0.9), (100, 0.95), (256, 0.5), (256, 1.0)])
-def test_stages_and_ids_equal_the_cluster_path(top_k, top_p, dtype):
+@pytest.mark.parametrize("path", PATHS)
+def test_stages_and_ids_equal_the_cluster_path(top_k, top_p, dtype, path):
     x = dev_randn(96, 151936, 3.0, dtype, seed=top_k)
     u = torch.rand(96, generator=torch.Generator().manual_seed(top_k)).cuda()
-    assert_paths_agree(x, top_k, top_p, uniforms=u)
-    assert_paths_agree(x, top_k, top_p, seed=17, offset=top_k)
+    assert_paths_agree(x, top_k, top_p, path, uniforms=u)
+    assert_paths_agree(x, top_k, top_p, path, seed=17, offset=top_k)
 
 
 def test_anchor_batch_takes_the_streaming_path_and_matches_the_oracle():
@@ -118,13 +129,15 @@ def test_anchor_batch_takes_the_streaming_path_and_matches_the_oracle():
     assert int(d.near_boundary.sum()) <= 2
 
 
-def test_zipf_rows_match_the_oracle():
+@pytest.mark.parametrize("path", PATHS)
+def test_zipf_rows_match_the_oracle(path):
     x = orc.zipf_logits(64, 151936, seed=2).cuda()
     for k in (50, 256):
-        assert torch.equal(abi.topk(x, k, path=STREAM).cpu(), oracle_topk(x, k))
+        assert torch.equal(abi.topk(x, k, path=path).cpu(), oracle_topk(x, k))
 
 
-def test_per_row_k_and_p_and_bad_rows():
+@pytest.mark.parametrize("path", PATHS)
+def test_per_row_k_and_p_and_bad_rows(path):
     B = 80
     x = dev_randn(B, 151936, 3.0, torch.bfloat16, seed=8)
     g = torch.Generator().manual_seed(3)
@@ -133,18 +146,19 @@ def test_per_row_k_and_p_and_bad_rows():
     ks[5] = 0       # bad parameter
     ps[7] = 1.5     # bad parameter
     u = torch.rand(B, generator=g).cuda()
-    out = assert_paths_agree(x, 256, 1.0, top_k_rows=ks.cuda(), top_p_rows=ps.cuda(), uniforms=u)
+    out = assert_paths_agree(x, 256, 1.0, path, top_k_rows=ks.cuda(), top_p_rows=ps.cuda(), uniforms=u)
     status = out[4].cpu()
     assert status[5] == 4 and status[7] == 4
 
 
-def test_invalid_rows_report_the_same_status():
+@pytest.mark.parametrize("path", PATHS)
+def test_invalid_rows_report_the_same_status(path):
     x = orc.adversarial_logits(4, B=8, V=151936).cuda()
     y = x.clone()
     y[1, 77] = float("nan")
     y[2, :] = float("-inf")
     for z in (x, y):
-        out = assert_paths_agree(z, 50, 0.9, seed=1, offset=1)
+        out = assert_paths_agree(z, 50, 0.9, path, seed=1, offset=1)
         assert out[4].cpu().numpy().tolist() == orc.row_status(z.cpu()).tolist()
 
 
@@ -160,6 +174,77 @@ def test_strided_unaligned_and_odd_vocab_rows():
     assert_paths_agree(odd, 50, 0.9, uniforms=u)
 
 
+def test_persistent_path_refuses_rows_bulk_copies_cannot_move_and_auto_falls_back():
+    base = dev_randn(160, 151936 + 24, 3.0, torch.bfloat16, seed=13)
+    odd = base[:, 3:3 + 151936]  # rows not 16-byte aligned
+    with pytest.raises(abi.FsError) as e:
+        abi.topk(odd, 50, path=PERSIST)
+    assert e.value.status == abi.FS_EUNSUPPORTED
+    assert torch.equal(abi.topk(odd, 50).cpu(), oracle_topk(odd.contiguous(), 50))
+    y = dev_randn(160, 100003, 3.0, torch.float16, seed=14)  # V % 8 != 0
+    with pytest.raises(abi.FsError):
+        abi.topk(y, 50, path=PERSIST)
+    u = torch.rand(160, generator=torch.Generator().manual_seed(5)).cuda()
+    a = run(y, 50, 0.9, abi.FS_PATH_AUTO, uniforms=u)
+    b = run(y, 50, 0.9, CLUSTER, uniforms=u)
+    for p, q in zip(a, b):
+        assert torch.equal(p, q)
+    view = base[:, 8:8 + 151936]  # aligned view with a padded stride
+    assert torch.equal(abi.topk(view, 50, path=PERSIST).cpu(), oracle_topk(view.contiguous(), 50))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("batch", [1, 149, 300, 1024])
+def test_persistent_rows_spread_over_the_grid(batch, dtype):
+    # more rows than SMs: each CTA walks several rows and its ring crosses row boundaries
+    x = dev_randn(batch, 151936, 3.0, dtype, seed=batch)
+    u = torch.rand(batch, generator=torch.Generator().manual_seed(batch)).cuda()
+    assert_paths_agree(x, 50, 0.9, PERSIST, uniforms=u)
+    rows = torch.arange(0, batch, max(1, batch // 7))
+    assert torch.equal(abi.topk(x, 50, path=PERSIST).cpu()[rows], oracle_topk(x[rows], 50))
+
+
+@pytest.mark.parametrize("top_k", [1, 50, 128, 256])
+def test_rising_rows_force_candidate_compaction(top_k):
+    # every stage lifts the row by about one sigma, so each stage adds hundreds of candidates
+    # above the running threshold and the buffer is cut back to the exact k-th key repeatedly
+    B, V = 8, 151936
+    g = torch.Generator().manual_seed(top_k)
+    trend = torch.arange(V, dtype=torch.float32) // 16384 * 0.95
+    x = (torch.randn(B, V, generator=g) + trend).to(torch.bfloat16).cuda()
+    assert torch.equal(abi.topk(x, top_k, path=PERSIST).cpu(), oracle_topk(x, top_k))
+    u = torch.rand(B, generator=g).cuda()
+    assert_paths_agree(x, top_k, 0.9, PERSIST, uniforms=u)
+    steep = (torch.randn(B, V, generator=g) * 0.3 + trend * 3).to(torch.float16).cuda()
+    assert torch.equal(abi.topk(steep, top_k, path=PERSIST).cpu(), oracle_topk(steep, top_k))
+
+
+def test_late_stage_ties_overflow_into_the_exact_fallback():
+    # a tie block in the last stages: the candidate buffer overflows mid-row
+    x = torch.randn(4, 151936, generator=torch.Generator().manual_seed(1))
+    x[:, 140000:] = 3.5
+    x[1, 5] = 9.0
+    x[2, 100000:100600] = 3.5
+    for dtype in DTYPES:
+        xd = x.to(dtype).cuda()
+        for k in (1, 50, 256):
+            assert torch.equal(abi.topk(xd, k, path=PERSIST).cpu(), oracle_topk(xd, k))
+        u = torch.rand(4, generator=torch.Generator().manual_seed(2)).cuda()
+        assert_paths_agree(xd, 50, 0.9, PERSIST, uniforms=u)
+
+
+def test_nan_and_inf_in_a_late_stage_are_reported():
+    x = dev_randn(6, 151936, 2.0, torch.bfloat16, seed=15)
+    x[0, 151000] = float("nan")
+    x[1, 140001] = float("inf")
+    x[2, :] = float("-inf")
+    x[3, :150000] = float("-inf")  # finite values only in the last stage
+    x[4, 16384 * 3 + 7] = float("-inf")
+    out = assert_paths_agree(x, 50, 0.9, PERSIST, seed=3, offset=4)
+    assert out[4].cpu().tolist() == orc.row_status(x.cpu()).tolist()
+    assert out[4].cpu().tolist()[:4] == [1, 2, 3, 0]
+
+
 def test_vocab_shard_candidates_from_the_streaming_path_merge_exactly():
     x = dev_randn(128, 256000, 2.5, torch.bfloat16, seed=4)
     u = torch.rand(128, generator=torch.Generator().manual_seed(3)).cuda()
@@ -173,11 +258,12 @@ def test_vocab_shard_candidates_from_the_streaming_path_merge_exactly():
     assert (status == 0).all()
 
 
-def test_repeated_calls_reuse_no_state():
+@pytest.mark.parametrize("path", PATHS)
+def test_repeated_calls_reuse_no_state(path):
     x = dev_randn(70, 151936, 2.0, torch.float16, seed=12)
-    a = abi.sample(x, 50, 0.9, seed=5, offset=6, path=STREAM)
+    a = abi.sample(x, 50, 0.9, seed=5, offset=6, path=path)
     y = torch.zeros_like(x)
-    abi.sample(y, 50, 0.9, seed=5, offset=6, path=STREAM)
-    b = abi.sample(x, 50, 0.9, seed=5, offset=6, path=STREAM)
+    abi.sample(y, 50, 0.9, seed=5, offset=6, path=path)
+    b = abi.sample(x, 50, 0.9, seed=5, offset=6, path=path)
     assert torch.equal(a, b)
     assert torch.equal(a, abi.sample(x, 50, 0.9, seed=5, offset=6, path=CLUSTER))
