@@ -129,6 +129,13 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int q) {
   return q == 0 ? v.x : q == 1 ? v.y : q == 2 ? v.z : v.w;
 }
 
+// Programmatic dependent launch (griddepcontrol): no-ops when the grid was launched without the
+// programmatic-serialization attribute.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
 // Split cluster barrier: arrive (release) now, wait (acquire) later.
 __device__ __forceinline__ void cluster_arrive() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
@@ -718,6 +725,12 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
 
   cluster_arrive();  // B1 (split): waited for only before the first remote access
 
+  // Programmatic dependent launch: this grid may have started while the previous kernel of the
+  // stream was still running; wait for it (and its writes) before reading any input, then let
+  // the next kernel of the stream start its own launch while this one runs.
+  grid_dependency_wait();
+  grid_launch_dependents();
+
   int kk;
   float pp;
   bool bad;
@@ -1084,39 +1097,47 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_slice_kernel(const Par
   sh.h1[t] = 0u;
   if (t < 16) sh.ctl[t] = 0u;
 
-  // sub-chunk maxima of this thread (mpt of them) and the row flags they carry
-  uint32_t mx[4] = {Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2};
+  // Per-chunk pair maxima (each half: the max of 4 logits of the chunk) and their fold over the
+  // thread's chunks; they give the sub-chunk maxima for 1 or 2 per thread, and later tell which
+  // chunks hold a candidate. Finer maxima (4 or 8 per thread) come from per-word columns.
+  uint32_t cp[C];
 #pragma unroll
-  for (int c = 0; c < C; ++c) {
+  for (int c = 0; c < C; ++c)
+    cp[c] = pair_max_nan<DT>(pair_max_nan<DT>(v[c].x, v[c].y), pair_max_nan<DT>(v[c].z, v[c].w));
+  uint32_t acc = cp[0];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) mx[q] = pair_max_nan<DT>(mx[q], word_of(v[c], q));
-  }
+  for (int c = 1; c < C; ++c) acc = pair_max_nan<DT>(acc, cp[c]);
   uint32_t m16[8];
   int nm;
-  if (p.mpt == 8) {
+  if (p.mpt >= 4) {
+    uint32_t mx[4] = {Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2};
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      m16[2 * q] = mx[q] & 0xFFFFu;
-      m16[2 * q + 1] = mx[q] >> 16;
+    for (int c = 0; c < C; ++c) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) mx[q] = pair_max_nan<DT>(mx[q], word_of(v[c], q));
     }
-    nm = 8;
-  } else if (p.mpt == 4) {
-    const uint32_t a = pair_max_nan<DT>(mx[0], mx[2]), c2 = pair_max_nan<DT>(mx[1], mx[3]);
-    m16[0] = a & 0xFFFFu;
-    m16[1] = a >> 16;
-    m16[2] = c2 & 0xFFFFu;
-    m16[3] = c2 >> 16;
-    nm = 4;
-  } else {
-    const uint32_t a = pair_max_nan<DT>(pair_max_nan<DT>(mx[0], mx[2]), pair_max_nan<DT>(mx[1], mx[3]));
-    if (p.mpt == 2) {
+    if (p.mpt == 8) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        m16[2 * q] = mx[q] & 0xFFFFu;
+        m16[2 * q + 1] = mx[q] >> 16;
+      }
+      nm = 8;
+    } else {
+      const uint32_t a = pair_max_nan<DT>(mx[0], mx[2]), c2 = pair_max_nan<DT>(mx[1], mx[3]);
       m16[0] = a & 0xFFFFu;
       m16[1] = a >> 16;
-      nm = 2;
-    } else {
-      m16[0] = half_max_nan<DT>(a & 0xFFFFu, a >> 16);
-      nm = 1;
+      m16[2] = c2 & 0xFFFFu;
+      m16[3] = c2 >> 16;
+      nm = 4;
     }
+  } else if (p.mpt == 2) {
+    m16[0] = acc & 0xFFFFu;
+    m16[1] = acc >> 16;
+    nm = 2;
+  } else {
+    m16[0] = half_max_nan<DT>(acc & 0xFFFFu, acc >> 16);
+    nm = 1;
   }
   uint32_t flags = 0u;
 #pragma unroll
@@ -1141,67 +1162,38 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_slice_kernel(const Par
   const uint32_t lbits = key_to_bits(lkey);
   const uint32_t l2 = lbits | (lbits << 16);
 
-  // Filter, warp-cooperative: a lane whose maximum reaches L marks its chunks that hold an
-  // element >= L; the warp lists the marked (lane, chunk) pairs, hands one pair to each lane,
-  // which re-reads that chunk (an L1 hit) and appends its hits with one shared atomic per warp.
+  // Filter: the per-chunk maxima mark the chunks of each thread that hold an element >= L (one
+  // packed compare per chunk). A lane then takes its marked chunks one at a time out of its
+  // registers, compares their 8 logits with L and reserves slots for the hits with one shared
+  // atomic per chunk; no warp-wide step.
   uint64_t* slots = cand + (static_cast<size_t>(b) * S + s) * M;
-  const uint32_t pmax = pair_max_nan<DT>(pair_max_nan<DT>(mx[0], mx[2]), pair_max_nan<DT>(mx[1], mx[3]));
-  const uint32_t tmax = half_max_nan<DT>(pmax & 0xFFFFu, pmax >> 16);
-  const bool hot = !Fmt<DT>::is_nan(tmax) && order_key(tmax) >= lkey;
-  if (__ballot_sync(0xFFFFFFFFu, hot) != 0u) {
-    const int lane = t & 31;
-    uint32_t cm = 0u;
-    if (hot) {
+  uint32_t cm = 0u;
 #pragma unroll
-      for (int c = 0; c < C; ++c) {
-        const uint32_t any = pair_ge_mask<DT>(v[c].x, l2) | pair_ge_mask<DT>(v[c].y, l2) |
-                             pair_ge_mask<DT>(v[c].z, l2) | pair_ge_mask<DT>(v[c].w, l2);
-        cm |= (any != 0u ? 1u : 0u) << c;
-      }
-    }
-    const int np = __popc(cm);
-    const int pincl = warp_incl_scan(np);
-    const int npairs = __shfl_sync(0xFFFFFFFFu, pincl, 31);
-    uint16_t* wp = reinterpret_cast<uint16_t*>(g_smem + sizeof(Shared)) + (t >> 5) * (32 * C);
-    int k = pincl - np;
-    while (cm != 0u) {
-      const int c = __ffs(cm) - 1;
-      cm &= cm - 1u;
-      wp[k++] = static_cast<uint16_t>((lane << 4) | c);
-    }
-    __syncwarp();
-    for (int base = 0; base < npairs; base += 32) {
-      const int pi = base + lane;
-      uint32_t hits = 0u;  // bit 2w + h: half h of word w of the chunk is >= L
-      uint4 x = make_uint4(0u, 0u, 0u, 0u);
-      int e0 = 0;
-      if (pi < npairs) {
-        const int pr = wp[pi];
-        const int owner = (t & ~31) + (pr >> 4);
-        e0 = (vbase + (pr & 15) * NT + owner) * 8;
-        x = load_chunk<DT>(row, e0, V, p.vec);
+  for (int c = 0; c < C; ++c) cm |= (pair_ge_mask<DT>(cp[c], l2) != 0u ? 1u : 0u) << c;
+  while (cm != 0u) {
+    const int c = __ffs(cm) - 1;
+    cm &= cm - 1u;
+    uint4 x = v[0];
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          const uint32_t m = pair_ge_mask<DT>(word_of(x, w), l2);
-          hits |= ((m & 1u) | ((m >> 15) & 2u)) << (2 * w);
-        }
-        if (e0 + 8 > V) hits &= (e0 < V) ? ((1u << (V - e0)) - 1u) : 0u;  // past the row end
-      }
-      const int nh = __popc(hits);
-      const int hincl = warp_incl_scan(nh);
-      const int htot = __shfl_sync(0xFFFFFFFFu, hincl, 31);
-      uint32_t hbase = 0u;
-      if (lane == 31 && htot > 0) hbase = atomicAdd(&sh.ctl[kCtlLocal], static_cast<uint32_t>(htot));
-      hbase = __shfl_sync(0xFFFFFFFFu, hbase, 31);
-      uint32_t j = hbase + static_cast<uint32_t>(hincl - nh);
-      while (hits != 0u) {
-        const int bit = __ffs(hits) - 1;
-        hits &= hits - 1u;
-        const int w = bit >> 1;
-        const uint32_t word = w == 0 ? x.x : w == 1 ? x.y : w == 2 ? x.z : x.w;
-        if (j < M) slots[j] = pack(order_key((word >> (16 * (bit & 1))) & 0xFFFFu), p.id_base + e0 + bit);
-        ++j;
-      }
+    for (int cc = 1; cc < C; ++cc)
+      if (c == cc) x = v[cc];
+    const int e0 = (vbase + c * NT + t) * 8;
+    uint32_t hits = 0u;  // bit 2w + h: half h of word w of the chunk is >= L
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const uint32_t m = pair_ge_mask<DT>(word_of(x, w), l2);
+      hits |= ((m & 1u) | ((m >> 15) & 2u)) << (2 * w);
+    }
+    if (e0 + 8 > V) hits &= (e0 < V) ? ((1u << (V - e0)) - 1u) : 0u;  // past the row end
+    if (hits == 0u) continue;
+    uint32_t j = atomicAdd(&sh.ctl[kCtlLocal], static_cast<uint32_t>(__popc(hits)));
+    while (hits != 0u) {
+      const int bit = __ffs(hits) - 1;
+      hits &= hits - 1u;
+      const int w = bit >> 1;
+      const uint32_t word = w == 0 ? x.x : w == 1 ? x.y : w == 2 ? x.z : x.w;
+      if (j < M) slots[j] = pack(order_key((word >> (16 * (bit & 1))) & 0xFFFFu), p.id_base + e0 + bit);
+      ++j;
     }
   }
   __syncthreads();
@@ -1940,7 +1932,7 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t pat
     out->mgroup = 1;
     out->mcta = NT * out->mpt;
     out->slot = M;
-    out->smem = static_cast<int>(sizeof(Shared) + static_cast<size_t>(NT) * Cs * sizeof(uint16_t));
+    out->smem = static_cast<int>(sizeof(Shared));
     out->merge_cap = std::max(256, pow2_ceil(static_cast<int64_t>(S) * M));
     out->merge_smem = static_cast<int>(merge_warps(out->merge_cap, static_cast<int>(K)) *
                                        merge_warp_bytes(out->merge_cap, static_cast<int>(K)));
@@ -2016,13 +2008,17 @@ static fs_status launch_cluster(int dtype, const PlanOut& plan, int64_t B, const
   cfg.blockDim = dim3(NT, 1, 1);
   cfg.dynamicSmemBytes = plan.smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = plan.splits;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // may start while the stream's previous kernel finishes (the kernel waits for it before it
+  // reads anything), which hides most of the launch latency of back-to-back calls
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, fn, prm);
   if (e != cudaSuccess) {
     set_error("cluster launch (splits=%d chunks=%d smem=%d B=%lld): %s", plan.splits, plan.chunks,
@@ -2290,7 +2286,7 @@ void append_cluster_attrs(std::vector<fs_kernel_attr>& rows) {
       std::snprintf(r.name, sizeof(r.name), "fs_slice_kernel<%s>", dt ? "bf16" : "fp16");
       r.param = C;
       r.block = NT;
-      fill_attr(reinterpret_cast<const void*>(fn), NT, static_cast<int>(sizeof(Shared) + NT * C * 2), &r);
+      fill_attr(reinterpret_cast<const void*>(fn), NT, static_cast<int>(sizeof(Shared)), &r);
       rows.push_back(r);
     }
     {
