@@ -1270,7 +1270,7 @@ __global__ void __launch_bounds__(NT) fs_rowmerge_kernel(const Params p, const u
   row_params(p, b, &kk, &pp, &bad);
   const float u = row_uniform(p, b);
   const uint32_t w = lane < S ? __ldcg(cnt + static_cast<size_t>(b) * S + lane) : 0u;
-  const uint32_t c = w & kCountMask;
+  const uint32_t c = min(w & kCountMask, M);  // (never above M; the clamp keeps reads in range)
   const uint32_t inc = warp_incl_scan(c);
   const uint32_t f = __reduce_or_sync(0xFFFFFFFFu, w >> 24);
   const uint32_t n = __shfl_sync(0xFFFFFFFFu, inc, 31);
