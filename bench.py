@@ -372,7 +372,10 @@ def run_ours(args):
                 "d2h_bytes_per_step": C1["B"] * 8, "api": "llm_sampling_kernel_b200.fused.sample_fused"},
         "roofline": {
             "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-            "frac": round(achieved / hbm_peak, 4), "traffic": committed_traffic(),
+            "frac": round(achieved / hbm_peak, 4),
+            # the committed summary is a B=1024 call; a rank's call reads its rows' share
+            "traffic": (None if committed_traffic() is None
+                        else int(committed_traffic() * b_rank / C3["B"])),
             "kernel": (f"fs_slice_kernel<bf16,{plan3[1]}> + fs_rowmerge_kernel<bf16> (one call, both launches)"
                        if plan3[7] == 2 else f"fs_cluster_kernel<bf16,{plan3[1]}>"),
             "workload": f"C3 B={b_rank} per GPU, V=151936, k=50, p=0.95, Zipf(1.1)-biased N(0,3^2), "
