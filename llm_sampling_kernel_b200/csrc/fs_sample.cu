@@ -761,30 +761,41 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
   if (t < 16) sh.ctl[t] = 0u;
 
   // ---- phase 1: sub-chunk maxima ----
-  uint32_t mx[4] = {Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2};
+  // Per-chunk pair maxima (each half: the max of 4 logits of the chunk): folded, they give 1-2
+  // maxima per thread; in phase 4 they tell which chunks hold a survivor. Finer maxima (4 or 8
+  // per thread) come from per-word columns.
+  uint32_t cp[C];
 #pragma unroll
-  for (int c = 0; c < C; ++c) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) mx[q] = pair_max_nan<DT>(mx[q], word_of(v[c], q));
-  }
+  for (int c = 0; c < C; ++c)
+    cp[c] = pair_max_nan<DT>(pair_max_nan<DT>(v[c].x, v[c].y), pair_max_nan<DT>(v[c].z, v[c].w));
   uint32_t m16[8];
   int nm;
-  if (p.mpt == 8) {
+  if (p.mpt >= 4) {
+    uint32_t mx[4] = {Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2};
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      m16[2 * q] = mx[q] & 0xFFFFu;
-      m16[2 * q + 1] = mx[q] >> 16;
+    for (int c = 0; c < C; ++c) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) mx[q] = pair_max_nan<DT>(mx[q], word_of(v[c], q));
     }
-    nm = 8;
-  } else if (p.mpt == 4) {
-    const uint32_t a = pair_max_nan<DT>(mx[0], mx[2]), c2 = pair_max_nan<DT>(mx[1], mx[3]);
-    m16[0] = a & 0xFFFFu;
-    m16[1] = a >> 16;
-    m16[2] = c2 & 0xFFFFu;
-    m16[3] = c2 >> 16;
-    nm = 4;
+    if (p.mpt == 8) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        m16[2 * q] = mx[q] & 0xFFFFu;
+        m16[2 * q + 1] = mx[q] >> 16;
+      }
+      nm = 8;
+    } else {
+      const uint32_t a = pair_max_nan<DT>(mx[0], mx[2]), c2 = pair_max_nan<DT>(mx[1], mx[3]);
+      m16[0] = a & 0xFFFFu;
+      m16[1] = a >> 16;
+      m16[2] = c2 & 0xFFFFu;
+      m16[3] = c2 >> 16;
+      nm = 4;
+    }
   } else {
-    const uint32_t a = pair_max_nan<DT>(pair_max_nan<DT>(mx[0], mx[2]), pair_max_nan<DT>(mx[1], mx[3]));
+    uint32_t a = cp[0];
+#pragma unroll
+    for (int c = 1; c < C; ++c) a = pair_max_nan<DT>(a, cp[c]);
     if (p.mpt == 2) {
       m16[0] = a & 0xFFFFu;
       m16[1] = a >> 16;
@@ -872,34 +883,37 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
   const uint32_t l2 = lbits | (lbits << 16);
   const uint32_t M = static_cast<uint32_t>(p.slot);
   const uint32_t slot0 = dsmem_addr(&surv[s * M], 0);
-  // bit 8c+2q+h of the mask: element (chunk c, word q, half h) of this thread is >= L
-  constexpr int MW = (C * 8 + 31) / 32;
-  uint32_t mask[MW];
+  // The per-chunk maxima mark the chunks holding an element >= L (one packed compare per chunk);
+  // a thread takes its marked chunks out of its registers one at a time, reserves slots for the
+  // chunk's hits with one shared atomic and stores them into its slot range of the leader.
+  uint32_t cm = 0u;
 #pragma unroll
-  for (int i = 0; i < MW; ++i) mask[i] = 0u;
+  for (int c = 0; c < C; ++c) cm |= (pair_ge_mask<DT>(cp[c], l2) != 0u ? 1u : 0u) << c;
+  while (cm != 0u) {
+    const int c = __ffs(cm) - 1;
+    cm &= cm - 1u;
+    uint4 x = v[0];
 #pragma unroll
-  for (int c = 0; c < C; ++c) {
+    for (int cc = 1; cc < C; ++cc)
+      if (c == cc) x = v[cc];
+    const int e0 = (vbase + c * NT + t) * 8;
+    uint32_t hits = 0u;  // bit 2w + h: half h of word w of the chunk is >= L
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t m = pair_ge_mask<DT>(word_of(v[c], q), l2);
-      const uint32_t bits2 = (m & 1u) | ((m >> 15) & 2u);
-      const int bit = 8 * c + 2 * q;
-      mask[bit >> 5] |= bits2 << (bit & 31);
+    for (int w = 0; w < 4; ++w) {
+      const uint32_t m = pair_ge_mask<DT>(word_of(x, w), l2);
+      hits |= ((m & 1u) | ((m >> 15) & 2u)) << (2 * w);
     }
-  }
-  // rare: one rolled loop over the set bits; the value is re-read (an L1 hit)
-#pragma unroll
-  for (int i = 0; i < MW; ++i) {
-    uint32_t w = mask[i];
-    while (w != 0u) {
-      const int bit = 32 * i + __ffs(w) - 1;
-      w &= w - 1;
-      const int c = bit >> 3, j = bit & 7;
-      const int e = (vbase + c * NT + t) * 8 + j;
-      if (e < V) {
-        const uint32_t slot = atomicAdd(&sh.ctl[kCtlLocal], 1u);
-        if (slot < M) st_dsmem64(slot0 + 8u * slot, pack(order_key(row[e]), p.id_base + e));
-      }
+    if (e0 + 8 > V) hits &= (e0 < V) ? ((1u << (V - e0)) - 1u) : 0u;  // past the row end
+    if (hits == 0u) continue;
+    uint32_t slot = atomicAdd(&sh.ctl[kCtlLocal], static_cast<uint32_t>(__popc(hits)));
+    while (hits != 0u) {
+      const int bit = __ffs(hits) - 1;
+      hits &= hits - 1u;
+      const int w = bit >> 1;
+      const uint32_t word = w == 0 ? x.x : w == 1 ? x.y : w == 2 ? x.z : x.w;
+      if (slot < M)
+        st_dsmem64(slot0 + 8u * slot, pack(order_key((word >> (16 * (bit & 1))) & 0xFFFFu), p.id_base + e0 + bit));
+      ++slot;
     }
   }
   __syncthreads();
