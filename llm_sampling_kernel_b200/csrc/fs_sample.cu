@@ -272,6 +272,38 @@ __device__ uint32_t anchored_threshold(const uint32_t* keys, int n, int want, in
   return scratch[8];
 }
 
+// The want-th largest of n 16-bit keys in shared memory by one warp (no block barrier):
+// one 256-bin histogram anchored at the largest key (bin = (max - key) >> sh) in the warp's own
+// 256 words `h`, one warp scan. Returns the lower edge of the boundary bin (exactly the want-th
+// key when sh == 0), or sets *clamped when the boundary falls in the last, open-ended bin (keys
+// spread wider than the histogram) and the caller must search another way. 0 when n < want.
+__device__ uint32_t warp_anchored_kth(const uint32_t* keys, int n, int want, int sh, uint32_t* h,
+                                      bool* clamped) {
+  const int lane = threadIdx.x & 31;
+  uint32_t m = 0u;
+  for (int i = lane; i < n; i += 32) m = max(m, keys[i]);
+  m = __reduce_max_sync(0xFFFFFFFFu, m);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) h[lane * 8 + j] = 0u;
+  __syncwarp();
+  for (int i = lane; i < n; i += 32) atomicAdd(&h[255u - min(255u, (m - keys[i]) >> sh)], 1u);
+  __syncwarp();
+  uint32_t idx = 0u, above = 0u, L = 0u;
+  *clamped = false;
+  if (warp_boundary_256(h, static_cast<uint32_t>(want), &idx, &above)) {
+    const uint32_t bin = 255u - idx;
+    if (bin < 255u) {
+      const uint32_t hi = m - (bin << sh);
+      const uint32_t width = (1u << sh) - 1u;
+      L = hi > width ? hi - width : 0u;
+    } else {
+      *clamped = true;
+    }
+  }
+  __syncwarp();
+  return L;
+}
+
 __device__ __forceinline__ float row_uniform(const Params& p, int b) {
   if (p.uniforms != nullptr) return p.uniforms[b];
   uint64_t seed = p.seed, off = p.offset;
@@ -850,7 +882,10 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
   }
 
   // ---- phase 3: the k-th largest maximum, searched locally by every rank ----
+  // Up to 512 maxima, warp 0 alone finds it with one anchored histogram; otherwise (or when the
+  // maxima spread wider than that histogram) the CTA runs the two-level radix select.
   const int nmax = S * p.mcta;
+  constexpr uint32_t kNoKey = 0xFFFFFFFFu;
   if (t < 32) {
     uint32_t f = t < S ? sh.flags[t] : 0u;
     f = __reduce_or_sync(0xFFFFFFFFu, f);
@@ -860,12 +895,23 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
     else if (f & kFlagPosInf) st = FS_ROW_POSINF;
     else if (!(f & kFlagAboveNegInf)) st = FS_ROW_ALL_NEGINF;
     if (t == 0) sh.ctl[kCtlStatus] = static_cast<uint32_t>(st);
-  }
-  {
-    const uint32_t kth = kth_largest_key(sh.mkeys, nmax, kk, sh.h1, sh.h2, &sh.ctl[kCtlScr0]);
-    if (t == 0) sh.ctl[kCtlLKey] = max(kth, order_key(Fmt<DT>::kNegInf));
+    uint32_t lk = kNoKey;
+    if (nmax <= 512) {
+      constexpr int kSh = DT ? 0 : 2;  // bf16: one key per bin; fp16: four (same span in value)
+      bool clamped = false;
+      const uint32_t kth = warp_anchored_kth(sh.mkeys, nmax, kk, kSh, sh.h1, &clamped);
+      if (!clamped) lk = max(kth, order_key(Fmt<DT>::kNegInf));
+    }
+    if (t == 0) sh.ctl[kCtlLKey] = lk;
   }
   __syncthreads();
+  if (sh.ctl[kCtlLKey] == kNoKey) {
+    sh.h1[t] = 0u;  // (the warp's histogram may have used it)
+    __syncthreads();
+    const uint32_t kth = kth_largest_key(sh.mkeys, nmax, kk, sh.h1, sh.h2, &sh.ctl[kCtlScr0]);
+    if (t == 0) sh.ctl[kCtlLKey] = max(kth, order_key(Fmt<DT>::kNegInf));
+    __syncthreads();
+  }
   const int st = static_cast<int>(sh.ctl[kCtlStatus]);
   if (st != FS_ROW_OK) {
     // every remote access of this launch is complete (B2), so ranks may leave independently
