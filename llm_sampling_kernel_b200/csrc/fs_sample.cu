@@ -92,7 +92,6 @@ constexpr int kCtlLKey = 0;     // threshold key
 constexpr int kCtlStatus = 1;   // row status
 constexpr int kCtlLocal = 2;    // this rank's staged survivors
 constexpr int kCtlN = 3;        // survivors of the row
-constexpr int kCtlOverflow = 4; // some rank overflowed its slots
 constexpr int kCtlScr0 = 5;     // two words of block-search results
 constexpr int kCtlHb = 8;       // fallback scratch
 constexpr int kCtlAbove = 9;
@@ -105,7 +104,6 @@ constexpr uint32_t kFlagNaN = 1u, kFlagPosInf = 2u, kFlagAboveNegInf = 4u;
 struct alignas(16) Shared {
   uint32_t mkeys[kMaxMaxima]; // every rank's maxima keys; rank r at [r * mcta, (r + 1) * mcta)
   uint32_t flags[kMaxSplits]; // every rank's row flags
-  uint32_t scnt[kMaxSplits];  // leader: every rank's survivor count
   uint32_t cnt[kMaxSplits];   // fallback: per-rank counts above T
   uint32_t cnt2[kMaxSplits];  // fallback: per-rank tie counts
   uint32_t h1[256];           // threshold radix histograms
@@ -163,6 +161,12 @@ __device__ __forceinline__ uint32_t ld_dsmem(uint32_t addr) {
 }
 __device__ __forceinline__ void st_dsmem(uint32_t addr, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
+}
+// Atomic add on a word in some rank's shared memory (address from dsmem_addr); returns the old value.
+__device__ __forceinline__ uint32_t atom_add_dsmem(uint32_t addr, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.shared::cluster.add.u32 %0, [%1], %2;\n" : "=r"(old) : "r"(addr), "r"(v) : "memory");
+  return old;
 }
 __device__ __forceinline__ void st_dsmem64(uint32_t addr, uint64_t v) {
   asm volatile("st.shared::cluster.u64 [%0], %1;\n" ::"r"(addr), "l"(v) : "memory");
@@ -739,8 +743,12 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
 // Resident CTAs per SM the register budget must allow: the row slice lives in 4*C registers.
 constexpr int min_ctas_for(int C) { return C <= 10 ? 4 : (C <= 12 ? 3 : 2); }
 
+// Cluster-kernel residency: the small-chunk variants serve small batches (at most 32 rows of 16
+// CTAs), so they trade residency for registers; C = 10 serves batches up to 127 rows at 8 CTAs.
+constexpr int cluster_min_ctas(int C) { return C <= 6 ? 2 : (C <= 10 ? 3 : min_ctas_for(C)); }
+
 template <int DT, int C>
-__global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const Params p) {
+__global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(const Params p) {
   cg::cluster_group cluster = cg::this_cluster();
   const int S = static_cast<int>(cluster.num_blocks());
   const int s = static_cast<int>(cluster.block_rank());
@@ -924,14 +932,16 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
     return;
   }
 
-  // ---- phase 4: survivors (every element >= L) into this rank's slots of the leader ----
+  // ---- phase 4: survivors (every element >= L) into the leader's buffer ----
+  // The per-chunk maxima mark the chunks holding an element >= L (one packed compare per chunk);
+  // a thread takes its marked chunks out of its registers one at a time, reserves positions for
+  // the chunk's hits with one atomic on the leader's counter and stores them there, so the
+  // leader's survivors are contiguous when the cluster barrier completes.
   const uint32_t lbits = key_to_bits(lkey);
   const uint32_t l2 = lbits | (lbits << 16);
-  const uint32_t M = static_cast<uint32_t>(p.slot);
-  const uint32_t slot0 = dsmem_addr(&surv[s * M], 0);
-  // The per-chunk maxima mark the chunks holding an element >= L (one packed compare per chunk);
-  // a thread takes its marked chunks out of its registers one at a time, reserves slots for the
-  // chunk's hits with one shared atomic and stores them into its slot range of the leader.
+  const uint32_t cap = static_cast<uint32_t>(p.cap);
+  const uint32_t surv0 = dsmem_addr(surv, 0);
+  const uint32_t ctr = dsmem_addr(&sh.ctl[kCtlN], 0);
   uint32_t cm = 0u;
 #pragma unroll
   for (int c = 0; c < C; ++c) cm |= (pair_ge_mask<DT>(cp[c], l2) != 0u ? 1u : 0u) << c;
@@ -951,37 +961,20 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
     }
     if (e0 + 8 > V) hits &= (e0 < V) ? ((1u << (V - e0)) - 1u) : 0u;  // past the row end
     if (hits == 0u) continue;
-    uint32_t slot = atomicAdd(&sh.ctl[kCtlLocal], static_cast<uint32_t>(__popc(hits)));
+    uint32_t slot = atom_add_dsmem(ctr, static_cast<uint32_t>(__popc(hits)));
     while (hits != 0u) {
       const int bit = __ffs(hits) - 1;
       hits &= hits - 1u;
       const int w = bit >> 1;
       const uint32_t word = w == 0 ? x.x : w == 1 ? x.y : w == 2 ? x.z : x.w;
-      if (slot < M)
-        st_dsmem64(slot0 + 8u * slot, pack(order_key((word >> (16 * (bit & 1))) & 0xFFFFu), p.id_base + e0 + bit));
+      if (slot < cap)
+        st_dsmem64(surv0 + 8u * slot, pack(order_key((word >> (16 * (bit & 1))) & 0xFFFFu), p.id_base + e0 + bit));
       ++slot;
     }
   }
-  __syncthreads();
-  if (t == 0) st_dsmem(dsmem_addr(&sh.scnt[s], 0), sh.ctl[kCtlLocal]);
-  cluster.sync();  // B4: the leader's slots and counts are final
-  if (t < 32) {
-    uint32_t c = 0u;
-    if (t < S) c = leader ? sh.scnt[t] : ld_dsmem(dsmem_addr(&sh.scnt[t], 0));
-    const uint32_t inc = warp_incl_scan(c);
-    const unsigned over = __ballot_sync(0xFFFFFFFFu, c > M);
-    if (t < S) {
-      sh.cnt[t] = c;
-      sh.cnt2[t] = inc - c;  // exclusive prefix: first compact index of rank t
-    }
-    if (t == 31) {
-      sh.ctl[kCtlN] = inc;
-      sh.ctl[kCtlOverflow] = over != 0u ? 1u : 0u;
-    }
-  }
-  __syncthreads();
-  int n = static_cast<int>(sh.ctl[kCtlN]);
-  const bool overflow = sh.ctl[kCtlOverflow] != 0u;
+  cluster.sync();  // B4: the leader's survivors and count are final
+  int n = static_cast<int>(leader ? sh.ctl[kCtlN] : ld_dsmem(ctr));
+  const bool overflow = n > static_cast<int>(cap);  // the same decision in every rank
   if (overflow) {
     uint64_t* lsurv = cluster.map_shared_rank(surv, 0);
     n = exact_select<DT, C>(sh, row, V, p.vec, p.id_base, vbase, kk, lsurv);
@@ -992,23 +985,21 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_cluster_kernel(const P
   cluster_arrive_relaxed();
   if (!leader) return;
 
-  // ---- phases 5-7 in the leader: compact, sort, tail ----
-  if (overflow) {
-    for (int i = t; i < n; i += NT) tmp[i] = surv[i];
-  } else {
-    // slot i = r * M + j of rank r goes to compact index prefix[r] + j (M is a power of two)
-    const int mshift = __ffs(static_cast<int>(M)) - 1;
-    for (int i = t; i < S * static_cast<int>(M); i += NT) {
-      const int r = i >> mshift;
-      const int j = i & (static_cast<int>(M) - 1);
-      if (j < static_cast<int>(sh.cnt[r])) tmp[sh.cnt2[r] + j] = surv[i];
-    }
-  }
-  __syncthreads();
+  // ---- phases 5-7 in the leader: sort, tail ----
   if (p.stop == 4) {
     if (t == 0) p.out[b] = static_cast<int64_t>(n);
   } else {
-    finish_row<DT>(p, b, tmp, n, surv, kk, pp, u, prob, cum, sh);
+    // the maxima keys are dead: their space holds the sorted top kk (else the survivors move to
+    // the probability buffers, which the sort may overwrite, and the top kk goes back to surv)
+    uint64_t* src = surv;
+    uint64_t* dst = reinterpret_cast<uint64_t*>(sh.mkeys);
+    if (kk > kMaxMaxima / 2) {
+      for (int i = t; i < n; i += NT) tmp[i] = surv[i];
+      __syncthreads();
+      src = tmp;
+      dst = surv;
+    }
+    finish_row<DT>(p, b, src, n, dst, kk, pp, u, prob, cum, sh);
   }
   cluster_wait();
 }
