@@ -402,31 +402,44 @@ def run_ours(args):
 
 def run_tp(ops, world, rank, device, args):
     """C4: vocab-sharded TP through llm_sampling_kernel_b200.sharded.VocabShardedSampler: local
-    shard top-k -> NCCL all-gather of packed candidates -> merge + sample on every rank."""
+    shard top-k -> exchange of packed candidates -> merge + sample on every rank. Two exchanges:
+    the p2p kernel (pushes into every rank's buffers over NVLink, flags, bounded wait, merge in
+    the same kernel) and an NCCL all-gather followed by the merge kernel."""
     import torch.distributed as dist
 
     from llm_sampling_kernel_b200.sharded import VocabShardedSampler
 
     B, V, k, p = C4["B"], C4["V"], C4["k"], C4["p"]
-    sampler = VocabShardedSampler(vocab=V, top_k=k, ops=ops)
-    lo, hi = sampler.cols
-    full = tp_logits(B, V, device)
-    shard = full[:, lo:hi].contiguous()
-    del full
+    out = {"B": B, "V": V, "top_k": k, "top_p": p, "exchange_bytes_per_rank": B * (k + 1) * 8}
+    launches = 0
+    results = {}
+    for backend in ("p2p", "nccl"):
+        sampler = VocabShardedSampler(vocab=V, top_k=k, ops=ops, backend=backend, max_batch=B)
+        lo, hi = sampler.cols
+        full = tp_logits(B, V, device)
+        shard = full[:, lo:hi].contiguous()
+        del full
 
-    def step(i):
-        sampler.sample(shard, p, seed=0x5EED, offset=i)
+        def step(i):
+            sampler.sample(shard, p, seed=0x5EED, offset=i)
 
-    steps = max(3, min(args.steps, 200))
-    ms = timed_steps(step, steps, max(3, args.warmup), world)
-    us = max_over_ranks(ms * 1000.0 / steps, world)
-    ids, _ = sampler.sample(shard, p, seed=0x5EED, offset=0)
-    all_ids = [torch.empty_like(ids) for _ in range(world)]
-    dist.all_gather(all_ids, ids)
-    agree = all(torch.equal(all_ids[0], t) for t in all_ids)
-    return {"us_per_call": round(us, 3), "B": B, "V": V, "shard_vocab": hi - lo, "top_k": k, "top_p": p,
-            "exchange_bytes_per_rank": B * (k + 1) * 8, "ranks_agree": agree, "launches": 2 * steps,
-            "backend": "nccl all_gather_into_tensor"}
+        steps = max(3, min(args.steps, 200))
+        ms = timed_steps(step, steps, max(3, args.warmup), world)
+        us = max_over_ranks(ms * 1000.0 / steps, world)
+        launches += 2 * steps
+        ids, status = sampler.sample(shard, p, seed=0x5EED, offset=0)
+        all_ids = [torch.empty_like(ids) for _ in range(world)]
+        dist.all_gather(all_ids, ids)
+        results[backend] = (us, all(torch.equal(all_ids[0], t) for t in all_ids) and bool((status == 0).all()), ids)
+        sampler.close()
+        out["shard_vocab"] = hi - lo
+    out["us_per_call"] = round(results["p2p"][0], 3)
+    out["backend"] = "p2p: shard top-k kernel + exchange-merge kernel over NVLink peer memory"
+    out["nccl_us_per_call"] = round(results["nccl"][0], 3)
+    out["ranks_agree"] = results["p2p"][1] and results["nccl"][1]
+    out["backends_agree"] = bool(torch.equal(results["p2p"][2], results["nccl"][2]))
+    out["launches"] = launches
+    return out
 
 
 # ---------------------------------------------------------------------------------------------

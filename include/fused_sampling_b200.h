@@ -154,6 +154,43 @@ FS_API fs_status fs_shard_candidates(const fs_sample_args* args, uint64_t* cand_
 FS_API fs_status fs_merge_sample(const fs_sample_args* args, const uint64_t* cand, int32_t parts,
                           fs_stream_t stream);
 
+/* Exchange and merge without a collective library (no counterpart in the reference; the
+ * peer-to-peer form of the all-gather + fs_merge_sample pair): every rank pushes its [B, K + 1] candidate
+ * block (from fs_shard_candidates) into every rank's receive buffer over NVLink and raises one
+ * flag per (row, source rank) there, then waits for its own flags and merges. All ranks call it
+ * with the same epoch (1, 2, 3, ... per call). Buffers, set up once per process group:
+ *   recv  : device [2][world][max_batch][K + 1] uint64, flags: device [2][world][max_batch]
+ *           uint32 (zeroed before the first call),
+ *   peer_recv / peer_flags: device arrays of `world` pointers to every rank's recv / flags
+ *           (this rank's own included), mapped with fs_ipc_open.
+ * A flag that does not arrive within wait_polls polls (0 = the default, about a second) marks
+ * the row FS_ROW_TIMEOUT (id -1). Uses args: dtype, batch, top_k (K), top_p, rng, out_ids,
+ * row_status. */
+typedef struct fs_tp_peers {
+  int32_t world;
+  int32_t rank;
+  int64_t max_batch;
+  uint32_t epoch;
+  int64_t wait_polls;
+  uint64_t* recv;
+  uint32_t* flags;
+  uint64_t* const* peer_recv;
+  uint32_t* const* peer_flags;
+} fs_tp_peers;
+FS_API fs_status fs_tp_merge_sample(const fs_sample_args* args, const uint64_t* local_cand,
+                                    const fs_tp_peers* tp, fs_stream_t stream);
+
+/* CUDA IPC plumbing for the buffers above, used once at set-up: fs_ipc_alloc allocates a zeroed
+ * device buffer on the current device (its own allocation, so its address is the base an IPC
+ * handle describes), fs_ipc_handle exports it (FS_IPC_HANDLE_BYTES bytes), a peer process maps
+ * it with fs_ipc_open and unmaps it with fs_ipc_close; fs_ipc_free releases it. */
+#define FS_IPC_HANDLE_BYTES 64
+FS_API fs_status fs_ipc_alloc(uint64_t bytes, void** dev_ptr_out);
+FS_API fs_status fs_ipc_free(void* dev_ptr);
+FS_API fs_status fs_ipc_handle(const void* dev_ptr, void* handle_out);
+FS_API fs_status fs_ipc_open(const void* handle, void** dev_ptr_out);
+FS_API fs_status fs_ipc_close(void* dev_ptr);
+
 /* ---- floor probes (measurement brackets) ---------------------------------------------------
  * Replace: probe_noop / probe_scan_rowblock / probe_scan_split (csrc/probes.cu:86-125). */
 FS_API fs_status fs_probe_noop(int64_t* out, int64_t batch, fs_stream_t stream);

@@ -40,7 +40,14 @@ EXPORTED = (
     "fs_version",
     "fs_workspace_size",
     "fs_sample_noalloc",
+    "fs_tp_merge_sample",
+    "fs_ipc_alloc",
+    "fs_ipc_free",
+    "fs_ipc_handle",
+    "fs_ipc_open",
+    "fs_ipc_close",
 )
+FS_IPC_HANDLE_BYTES = 64
 FS_PATH_AUTO, FS_PATH_CLUSTER, FS_PATH_STREAM, FS_PATH_PERSIST = 0, 1, 2, 3
 
 
@@ -79,6 +86,20 @@ class FsSampleArgs(ctypes.Structure):
         ("path", ctypes.c_int32),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_uint64),
+    ]
+
+
+class FsTpPeers(ctypes.Structure):
+    _fields_ = [
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("max_batch", ctypes.c_int64),
+        ("epoch", ctypes.c_uint32),
+        ("wait_polls", ctypes.c_int64),
+        ("recv", ctypes.c_void_p),
+        ("flags", ctypes.c_void_p),
+        ("peer_recv", ctypes.c_void_p),
+        ("peer_flags", ctypes.c_void_p),
     ]
 
 
@@ -134,7 +155,14 @@ def lib() -> ctypes.CDLL:
         L.fs_workspace_size.argtypes = [P(FsSampleArgs)]
         L.fs_workspace_size.restype = ctypes.c_uint64
         L.fs_sample_noalloc.argtypes = [P(FsSampleArgs), ctypes.c_void_p]
-        for name in ("fs_sample", "fs_sample_noalloc", "fs_topk", "fs_probe_phase", "fs_shard_candidates", "fs_merge_sample",
+        L.fs_tp_merge_sample.argtypes = [P(FsSampleArgs), ctypes.c_void_p, P(FsTpPeers), ctypes.c_void_p]
+        L.fs_ipc_alloc.argtypes = [ctypes.c_uint64, P(ctypes.c_void_p)]
+        L.fs_ipc_free.argtypes = [ctypes.c_void_p]
+        L.fs_ipc_handle.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        L.fs_ipc_open.argtypes = [ctypes.c_void_p, P(ctypes.c_void_p)]
+        L.fs_ipc_close.argtypes = [ctypes.c_void_p]
+        for name in ("fs_tp_merge_sample", "fs_ipc_alloc", "fs_ipc_free", "fs_ipc_handle", "fs_ipc_open", "fs_ipc_close",
+                     "fs_sample", "fs_sample_noalloc", "fs_topk", "fs_probe_phase", "fs_shard_candidates", "fs_merge_sample",
                      "fs_probe_noop", "fs_probe_scan_rowblock", "fs_probe_scan_split", "fs_plan"):
             getattr(L, name).restype = ctypes.c_int
         _lib = L
@@ -311,3 +339,49 @@ def merge_sample(cand, bf16: bool, top_k: int, top_p: float, *, seed: int = 0, o
     a.batch = B
     check(lib().fs_merge_sample(ctypes.byref(a), _ptr(cand), parts, _stream(stream)), "fs_merge_sample")
     return out, status
+
+
+# ---- peer buffers for the tensor-parallel exchange (set-up time only) ------------------------
+
+
+class _CudaBuffer:
+    """A raw device allocation seen as a tensor (zero copy, __cuda_array_interface__)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 2}
+
+
+def ipc_alloc(shape, dtype) -> tuple:
+    """A zeroed device buffer of its own allocation on the current device: (tensor, pointer)."""
+    import torch
+
+    typestr = {torch.int64: "<i8", torch.int32: "<i4"}[dtype]
+    n = 1
+    for d in shape:
+        n *= d
+    ptr = ctypes.c_void_p()
+    check(lib().fs_ipc_alloc(n * (8 if dtype == torch.int64 else 4), ctypes.byref(ptr)), "fs_ipc_alloc")
+    t = torch.as_tensor(_CudaBuffer(ptr.value, shape, typestr), device="cuda")
+    return t, ptr.value
+
+
+def ipc_handle(ptr: int) -> bytes:
+    buf = ctypes.create_string_buffer(FS_IPC_HANDLE_BYTES)
+    check(lib().fs_ipc_handle(ctypes.c_void_p(ptr), buf), "fs_ipc_handle")
+    return buf.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    ptr = ctypes.c_void_p()
+    check(lib().fs_ipc_open(ctypes.create_string_buffer(handle, FS_IPC_HANDLE_BYTES), ctypes.byref(ptr)),
+          "fs_ipc_open")
+    return ptr.value
+
+
+def ipc_close(ptr: int) -> None:
+    check(lib().fs_ipc_close(ctypes.c_void_p(ptr)), "fs_ipc_close")
+
+
+def ipc_free(ptr: int) -> None:
+    check(lib().fs_ipc_free(ctypes.c_void_p(ptr)), "fs_ipc_free")

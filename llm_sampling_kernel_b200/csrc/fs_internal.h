@@ -35,6 +35,8 @@ void set_error(const char* fmt, ...);
 fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t path, PlanOut* out);
 fs_status run_cluster(const fs_sample_args* a, int mode, uint64_t* cand_out, cudaStream_t stream);
 fs_status run_merge(const fs_sample_args* a, const uint64_t* cand, int parts, cudaStream_t stream);
+fs_status run_tp_merge(const fs_sample_args* a, const uint64_t* local_cand, const fs_tp_peers* tp,
+                       cudaStream_t stream);
 
 // cudaFuncGetAttributes + occupancy into an fs_kernel_attr row.
 void fill_attr(const void* fn, int block, int smem, fs_kernel_attr* row);

@@ -1816,6 +1816,114 @@ __global__ void __launch_bounds__(NT) fs_merge_kernel(const Params p, const uint
 }
 
 // ------------------------------------------------------------------------------------------
+// Vocab-sharded tensor parallelism without a collective library: every rank pushes its [B, K+1]
+// candidate block straight into every peer's receive buffer over NVLink (CUDA IPC mappings, plain
+// stores), then raises one flag per (row, source rank) in every peer with a system-scope release
+// store; each rank waits for its own flags (acquire loads, bounded) and merges locally.
+// Receive buffers and flags are double-buffered by call parity: a rank can only be one call
+// ahead of a peer (its merge needs the peer's push of the same call, and the peer pushes a call
+// only after its previous merge has finished), so a slot is never overwritten while being read.
+// ------------------------------------------------------------------------------------------
+
+struct TpPeers {
+  int32_t world, rank;
+  int64_t max_batch;
+  uint32_t epoch;                  // this call's number (>= 1); its slot is epoch & 1
+  long long wait_polls;            // bound on the polls of one flag
+  uint64_t* recv;                  // local [2][world][max_batch][K + 1]
+  uint32_t* flags;                 // local [2][world][max_batch]
+  uint64_t* const* peer_recv;      // device array: every rank's recv (this rank's included)
+  uint32_t* const* peer_flags;     // device array: every rank's flags
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* ptr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* ptr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(NT) fs_tp_merge_kernel(const Params p, const uint64_t* __restrict__ local_cand,
+                                                         const TpPeers tp) {
+  Shared& sh = *reinterpret_cast<Shared*>(g_smem);
+  uint64_t* surv = reinterpret_cast<uint64_t*>(g_smem + sizeof(Shared));
+  float* prob = reinterpret_cast<float*>(surv + p.cap);
+  float* cum = prob + p.cap;
+  uint64_t* tmp = reinterpret_cast<uint64_t*>(prob);
+  const int b = blockIdx.x;
+  const int t = threadIdx.x;
+  const int W = tp.world;
+  const int K1 = p.K + 1;
+  const uint32_t slot = tp.epoch & 1u;
+  // 1. push this rank's row to every rank, then raise the row's flag there
+  for (int i = t; i < K1; i += NT) {
+    const uint64_t x = local_cand[static_cast<size_t>(b) * K1 + i];
+    for (int r = 0; r < W; ++r)
+      tp.peer_recv[r][((static_cast<size_t>(slot) * W + tp.rank) * tp.max_batch + b) * K1 + i] = x;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (t < W) st_release_sys(&tp.peer_flags[t][(static_cast<size_t>(slot) * W + tp.rank) * tp.max_batch + b], tp.epoch);
+  // 2. wait for every rank's row (bounded)
+  if (t < 32) {
+    bool ok = true;
+    if (t < W) {
+      const uint32_t* f = &tp.flags[(static_cast<size_t>(slot) * W + t) * tp.max_batch + b];
+      ok = false;
+      for (long long i = 0; i < tp.wait_polls; ++i) {
+        if (ld_acquire_sys(f) == tp.epoch) {
+          ok = true;
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+    const bool all = __all_sync(0xFFFFFFFFu, ok);
+    if (t == 0) sh.ctl[kCtlTmo] = all ? 0u : 1u;
+  }
+  __syncthreads();
+  if (sh.ctl[kCtlTmo] != 0u) {
+    write_invalid_row(p, b, FS_ROW_TIMEOUT);
+    return;
+  }
+  __threadfence();
+  // 3. merge: exact top-k over the W * K gathered candidates, then the common tail
+  int kk;
+  float pp;
+  bool bad;
+  row_params(p, b, &kk, &pp, &bad);
+  const float u = t < 32 ? row_uniform(p, b) : 0.0f;
+  const uint64_t* rows = tp.recv + static_cast<size_t>(slot) * W * tp.max_batch * K1;
+  const int n = W * p.K;
+  for (int i = t; i < n; i += NT) {
+    const int part = i / p.K, j = i - part * p.K;
+    tmp[i] = __ldcg(rows + (static_cast<size_t>(part) * tp.max_batch + b) * K1 + j);
+  }
+  if (t == 0) {
+    int nan = 0, inf = 0, neg = 0;
+    for (int part = 0; part < W; ++part) {
+      const uint64_t w = __ldcg(rows + (static_cast<size_t>(part) * tp.max_batch + b) * K1 + p.K);
+      nan |= w == FS_ROW_NAN;
+      inf |= w == FS_ROW_POSINF;
+      neg += w == FS_ROW_ALL_NEGINF;
+    }
+    const int st = bad ? FS_ROW_BAD_PARAM
+                       : nan ? FS_ROW_NAN : inf ? FS_ROW_POSINF : (neg == W ? FS_ROW_ALL_NEGINF : FS_ROW_OK);
+    sh.ctl[kCtlStatus] = static_cast<uint32_t>(st);
+  }
+  __syncthreads();
+  const int st = static_cast<int>(sh.ctl[kCtlStatus]);
+  if (st != FS_ROW_OK) {
+    write_invalid_row(p, b, st);
+    return;
+  }
+  finish_row<DT>(p, b, tmp, n, surv, kk, pp, u, prob, cum, sh);
+}
+
+// ------------------------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------------------------
 
@@ -2320,6 +2428,42 @@ fs_status run_merge(const fs_sample_args* a, const uint64_t* cand, int parts, cu
   return FS_OK;
 }
 
+fs_status run_tp_merge(const fs_sample_args* a, const uint64_t* local_cand, const fs_tp_peers* tpa,
+                       cudaStream_t stream) {
+  const int64_t K = a->top_k;
+  const int64_t n = static_cast<int64_t>(tpa->world) * K;
+  int cap = std::max(256, pow2_ceil(n));
+  if (cap > kMaxCap) {
+    set_error("world * top_k = %lld exceeds the merge capacity %d", static_cast<long long>(n), kMaxCap);
+    return FS_EUNSUPPORTED;
+  }
+  Params prm = base_params(a, K);
+  prm.vec = 0;
+  prm.cap = cap;
+  prm.mode = kModeSample;
+  TpPeers tp;
+  tp.world = tpa->world;
+  tp.rank = tpa->rank;
+  tp.max_batch = tpa->max_batch;
+  tp.epoch = tpa->epoch;
+  tp.wait_polls = tpa->wait_polls > 0 ? tpa->wait_polls : (1LL << 22);
+  tp.recv = tpa->recv;
+  tp.flags = tpa->flags;
+  tp.peer_recv = tpa->peer_recv;
+  tp.peer_flags = tpa->peer_flags;
+  const int smem = static_cast<int>(shared_bytes(cap));
+  auto fn = a->dtype == FS_BF16 ? fs_tp_merge_kernel<1> : fs_tp_merge_kernel<0>;
+  fs_status st = prepare_kernel(reinterpret_cast<KernelFn>(fn), 1, smem);
+  if (st != FS_OK) return st;
+  fn<<<static_cast<unsigned>(a->batch), NT, smem, stream>>>(prm, local_cand, tp);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("tp merge launch: %s", cudaGetErrorString(e));
+    return FS_ELAUNCH;
+  }
+  return FS_OK;
+}
+
 void append_cluster_attrs(std::vector<fs_kernel_attr>& rows) {
   for (int dt = 0; dt < 2; ++dt) {
     for (int C : kChunkOptions) {
@@ -2462,6 +2606,93 @@ extern "C" fs_status fs_merge_sample(const fs_sample_args* a, const uint64_t* ca
   }
   if (a->out_ids != nullptr && (st = fsb::check_top_p(a)) != FS_OK) return st;
   return fsb::run_merge(a, cand, parts, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" fs_status fs_tp_merge_sample(const fs_sample_args* a, const uint64_t* local_cand,
+                                        const fs_tp_peers* tp, fs_stream_t stream) {
+  fs_status st = fsb::check_common(a, false);
+  if (st != FS_OK) return st;
+  if (local_cand == nullptr || tp == nullptr || tp->world < 1 || tp->world > 32 || tp->rank < 0 ||
+      tp->rank >= tp->world || tp->recv == nullptr || tp->flags == nullptr || tp->peer_recv == nullptr ||
+      tp->peer_flags == nullptr || tp->epoch == 0u || a->batch > tp->max_batch) {
+    fsb::set_error("invalid tensor-parallel exchange arguments (world 1..32, rank < world, buffers set, "
+                   "epoch >= 1, batch <= max_batch)");
+    return FS_EINVAL;
+  }
+  if (a->out_ids == nullptr) {
+    fsb::set_error("out_ids is NULL");
+    return FS_EINVAL;
+  }
+  if ((st = fsb::check_top_p(a)) != FS_OK) return st;
+  return fsb::run_tp_merge(a, local_cand, tp, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" fs_status fs_ipc_alloc(uint64_t bytes, void** dev_ptr_out) {
+  if (bytes == 0 || dev_ptr_out == nullptr) {
+    fsb::set_error("bytes is 0 or dev_ptr_out is NULL");
+    return FS_EINVAL;
+  }
+  cudaError_t e = cudaMalloc(dev_ptr_out, bytes);
+  if (e == cudaSuccess) e = cudaMemset(*dev_ptr_out, 0, bytes);
+  if (e != cudaSuccess) {
+    fsb::set_error("peer buffer of %llu bytes: %s", static_cast<unsigned long long>(bytes), cudaGetErrorString(e));
+    return FS_ELAUNCH;
+  }
+  return FS_OK;
+}
+
+extern "C" fs_status fs_ipc_free(void* dev_ptr) {
+  if (dev_ptr == nullptr) return FS_OK;
+  const cudaError_t e = cudaFree(dev_ptr);
+  if (e != cudaSuccess) {
+    fsb::set_error("cudaFree: %s", cudaGetErrorString(e));
+    return FS_ELAUNCH;
+  }
+  return FS_OK;
+}
+
+extern "C" fs_status fs_ipc_handle(const void* dev_ptr, void* handle_out) {
+  if (dev_ptr == nullptr || handle_out == nullptr) {
+    fsb::set_error("dev_ptr or handle_out is NULL");
+    return FS_EINVAL;
+  }
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr));
+  if (e != cudaSuccess) {
+    fsb::set_error("cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+    return FS_ELAUNCH;
+  }
+  static_assert(sizeof(h) == FS_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle_out, &h, sizeof(h));
+  return FS_OK;
+}
+
+extern "C" fs_status fs_ipc_open(const void* handle, void** dev_ptr_out) {
+  if (handle == nullptr || dev_ptr_out == nullptr) {
+    fsb::set_error("handle or dev_ptr_out is NULL");
+    return FS_EINVAL;
+  }
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(dev_ptr_out, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    fsb::set_error("cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+    return FS_ELAUNCH;
+  }
+  return FS_OK;
+}
+
+extern "C" fs_status fs_ipc_close(void* dev_ptr) {
+  if (dev_ptr == nullptr) {
+    fsb::set_error("dev_ptr is NULL");
+    return FS_EINVAL;
+  }
+  const cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  if (e != cudaSuccess) {
+    fsb::set_error("cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
+    return FS_ELAUNCH;
+  }
+  return FS_OK;
 }
 
 extern "C" uint64_t fs_workspace_size(const fs_sample_args* a) { return fsb::workspace_size(a); }

@@ -330,6 +330,58 @@ std::vector<torch::Tensor> merge_sample(torch::Tensor cand, bool bf16, int64_t t
   return {out, status};
 }
 
+// Peer-to-peer exchange + merge (fs_tp_merge_sample): local_cand [B, K + 1] from
+// shard_candidates; recv [2, world, max_batch, K + 1] int64 and flags [2, world, max_batch] int32
+// on this rank's GPU; peer_recv / peer_flags: int64 cuda [world] tensors of device pointers.
+std::vector<torch::Tensor> tp_merge(torch::Tensor local_cand, bool bf16, int64_t top_k, double top_p,
+                                    torch::Tensor recv, torch::Tensor flags, torch::Tensor peer_recv,
+                                    torch::Tensor peer_flags, int64_t world, int64_t rank, int64_t epoch,
+                                    std::optional<torch::Tensor> uniforms, int64_t seed, int64_t offset,
+                                    int64_t row_base, int64_t wait_polls) {
+  TORCH_CHECK(local_cand.is_cuda() && local_cand.dim() == 2 && local_cand.is_contiguous() &&
+                  local_cand.scalar_type() == at::kLong && local_cand.size(1) == top_k + 1,
+              "local_cand must be a contiguous int64 cuda [B, top_k + 1] tensor");
+  TORCH_CHECK(recv.is_cuda() && recv.dim() == 4 && recv.is_contiguous() && recv.scalar_type() == at::kLong &&
+                  recv.size(0) == 2 && recv.size(1) == world && recv.size(3) == top_k + 1,
+              "recv must be a contiguous int64 cuda [2, world, max_batch, top_k + 1] tensor");
+  TORCH_CHECK(flags.is_cuda() && flags.dim() == 3 && flags.is_contiguous() && flags.scalar_type() == at::kInt &&
+                  flags.size(0) == 2 && flags.size(1) == world && flags.size(2) == recv.size(2),
+              "flags must be a contiguous int32 cuda [2, world, max_batch] tensor");
+  TORCH_CHECK(peer_recv.is_cuda() && peer_recv.numel() == world && peer_recv.scalar_type() == at::kLong &&
+                  peer_flags.is_cuda() && peer_flags.numel() == world && peer_flags.scalar_type() == at::kLong,
+              "peer_recv / peer_flags must be int64 cuda [world] tensors of device pointers");
+  check_top_k(top_k);
+  check_top_p(top_p);
+  c10::cuda::CUDAGuard guard(local_cand.device());
+  const int64_t B = local_cand.size(0);
+  auto out = empty_i64(local_cand, {B});
+  auto status = torch::empty({B}, local_cand.options().dtype(torch::kInt32));
+  fs_sample_args a = {};
+  a.dtype = bf16 ? FS_BF16 : FS_F16;
+  a.batch = B;
+  a.top_k = top_k;
+  a.top_p = narrow_top_p(top_p);
+  fill_rows(&a, local_cand, std::nullopt, std::nullopt, uniforms, B);
+  if (!uniforms.has_value()) set_rng(&a.rng, seed, offset);
+  a.rng.row_base = row_base;
+  a.out_ids = out.data_ptr<int64_t>();
+  a.row_status = status.data_ptr<int32_t>();
+  fs_tp_peers tp = {};
+  tp.world = static_cast<int32_t>(world);
+  tp.rank = static_cast<int32_t>(rank);
+  tp.max_batch = recv.size(2);
+  tp.epoch = static_cast<uint32_t>(epoch);
+  tp.wait_polls = wait_polls;
+  tp.recv = reinterpret_cast<uint64_t*>(recv.data_ptr<int64_t>());
+  tp.flags = reinterpret_cast<uint32_t*>(flags.data_ptr<int32_t>());
+  tp.peer_recv = reinterpret_cast<uint64_t* const*>(peer_recv.data_ptr<int64_t>());
+  tp.peer_flags = reinterpret_cast<uint32_t* const*>(peer_flags.data_ptr<int64_t>());
+  check(fs_tp_merge_sample(&a, reinterpret_cast<const uint64_t*>(local_cand.data_ptr<int64_t>()), &tp,
+                           current_stream()),
+        "fs_tp_merge_sample");
+  return {out, status};
+}
+
 std::tuple<int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t> plan(
     int64_t batch, int64_t vocab, int64_t top_k, int64_t splits) {
   fs_plan_info p = {};
@@ -359,6 +411,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("top_k_rows") = py::none(), py::arg("top_p_rows") = py::none(),
         py::arg("uniforms") = py::none(), py::arg("seed") = 0, py::arg("offset") = -1,
         py::arg("row_base") = 0);
+  m.def("tp_merge", &tp_merge, "vocab-shard exchange over peer memory + merge + sample",
+        py::arg("local_cand"), py::arg("bf16"), py::arg("top_k"), py::arg("top_p"), py::arg("recv"),
+        py::arg("flags"), py::arg("peer_recv"), py::arg("peer_flags"), py::arg("world"), py::arg("rank"),
+        py::arg("epoch"), py::arg("uniforms") = py::none(), py::arg("seed") = 0, py::arg("offset") = -1,
+        py::arg("row_base") = 0, py::arg("wait_polls") = 0);
   m.def("plan", &plan,
         "launch plan (splits, chunks, threads, capacity, maxima/thread, lanes/max, smem, path, workspace)");
   m.attr("NUM_PHASES") = FS_NUM_PHASES;

@@ -75,13 +75,23 @@ class BatchShardedSampler:
 
 @dataclass
 class VocabShardedSampler:
-    """Samples rows whose vocabulary is split contiguously across the ranks of `group`."""
+    """Samples rows whose vocabulary is split contiguously across the ranks of `group`.
+
+    backend="nccl": all-gather of the [B, K+1] candidate blocks through NCCL, then the merge.
+    backend="p2p": one kernel per rank pushes its block into every rank's receive buffer over
+    NVLink (CUDA IPC mappings made once, at the first call, for up to `max_batch` rows), raises a
+    flag per row there, waits for its own flags (bounded) and merges; no collective library on the
+    data path. Call close() (every rank) before destroying the process group.
+    """
 
     vocab: int
     top_k: int
     group: Optional[dist.ProcessGroup] = None
     ops: object = None
     bf16: bool = True
+    backend: str = "nccl"
+    max_batch: int = 64
+    wait_polls: int = 0
 
     def __post_init__(self):
         self.world = dist.get_world_size(self.group) if dist.is_initialized() else 1
@@ -93,7 +103,54 @@ class VocabShardedSampler:
             raise ValueError(f"top_k {self.top_k} exceeds the shard width {hi - lo}")
         if self.ops is None:
             self.ops = _default_ops()
+        if self.backend not in ("nccl", "p2p"):
+            raise ValueError(f"backend must be 'nccl' or 'p2p', got {self.backend!r}")
         self._gathered = None
+        self._p2p = None
+
+    def _setup_p2p(self, device):
+        from . import abi
+
+        W, K1 = self.world, self.top_k + 1
+        with torch.cuda.device(device):
+            recv, recv_ptr = abi.ipc_alloc((2, W, self.max_batch, K1), torch.int64)
+            flags, flags_ptr = abi.ipc_alloc((2, W, self.max_batch), torch.int32)
+            torch.cuda.synchronize(device)
+            mine = (abi.ipc_handle(recv_ptr), abi.ipc_handle(flags_ptr))
+            handles = [None] * W
+            dist.all_gather_object(handles, mine, group=self.group)
+            opened, recv_ptrs, flag_ptrs = [], [], []
+            for r in range(W):
+                if r == self.rank:
+                    recv_ptrs.append(recv_ptr)
+                    flag_ptrs.append(flags_ptr)
+                else:
+                    rp, fp = abi.ipc_open(handles[r][0]), abi.ipc_open(handles[r][1])
+                    opened += [rp, fp]
+                    recv_ptrs.append(rp)
+                    flag_ptrs.append(fp)
+            peer_recv = torch.tensor(recv_ptrs, dtype=torch.int64, device=device)
+            peer_flags = torch.tensor(flag_ptrs, dtype=torch.int64, device=device)
+        # every rank has mapped every buffer before any rank pushes into one
+        dist.barrier(group=self.group)
+        self._p2p = dict(recv=recv, flags=flags, own=(recv_ptr, flags_ptr), opened=opened,
+                         peer_recv=peer_recv, peer_flags=peer_flags, epoch=0)
+
+    def close(self):
+        """Unmaps the peers' buffers and frees this rank's (p2p backend); collective."""
+        if self._p2p is None:
+            return
+        from . import abi
+
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # no peer still writes into this rank's buffers
+        for ptr in self._p2p["opened"]:
+            abi.ipc_close(ptr)
+        dist.barrier(group=self.group)  # no peer still maps this rank's buffers
+        recv_ptr, flags_ptr = self._p2p["own"]
+        self._p2p = None
+        abi.ipc_free(recv_ptr)
+        abi.ipc_free(flags_ptr)
 
     def local_candidates(self, shard_logits: torch.Tensor) -> torch.Tensor:
         lo, hi = self.cols
@@ -118,6 +175,18 @@ class VocabShardedSampler:
     def sample(self, shard_logits: torch.Tensor, top_p: float, *, seed: int, offset: int,
                uniforms: Optional[torch.Tensor] = None, row_base: int = 0):
         """Returns (ids [B], status [B]); identical on every rank."""
+        if self.backend == "p2p":
+            B = shard_logits.shape[0]
+            if B > self.max_batch:
+                raise ValueError(f"batch {B} exceeds max_batch {self.max_batch} of the p2p buffers")
+            if self._p2p is None:
+                self._setup_p2p(shard_logits.device)
+            st = self._p2p
+            st["epoch"] += 1
+            cand = self.local_candidates(shard_logits)
+            return self.ops.tp_merge(cand, self.bf16, self.top_k, top_p, st["recv"], st["flags"], st["peer_recv"],
+                                     st["peer_flags"], self.world, self.rank, st["epoch"], uniforms, seed, offset,
+                                     row_base, self.wait_polls)
         gathered = self.exchange(self.local_candidates(shard_logits))
         ids, status = self.ops.merge_sample(gathered, self.bf16, self.top_k, top_p, None, None, uniforms, seed,
                                             offset, row_base)

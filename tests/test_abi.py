@@ -41,7 +41,7 @@ def test_struct_layout_matches_the_header(tmp_path):
     if cc is None:
         pytest.skip("no C compiler")
     structs = {"fs_sample_args": abi.FsSampleArgs, "fs_rng": abi.FsRng, "fs_kernel_attr": abi.FsKernelAttr,
-               "fs_plan_info": abi.FsPlanInfo}
+               "fs_plan_info": abi.FsPlanInfo, "fs_tp_peers": abi.FsTpPeers}
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void) {"]
     for cname, cls in structs.items():
         lines.append(f'printf("{cname} sizeof %zu\\n", sizeof({cname}));')
@@ -180,3 +180,24 @@ def test_unknown_paths_and_unsupported_forced_paths_are_rejected():
     a.top_k, a.vocab, a.row_stride = 50, 151935, 151935
     assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EUNSUPPORTED
     assert "multiple of 8" in lib.fs_last_error().decode()
+
+
+def test_peer_exchange_arguments_are_checked_before_any_launch():
+    lib = abi.lib()
+    a = abi.FsSampleArgs()
+    a.dtype, a.batch, a.vocab, a.row_stride, a.top_k, a.top_p = abi.FS_BF16, 4, 128000, 128000, 64, 0.9
+    a.out_ids = 0x2000
+    tp = abi.FsTpPeers()
+    tp.world, tp.rank, tp.max_batch, tp.epoch = 2, 0, 4, 1
+    tp.recv, tp.flags, tp.peer_recv, tp.peer_flags = 0x3000, 0x4000, 0x5000, 0x6000
+    assert lib.fs_tp_merge_sample(ctypes.byref(a), None, ctypes.byref(tp), None) == abi.FS_EINVAL
+    cand = 0x7000
+    for field, bad in (("rank", 2), ("epoch", 0), ("max_batch", 3), ("world", 0), ("recv", None)):
+        saved = getattr(tp, field)
+        setattr(tp, field, bad)
+        assert lib.fs_tp_merge_sample(ctypes.byref(a), cand, ctypes.byref(tp), None) == abi.FS_EINVAL, field
+        setattr(tp, field, saved)
+    assert "epoch" in lib.fs_last_error().decode()
+    assert lib.fs_ipc_handle(None, None) == abi.FS_EINVAL
+    assert lib.fs_ipc_open(None, None) == abi.FS_EINVAL
+    assert lib.fs_ipc_close(None) == abi.FS_EINVAL

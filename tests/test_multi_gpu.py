@@ -5,8 +5,9 @@ the unsharded single-GPU call:
 
 * batch-sharded rows (no collective on the data path, ids all-gathered for the check) draw exactly
   what one GPU draws over the whole batch, because the uniform is evaluated at the global row;
-* vocab-sharded tensor parallelism (local top-k as packed candidates, NCCL all-gather, merge on
-  every rank) gives identical ids on both ranks, equal to the unsharded call.
+* vocab-sharded tensor parallelism (local top-k as packed candidates, exchanged by an NCCL
+  all-gather or pushed into every rank's buffers over NVLink by the p2p kernel, merge on every
+  rank) gives identical ids on both ranks, equal to the unsharded call.
 """
 
 import datetime
@@ -50,16 +51,18 @@ def _worker(rank, world, port):
         # vocab-sharded tensor parallelism
         B, V = 32, 256000
         full = (torch.randn(B, V, generator=g) * 2.5).to(torch.bfloat16).to(dev)
-        tp = VocabShardedSampler(vocab=V, top_k=64)
-        c0, c1 = tp.cols
-        for off in range(3):
-            tids, status = tp.sample(full[:, c0:c1].contiguous(), 0.9, seed=11, offset=off)
-            ref = ops().sample_ex(full, 64, 0.9, None, None, None, 11, off, 0, 0, 0, False)[0]
-            assert torch.equal(tids, ref), "vocab-sharded ids differ from the unsharded call"
-            assert (status == 0).all()
-            others = [torch.empty_like(tids) for _ in range(world)]
-            dist.all_gather(others, tids)
-            assert all(torch.equal(o, tids) for o in others), "ranks disagree"
+        for backend in ("nccl", "p2p"):
+            tp = VocabShardedSampler(vocab=V, top_k=64, backend=backend)
+            c0, c1 = tp.cols
+            for off in range(5):
+                tids, status = tp.sample(full[:, c0:c1].contiguous(), 0.9, seed=11, offset=off)
+                ref = ops().sample_ex(full, 64, 0.9, None, None, None, 11, off, 0, 0, 0, False)[0]
+                assert torch.equal(tids, ref), f"vocab-sharded ids ({backend}) differ from the unsharded call"
+                assert (status == 0).all()
+                others = [torch.empty_like(tids) for _ in range(world)]
+                dist.all_gather(others, tids)
+                assert all(torch.equal(o, tids) for o in others), "ranks disagree"
+            tp.close()
         torch.cuda.synchronize()
         dist.barrier()
     finally:
