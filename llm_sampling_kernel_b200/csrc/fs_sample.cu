@@ -1128,6 +1128,10 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_slice_kernel(const Par
   const uint32_t M = static_cast<uint32_t>(p.slot);
   Shared& sh = *reinterpret_cast<Shared*>(g_smem);
 
+  // programmatic dependent launch: wait for the stream's previous kernel before reading, and let
+  // the row merge launch once every slice CTA has started (it waits for this grid to finish)
+  grid_dependency_wait();
+  grid_launch_dependents();
   int kk;
   float pp;
   bool bad;
@@ -1305,6 +1309,10 @@ __global__ void __launch_bounds__(NT) fs_rowmerge_kernel(const Params p, const u
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int b = blockIdx.x * static_cast<int>(blockDim.x >> 5) + warp;
+  // the slices' lists are complete only when the slice grid is: wait for it, then let the next
+  // kernel of the stream start launching
+  grid_dependency_wait();
+  grid_launch_dependents();
   if (b >= B) return;  // whole warp
   const uint32_t M = static_cast<uint32_t>(p.slot);
   const int capn = p.cap;
@@ -2302,8 +2310,17 @@ static fs_status launch_stream(const fs_sample_args* a, const PlanOut& plan, con
   }
   fs_status st = prepare_kernel(reinterpret_cast<KernelFn>(sfn), 1, plan.smem);
   if (st != FS_OK) return st;
-  sfn<<<dim3(plan.splits, static_cast<unsigned>(a->batch)), NT, plan.smem, stream>>>(prm, cand, cnt);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchAttribute pdl[1];
+  pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t scfg = {};
+  scfg.gridDim = dim3(plan.splits, static_cast<unsigned>(a->batch), 1);
+  scfg.blockDim = dim3(NT, 1, 1);
+  scfg.dynamicSmemBytes = plan.smem;
+  scfg.stream = stream;
+  scfg.attrs = pdl;
+  scfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&scfg, sfn, prm, cand, cnt);
   if (e != cudaSuccess) {
     set_error("slice launch: %s", cudaGetErrorString(e));
     return FS_ELAUNCH;
@@ -2314,8 +2331,15 @@ static fs_status launch_stream(const fs_sample_args* a, const PlanOut& plan, con
   mp.cap = plan.merge_cap;
   const int mw = merge_warps(plan.merge_cap, static_cast<int>(prm.K));
   const unsigned mgrid = static_cast<unsigned>((a->batch + mw - 1) / mw);
-  mfn<<<mgrid, 32 * mw, plan.merge_smem, stream>>>(mp, cand, cnt, plan.splits, static_cast<int>(a->batch));
-  e = cudaGetLastError();
+  cudaLaunchConfig_t mcfg = {};
+  mcfg.gridDim = dim3(mgrid, 1, 1);
+  mcfg.blockDim = dim3(32 * mw, 1, 1);
+  mcfg.dynamicSmemBytes = plan.merge_smem;
+  mcfg.stream = stream;
+  mcfg.attrs = pdl;
+  mcfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&mcfg, mfn, static_cast<const Params>(mp), static_cast<const uint64_t*>(cand),
+                         static_cast<const uint32_t*>(cnt), plan.splits, static_cast<int>(a->batch));
   if (e != cudaSuccess) {
     set_error("row-merge launch: %s", cudaGetErrorString(e));
     return FS_ELAUNCH;
@@ -2501,6 +2525,15 @@ void append_cluster_attrs(std::vector<fs_kernel_attr>& rows) {
       fill_attr(reinterpret_cast<const void*>(dt ? fs_rowstream_kernel<1> : fs_rowstream_kernel<0>), NT,
                 static_cast<int>(sizeof(Shared) + kRingOffset + 5 * kStageBytes + 1024 * 24 + NT * kStageChunks),
                 &r);
+      rows.push_back(r);
+    }
+    {
+      fs_kernel_attr r = {};
+      std::snprintf(r.name, sizeof(r.name), "fs_tp_merge_kernel<%s>", dt ? "bf16" : "fp16");
+      r.param = 0;
+      r.block = NT;
+      fill_attr(reinterpret_cast<const void*>(dt ? fs_tp_merge_kernel<1> : fs_tp_merge_kernel<0>), NT,
+                static_cast<int>(shared_bytes(256)), &r);
       rows.push_back(r);
     }
     fs_kernel_attr r = {};
