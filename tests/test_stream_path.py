@@ -4,7 +4,7 @@ PERSIST (one CTA per SM streaming whole rows through bulk-copied shared-memory s
 Each must give exactly what the cluster path gives: the same top-k set and order (checked against
 the oracle), and, because all end in the same row tail over the same candidates, the same ids,
 keep mask, renormed probabilities and row status, bit for bit. `path=` forces a path at any batch
-(k <= 256); batches of 128 rows and more take STREAM by default when k <= 128.
+(k <= 256); batches of 192 rows and more take STREAM by default when k <= 128.
 """
 
 import numpy as np
@@ -246,12 +246,12 @@ def test_nan_and_inf_in_a_late_stage_are_reported():
 
 
 def test_vocab_shard_candidates_from_the_streaming_path_merge_exactly():
-    x = dev_randn(128, 256000, 2.5, torch.bfloat16, seed=4)
-    u = torch.rand(128, generator=torch.Generator().manual_seed(3)).cuda()
+    x = dev_randn(192, 256000, 2.5, torch.bfloat16, seed=4)
+    u = torch.rand(192, generator=torch.Generator().manual_seed(3)).cuda()
     want = run(x, 64, 0.9, CLUSTER, uniforms=u)[0]
     ops = fused.ops()
     world, vs = 4, 64000
-    assert abi.plan(128, vs, 64).path == STREAM
+    assert abi.plan(192, vs, 64).path == STREAM
     parts = [ops.shard_candidates(x[:, r * vs:(r + 1) * vs], 64, r * vs) for r in range(world)]
     ids, status = ops.merge_sample(torch.stack(parts), True, 64, 0.9, uniforms=u)
     assert torch.equal(ids, want)
