@@ -109,28 +109,61 @@ class VocabShardedSampler:
         self._p2p = None
 
     def _setup_p2p(self, device):
+        """Allocates this rank's buffers, exchanges IPC handles and maps every peer's. Every rank
+        reaches every collective here; a failure on any rank raises RuntimeError on all of them."""
         from . import abi
 
         W, K1 = self.world, self.top_k + 1
-        with torch.cuda.device(device):
-            recv, recv_ptr = abi.ipc_alloc((2, W, self.max_batch, K1), torch.int64)
-            flags, flags_ptr = abi.ipc_alloc((2, W, self.max_batch), torch.int32)
-            torch.cuda.synchronize(device)
-            mine = (abi.ipc_handle(recv_ptr), abi.ipc_handle(flags_ptr))
-            handles = [None] * W
-            dist.all_gather_object(handles, mine, group=self.group)
-            opened, recv_ptrs, flag_ptrs = [], [], []
-            for r in range(W):
-                if r == self.rank:
-                    recv_ptrs.append(recv_ptr)
-                    flag_ptrs.append(flags_ptr)
-                else:
-                    rp, fp = abi.ipc_open(handles[r][0]), abi.ipc_open(handles[r][1])
-                    opened += [rp, fp]
-                    recv_ptrs.append(rp)
-                    flag_ptrs.append(fp)
-            peer_recv = torch.tensor(recv_ptrs, dtype=torch.int64, device=device)
-            peer_flags = torch.tensor(flag_ptrs, dtype=torch.int64, device=device)
+
+        def agree(ok: bool, what: str):
+            oks = [None] * W
+            dist.all_gather_object(oks, ok, group=self.group)
+            if not all(oks):
+                raise RuntimeError(f"p2p exchange set-up failed on rank(s) "
+                                   f"{[r for r, o in enumerate(oks) if not o]} while {what}")
+
+        own, opened, handles = [], [], None
+        try:
+            with torch.cuda.device(device):
+                try:
+                    recv, recv_ptr = abi.ipc_alloc((2, W, self.max_batch, K1), torch.int64)
+                    own.append(recv_ptr)
+                    flags, flags_ptr = abi.ipc_alloc((2, W, self.max_batch), torch.int32)
+                    own.append(flags_ptr)
+                    torch.cuda.synchronize(device)
+                    mine = (abi.ipc_handle(recv_ptr), abi.ipc_handle(flags_ptr))
+                    ok = True
+                except Exception:
+                    mine, ok = None, False
+                handles = [None] * W
+                dist.all_gather_object(handles, mine, group=self.group)
+                agree(ok and all(h is not None for h in handles), "exporting buffers")
+                recv_ptrs, flag_ptrs = [], []
+                try:
+                    for r in range(W):
+                        if r == self.rank:
+                            recv_ptrs.append(recv_ptr)
+                            flag_ptrs.append(flags_ptr)
+                        else:
+                            rp = abi.ipc_open(handles[r][0])
+                            opened.append(rp)
+                            fp = abi.ipc_open(handles[r][1])
+                            opened.append(fp)
+                            recv_ptrs.append(rp)
+                            flag_ptrs.append(fp)
+                    ok = True
+                except Exception:
+                    ok = False
+                agree(ok, "mapping peer buffers")
+                peer_recv = torch.tensor(recv_ptrs, dtype=torch.int64, device=device)
+                peer_flags = torch.tensor(flag_ptrs, dtype=torch.int64, device=device)
+        except Exception:
+            for ptr in opened:
+                abi.ipc_close(ptr)
+            dist.barrier(group=self.group)  # no peer still maps this rank's buffers
+            for ptr in own:
+                abi.ipc_free(ptr)
+            raise
         # every rank has mapped every buffer before any rank pushes into one
         dist.barrier(group=self.group)
         self._p2p = dict(recv=recv, flags=flags, own=(recv_ptr, flags_ptr), opened=opened,
