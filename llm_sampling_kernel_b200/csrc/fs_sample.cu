@@ -1349,17 +1349,34 @@ __global__ void __launch_bounds__(NT) fs_rowmerge_kernel(const Params p, const u
 #pragma unroll
   for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0u;
   __syncwarp();
-  // gather every slot in use (independent L2 loads) and the high-byte histogram of the keys
+  // gather every slot in use and the high-byte histogram of the keys: pairs of slots (M is even)
+  // in batches of 8 independent 16-byte L2 loads per lane, issued before any is used
   const uint64_t* rowc = cand + static_cast<size_t>(b) * S * M;
+  const ulonglong2* rc2 = reinterpret_cast<const ulonglong2*>(rowc);
   const int mshift = __ffs(static_cast<int>(M)) - 1;
-  const uint32_t slots = static_cast<uint32_t>(S) * M;
-#pragma unroll 4
-  for (uint32_t i = lane; i < slots; i += 32) {
-    const uint32_t r = i >> mshift, j = i & (M - 1u);
-    if (j < offs_cnt[r]) {
-      const uint64_t x = __ldcg(rowc + i);
-      g[offs_cnt[16 + r] + j] = x;
-      atomicAdd(&hist[packed_key(x) >> 8], 1u);
+  const uint32_t pairs = static_cast<uint32_t>(S) * M / 2u;
+  for (uint32_t base = 0; base < pairs; base += 32u * 8u) {
+    ulonglong2 x[8];
+    uint32_t rj[8];  // slice << 16 | slot in the slice, or ~0u for a pair not in use
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const uint32_t q = base + lane + 32u * u;
+      const uint32_t r = (2u * q) >> mshift, j = (2u * q) & (M - 1u);
+      const bool ok = q < pairs && j < offs_cnt[r & 15u];
+      rj[u] = ok ? (r << 16 | j) : ~0u;
+      if (ok) x[u] = __ldcg(rc2 + q);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (rj[u] == ~0u) continue;
+      const uint32_t r = rj[u] >> 16, j = rj[u] & 0xFFFFu;
+      const uint32_t o = offs_cnt[16 + r] + j;
+      g[o] = x[u].x;
+      atomicAdd(&hist[packed_key(x[u].x) >> 8], 1u);
+      if (j + 1u < offs_cnt[r]) {
+        g[o + 1] = x[u].y;
+        atomicAdd(&hist[packed_key(x[u].y) >> 8], 1u);
+      }
     }
   }
   __syncwarp();
