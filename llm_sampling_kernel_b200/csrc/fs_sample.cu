@@ -88,6 +88,9 @@ constexpr int kModeShard = 2;
 
 // ctl[] slots (per CTA)
 constexpr int kCtlFlags = 14;   // this rank's row flags
+// uscr[16 + w]: warp w's row flags, written before the CTA's first barrier (no zeroing needed,
+// unlike a shared counter whose zeroing would race with other warps' updates before that barrier)
+constexpr int kUscrFlags = 16;
 constexpr int kCtlLKey = 0;     // threshold key
 constexpr int kCtlStatus = 1;   // row status
 constexpr int kCtlLocal = 2;    // this rank's staged survivors
@@ -238,27 +241,29 @@ __device__ uint32_t kth_largest_key(const uint32_t* keys, int n, int kk, uint32_
   return result[0];
 }
 
-// A lower bound L on the want-th largest of the n 16-bit keys in shared memory: one 256-bin
-// histogram anchored at the largest key (bin = (max - key) >> sh, clamped to the last bin), the
-// boundary found by one warp scan, L = the lower edge of the boundary bin. With sh == 0 and the
-// boundary below the last bin, L is exactly the want-th largest key. At least `want` keys are
-// >= L. Returns 0 when n < want. h: 256 zeroed shared words; scratch: >= 9 shared words. Every
-// thread of the CTA calls it.
-__device__ uint32_t anchored_threshold(const uint32_t* keys, int n, int want, int sh, uint32_t* h,
+// A lower bound L on the want-th largest of the CTA's 16-bit keys, nk <= 8 per thread in
+// registers: one 256-bin histogram anchored at the largest key (bin = (max - key) >> sh, clamped
+// to the last bin), the boundary found by one warp scan, L = the lower edge of the boundary bin.
+// With sh == 0 and the boundary below the last bin, L is exactly the want-th largest key. At
+// least `want` keys are >= L. Returns 0 when the CTA holds fewer than `want` keys. h: 256 shared
+// words, zeroed by the caller before the call (the call's first barrier publishes that);
+// scratch: >= 9 shared words. Every thread of the CTA calls it; three barriers.
+__device__ uint32_t anchored_threshold(const uint32_t (&keys)[8], int nk, int want, int sh, uint32_t* h,
                                        uint32_t* scratch) {
   const int t = threadIdx.x;
   uint32_t m = 0u;
-  for (int i = t; i < n; i += NT) m = max(m, keys[i]);
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (i < nk) m = max(m, keys[i]);
   m = __reduce_max_sync(0xFFFFFFFFu, m);
   if ((t & 31) == 0) scratch[t >> 5] = m;
   __syncthreads();
   uint32_t kmax = 0u;
 #pragma unroll
   for (int w = 0; w < NT / 32; ++w) kmax = max(kmax, scratch[w]);
-  for (int i = t; i < n; i += NT) {
-    const uint32_t bin = min(255u, (kmax - keys[i]) >> sh);
-    atomicAdd(&h[255u - bin], 1u);  // reversed so that the top of the histogram is the largest key
-  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (i < nk) atomicAdd(&h[255u - min(255u, (kmax - keys[i]) >> sh)], 1u);  // top bin = largest key
   __syncthreads();
   if (t < 32) {
     uint32_t idx = 0u, above = 0u, L = 0u;
@@ -869,7 +874,8 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
     }
     sh.mkeys[mbase + i] = order_key(bits);
   }
-  if (flags != 0u) atomicOr(&sh.ctl[kCtlFlags], flags);
+  flags = __reduce_or_sync(0xFFFFFFFFu, flags);
+  if ((t & 31) == 0) sh.uscr[kUscrFlags + (t >> 5)] = flags;
   __syncthreads();
   cluster_wait();  // B1: every rank of the cluster is running
   {
@@ -881,7 +887,12 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
       const int r = ro < s ? ro : ro + 1;
       st_dsmem(dsmem_addr(&sh.mkeys[own + j], static_cast<uint32_t>(r)), sh.mkeys[own + j]);
     }
-    if (t < S) st_dsmem(dsmem_addr(&sh.flags[s], static_cast<uint32_t>(t)), sh.ctl[kCtlFlags]);
+    if (t < S) {
+      uint32_t f = 0u;
+#pragma unroll
+      for (int w = 0; w < NT / 32; ++w) f |= sh.uscr[kUscrFlags + w];
+      st_dsmem(dsmem_addr(&sh.flags[s], static_cast<uint32_t>(t)), f);
+    }
   }
   cluster.sync();  // B2: every rank holds every rank's maxima and flags
   if (p.stop == 2) {
@@ -1195,6 +1206,7 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_slice_kernel(const Par
     nm = 1;
   }
   uint32_t flags = 0u;
+  uint32_t mk[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     if (i >= nm) break;
@@ -1205,14 +1217,15 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_slice_kernel(const Par
       if (bits == Fmt<DT>::kPosInf) flags |= kFlagPosInf;
       if (bits != Fmt<DT>::kNegInf) flags |= kFlagAboveNegInf;
     }
-    sh.mkeys[t * nm + i] = order_key(bits);
+    mk[i] = order_key(bits);
   }
-  if (flags != 0u) atomicOr(&sh.ctl[kCtlFlags], flags);
-  __syncthreads();
+  flags = __reduce_or_sync(0xFFFFFFFFu, flags);
+  if ((t & 31) == 0) sh.uscr[kUscrFlags + (t >> 5)] = flags;
 
-  // L_s: at most kk of this slice's elements lie above the kk-th largest of its maxima
+  // L_s: at most kk of this slice's elements lie above the kk-th largest of its maxima (the
+  // threshold's first barrier also publishes the zeroed histogram and counters, and the flags)
   constexpr int kSh = DT ? 0 : 2;  // bf16: one key per bin; fp16: four (same span in value)
-  const uint32_t kth = anchored_threshold(sh.mkeys, NT * nm, kk, kSh, sh.h1, sh.uscr);
+  const uint32_t kth = anchored_threshold(mk, nm, kk, kSh, sh.h1, sh.uscr);
   const uint32_t lkey = max(kth, order_key(Fmt<DT>::kNegInf));
   const uint32_t lbits = key_to_bits(lkey);
   const uint32_t l2 = lbits | (lbits << 16);
@@ -1258,7 +1271,12 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_slice_kernel(const Par
     __syncthreads();  // every thread has read the count before the fallback resets it
     written = static_cast<uint32_t>(span_exact_topk<DT>(sh, row, V, p.vec, p.id_base, vbase, C, kk, slots));
   }
-  if (t == 0) cnt[static_cast<size_t>(b) * S + s] = written | (sh.ctl[kCtlFlags] << 24);
+  if (t == 0) {
+    uint32_t f = 0u;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) f |= sh.uscr[kUscrFlags + w];
+    cnt[static_cast<size_t>(b) * S + s] = written | (f << 24);
+  }
 }
 
 // Row merge, one warp per row (blockDim.x / 32 rows per CTA, no block barrier). Per-warp shared
