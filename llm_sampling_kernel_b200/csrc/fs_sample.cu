@@ -120,6 +120,11 @@ struct alignas(16) Shared {
   double dscr[40];
 };
 
+// the 256-bin histograms are read with 16-byte loads
+static_assert(offsetof(Shared, h1) % 16 == 0 && offsetof(Shared, h2) % 16 == 0 && offsetof(Shared, fh1) % 16 == 0 &&
+                  offsetof(Shared, fh2) % 16 == 0 && offsetof(Shared, lh) % 16 == 0,
+              "histogram alignment");
+
 __host__ __device__ constexpr size_t shared_bytes(int cap) {
   return sizeof(Shared) + static_cast<size_t>(cap) * (sizeof(uint64_t) + 2 * sizeof(float));
 }
@@ -135,6 +140,24 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int q) {
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 __device__ __forceinline__ void grid_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
+// An L2 access policy that evicts the lines it touches first: for data read exactly once
+// (logits streamed by the slice kernel), so that it does not push out what later kernels of the
+// call read back from L2 (the slices' candidate lists).
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(pol));
+  return pol;
+}
+
+// 16-byte read-only global load under an L2 access policy.
+__device__ __forceinline__ uint4 ldg_policy(const uint4* ptr, uint64_t pol) {
+  uint4 v;
+  asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(ptr), "l"(pol));
+  return v;
 }
 
 // Split cluster barrier: arrive (release) now, wait (acquire) later.
@@ -184,15 +207,19 @@ __device__ __forceinline__ void hist_add_warp(uint32_t* h, uint32_t bin, bool va
 }
 
 // One warp: in the 256-bin histogram h, the bin where the count from the top reaches `want`
-// and the count strictly above it (lane l owns bins 255-8l .. 248-8l). Returns false when the
+// and the count strictly above it (lane l owns bins 255-8l .. 248-8l; h is 16-byte aligned). Returns false when the
 // total is below `want`. Results are valid in every lane.
 __device__ __forceinline__ bool warp_boundary_256(const uint32_t* h, uint32_t want, uint32_t* bin,
                                                   uint32_t* above) {
   const int lane = threadIdx.x & 31;
+  // the lane's 8 bins, 255 - 8 lane - j for j = 0..7, as two 16-byte loads
+  const uint4* h4 = reinterpret_cast<const uint4*>(h);
+  const uint4 lo = h4[62 - 2 * lane], hi = h4[63 - 2 * lane];
+  const uint32_t bins[8] = {hi.w, hi.z, hi.y, hi.x, lo.w, lo.z, lo.y, lo.x};
   uint32_t pre[8], acc = 0u;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    acc += h[255 - 8 * lane - j];
+    acc += bins[j];
     pre[j] = acc;  // inclusive count of this lane's first j+1 bins (from the top)
   }
   const uint32_t inc = warp_incl_scan(acc);
@@ -213,6 +240,40 @@ __device__ __forceinline__ bool warp_boundary_256(const uint32_t* h, uint32_t wa
   *above = __shfl_sync(0xFFFFFFFFu, ab, l0);
   return true;
 }
+
+// One warp's scan of a 256-bin histogram h (16-byte aligned, top bin h[255]; lane l owns bins
+// 255-8l .. 248-8l), loaded once and then searched for any number of wants.
+struct WarpHistScan {
+  uint32_t pre[8];  // inclusive count of this lane's first j+1 bins (from the top)
+  uint32_t inc;     // inclusive count through this lane
+  __device__ __forceinline__ explicit WarpHistScan(const uint32_t* h) {
+    const int lane = threadIdx.x & 31;
+    const uint4* h4 = reinterpret_cast<const uint4*>(h);
+    const uint4 lo = h4[62 - 2 * lane], hi = h4[63 - 2 * lane];
+    const uint32_t bins[8] = {hi.w, hi.z, hi.y, hi.x, lo.w, lo.z, lo.y, lo.x};
+    uint32_t acc = 0u;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      acc += bins[j];
+      pre[j] = acc;
+    }
+    inc = warp_incl_scan(acc);
+  }
+  // The bin where the count from the top first reaches `want`; false when the total is below it.
+  // Every lane calls it and gets the result.
+  __device__ __forceinline__ bool find(uint32_t want, uint32_t* bin) const {
+    const int lane = threadIdx.x & 31;
+    const uint32_t before = inc - pre[7];
+    const unsigned ball = __ballot_sync(0xFFFFFFFFu, inc >= want);
+    int j0 = 7;
+#pragma unroll
+    for (int j = 6; j >= 0; --j)
+      if (before + pre[j] >= want) j0 = j;
+    const int l0 = ball != 0u ? __ffs(ball) - 1 : 0;
+    *bin = __shfl_sync(0xFFFFFFFFu, static_cast<uint32_t>(255 - 8 * lane - j0), l0);
+    return ball != 0u;
+  }
+};
 
 // The kk-th largest of the n 16-bit keys keys[0..n) (0 when n < kk): two 8-bit radix levels with
 // shared-memory histograms h1 (high byte, filled by every thread) and h2 (low byte inside the
@@ -245,11 +306,14 @@ __device__ uint32_t kth_largest_key(const uint32_t* keys, int n, int kk, uint32_
 // registers: one 256-bin histogram anchored at the largest key (bin = (max - key) >> sh, clamped
 // to the last bin), the boundary found by one warp scan, L = the lower edge of the boundary bin.
 // With sh == 0 and the boundary below the last bin, L is exactly the want-th largest key. At
-// least `want` keys are >= L. Returns 0 when the CTA holds fewer than `want` keys. h: 256 shared
-// words, zeroed by the caller before the call (the call's first barrier publishes that);
-// scratch: >= 9 shared words. Every thread of the CTA calls it; three barriers.
+// least `want` keys are >= L. Returns 0 when the CTA holds fewer than `want` keys.
+// When `ladder` is not null, thread 0 also stores there the same kind of bound for the wants
+// ceil(want/8), ceil(want/4), ceil(want/2) and want, in 16-bit fields 0..3; a field is 0 (no
+// bound) unless it lies above `floor`, so that every key counted above it is a real element's.
+// h: 256 shared words, zeroed by the caller before the call (the call's first barrier publishes
+// that); scratch: >= 9 shared words. Every thread of the CTA calls it; three barriers.
 __device__ uint32_t anchored_threshold(const uint32_t (&keys)[8], int nk, int want, int sh, uint32_t* h,
-                                       uint32_t* scratch) {
+                                       uint32_t* scratch, uint32_t floor, uint64_t* ladder) {
   const int t = threadIdx.x;
   uint32_t m = 0u;
 #pragma unroll
@@ -266,16 +330,26 @@ __device__ uint32_t anchored_threshold(const uint32_t (&keys)[8], int nk, int wa
     if (i < nk) atomicAdd(&h[255u - min(255u, (kmax - keys[i]) >> sh)], 1u);  // top bin = largest key
   __syncthreads();
   if (t < 32) {
-    uint32_t idx = 0u, above = 0u, L = 0u;
-    if (warp_boundary_256(h, static_cast<uint32_t>(want), &idx, &above)) {
-      const uint32_t bin = 255u - idx;
-      if (bin < 255u) {
-        const uint32_t hi = kmax - (bin << sh);
+    const uint32_t w = static_cast<uint32_t>(want);
+    const WarpHistScan hs(h);
+    uint64_t word = 0ull;
+    uint32_t L = 0u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t wi = i == 0 ? (w + 7u) / 8u : i == 1 ? (w + 3u) / 4u : i == 2 ? (w + 1u) / 2u : w;
+      uint32_t idx = 0u;
+      L = 0u;
+      if (hs.find(wi, &idx) && idx != 0u) {  // idx 0: the last, open-ended bin
+        const uint32_t hi = kmax - ((255u - idx) << sh);
         const uint32_t width = (1u << sh) - 1u;
         L = hi > width ? hi - width : 0u;
       }
+      word |= static_cast<uint64_t>(L > floor ? L : 0u) << (16 * i);
     }
-    if (t == 0) scratch[8] = L;
+    if (t == 0) {
+      scratch[8] = L;  // the bound for `want` itself
+      if (ladder != nullptr) *ladder = word;
+    }
   }
   __syncthreads();
   return scratch[8];
@@ -1015,6 +1089,69 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
   cluster_wait();
 }
 
+// ---- mbarriers and bulk copies (row merge, persistent kernel) ----------------------------
+
+constexpr long long kWaitLimit = 1LL << 22;         // try_wait polls before a stage wait gives up
+
+__device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+// One poll of the phase with the given parity; true once it has completed.
+__device__ __forceinline__ bool mbar_done(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0u;
+}
+
+// Bounded wait for a stage; false if it did not complete within kWaitLimit polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (long long i = 0; i < kWaitLimit; ++i) {
+    if (mbar_done(bar, parity)) return true;
+  }
+  return false;
+}
+
+// Per-thread 16-byte global -> shared copy through L2 only (both addresses 16-byte aligned); the
+// thread's copies are complete after cp_async_wait_all.
+__device__ __forceinline__ void cp_async_16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+// Orders this CTA's earlier generic-proxy accesses of shared memory before later bulk copies.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
+// Global -> shared bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned),
+// completion signalled on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // ------------------------------------------------------------------------------------------
 // Streaming path for large batches: two launches, no cross-CTA waiting.
 //   fs_slice_kernel: one CTA per (slice, row). The slice is read once into registers; the CTA
@@ -1130,6 +1267,7 @@ __device__ __noinline__ int span_exact_topk(Shared& sh, const uint16_t* __restri
 
 template <int DT, int C>
 __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_slice_kernel(const Params p, uint64_t* __restrict__ cand,
+                                                                      uint64_t* __restrict__ lad,
                                                                       uint32_t* __restrict__ cnt) {
   const int S = static_cast<int>(gridDim.x);
   const int s = blockIdx.x;
@@ -1154,8 +1292,9 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_slice_kernel(const Par
   const bool full = p.vec && (vbase + C * NT) * 8 <= V;
   if (full) {
     const uint4* rv = reinterpret_cast<const uint4*>(row) + vbase + t;
+    const uint64_t pol = l2_evict_first_policy();
 #pragma unroll
-    for (int c = 0; c < C; ++c) v[c] = __ldg(rv + c * NT);
+    for (int c = 0; c < C; ++c) v[c] = ldg_policy(rv + c * NT, pol);
   } else {
 #pragma unroll
     for (int c = 0; c < C; ++c) v[c] = load_chunk<DT>(row, (vbase + c * NT + t) * 8, V, p.vec);
@@ -1225,7 +1364,8 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_slice_kernel(const Par
   // L_s: at most kk of this slice's elements lie above the kk-th largest of its maxima (the
   // threshold's first barrier also publishes the zeroed histogram and counters, and the flags)
   constexpr int kSh = DT ? 0 : 2;  // bf16: one key per bin; fp16: four (same span in value)
-  const uint32_t kth = anchored_threshold(mk, nm, kk, kSh, sh.h1, sh.uscr);
+  const uint32_t kth = anchored_threshold(mk, nm, kk, kSh, sh.h1, sh.uscr, order_key(Fmt<DT>::kNegInf),
+                                          lad + static_cast<size_t>(b) * S + s);
   const uint32_t lkey = max(kth, order_key(Fmt<DT>::kNegInf));
   const uint32_t lbits = key_to_bits(lkey);
   const uint32_t l2 = lbits | (lbits << 16);
@@ -1280,13 +1420,13 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_slice_kernel(const Par
 }
 
 // Row merge, one warp per row (blockDim.x / 32 rows per CTA, no block barrier). Per-warp shared
-// memory: a 256-bin histogram, the slice counts and offsets, the row's gathered candidates, the
-// sorted top kk and the probabilities of the tail.
+// memory: a 256-bin histogram and 256 bin cursors, the row's candidate slots (capn), the sorted
+// top kk and the probabilities of the tail.
 constexpr int kMergeWarps = NT / 32;
 
 __host__ __device__ constexpr size_t merge_warp_bytes(int capn, int K) {
-  return (1024 + 128 + static_cast<size_t>(capn) * 8 + static_cast<size_t>(K) * 8 + static_cast<size_t>(K) * 4 +
-          15) & ~static_cast<size_t>(15);
+  return (2048 + static_cast<size_t>(capn) * 8 + static_cast<size_t>(K) * 8 + static_cast<size_t>(K) * 4 + 15) &
+         ~static_cast<size_t>(15);
 }
 
 // Warps per row-merge CTA that fit the shared memory budget.
@@ -1321,8 +1461,133 @@ __device__ __noinline__ uint32_t warp_tie_cut(const uint64_t* g, uint32_t n, uin
   return prefix;
 }
 
+// The top kk of the n distinct packed values g[0..n) in descending order into dst (one warp):
+// each value's rank is the count of larger ones. For n <= 32 R, R values per lane are ranked
+// together against pairs of the list (16-byte loads; g[n] is padded with 0, below every packed
+// candidate, whose low word 0xFFFFFFFF - id is never 0); larger n rank one value at a time.
+// g must be 16-byte aligned with room for g[n].
+template <int R>
+__device__ __forceinline__ void warp_rank_top_regs(uint64_t* g, uint32_t n, uint32_t kk, uint64_t* dst) {
+  const int lane = threadIdx.x & 31;
+  if ((n & 1u) && lane == 0) g[n] = 0ull;
+  __syncwarp();
+  uint64_t x[R];
+  uint32_t r[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    x[i] = lane + 32u * i < n ? g[lane + 32u * i] : 0ull;
+    r[i] = 0u;
+  }
+  const ulonglong2* g2 = reinterpret_cast<const ulonglong2*>(g);
+  const uint32_t np = (n + 1u) >> 1;
+#pragma unroll 4
+  for (uint32_t j = 0; j < np; ++j) {
+    const ulonglong2 y = g2[j];
+#pragma unroll
+    for (int i = 0; i < R; ++i) r[i] += (y.x > x[i] ? 1u : 0u) + (y.y > x[i] ? 1u : 0u);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < R; ++i)
+    if (lane + 32u * i < n && r[i] < kk) dst[r[i]] = x[i];
+}
+
+__device__ __forceinline__ void warp_rank_top(uint64_t* g, uint32_t n, uint32_t kk, uint64_t* dst) {
+  const int lane = threadIdx.x & 31;
+  if (n <= 96u) {
+    warp_rank_top_regs<3>(g, n, kk, dst);
+  } else if (n <= 192u) {
+    warp_rank_top_regs<6>(g, n, kk, dst);
+  } else {
+    for (uint32_t i = lane; i < n; i += 32) {
+      const uint64_t x = g[i];
+      uint32_t rank = 0u;
+      for (uint32_t j = 0; j < n; ++j) rank += g[j] > x ? 1u : 0u;
+      if (rank < kk) dst[rank] = x;
+    }
+  }
+  __syncwarp();
+}
+
+// Top kk of the n (>= 1) distinct packed values g[0..n) in descending order into dst, by a
+// counting sort on the 16-bit key (one warp): bins from the largest key down, the values
+// scattered into t[0..n) grouped by bin, and each value of a bin that starts below kk ranked
+// among the bin's values. Returns false, having written nothing, when the keys span more than
+// 256 values or a bin holds more than 64 (heavy ties); the caller then ranks another way.
+// hist, cursor: 256 shared words each, 16-byte aligned; t must not overlap g.
+__device__ bool warp_count_rank_top(const uint64_t* g, uint32_t n, uint32_t kk, uint32_t* hist, uint32_t* cursor,
+                                    uint64_t* t, uint64_t* dst) {
+  const int lane = threadIdx.x & 31;
+  uint32_t kmax = 0u, kmin = 0xFFFFu;
+  for (uint32_t d = lane; d < n; d += 32) {
+    const uint32_t k = packed_key(g[d]);
+    kmax = max(kmax, k);
+    kmin = min(kmin, k);
+  }
+  kmax = __reduce_max_sync(0xFFFFFFFFu, kmax);
+  kmin = __reduce_min_sync(0xFFFFFFFFu, kmin);
+  if (kmax - kmin > 255u) return false;
+  uint4* h4 = reinterpret_cast<uint4*>(hist);
+  h4[2 * lane] = make_uint4(0u, 0u, 0u, 0u);
+  h4[2 * lane + 1] = make_uint4(0u, 0u, 0u, 0u);
+  __syncwarp();
+  for (uint32_t d = lane; d < n; d += 32) atomicAdd(&hist[kmax - packed_key(g[d])], 1u);
+  __syncwarp();
+  // exclusive prefix over the bins from the largest key (lane l owns bins 8l .. 8l+7)
+  const uint4 a = h4[2 * lane], b = h4[2 * lane + 1];
+  const uint32_t cnt[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  uint32_t acc = 0u, big = 0u;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    acc += cnt[j];
+    big = max(big, cnt[j]);
+  }
+  if (__reduce_max_sync(0xFFFFFFFFu, big) > 64u) return false;
+  uint32_t run = warp_incl_scan(acc) - acc;
+  uint32_t st[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    st[j] = run;
+    run += cnt[j];
+  }
+  uint4* c4 = reinterpret_cast<uint4*>(cursor);
+  c4[2 * lane] = make_uint4(st[0], st[1], st[2], st[3]);
+  c4[2 * lane + 1] = make_uint4(st[4], st[5], st[6], st[7]);
+  __syncwarp();
+  for (uint32_t d = lane; d < n; d += 32) {
+    const uint64_t x = g[d];
+    t[atomicAdd(&cursor[kmax - packed_key(x)], 1u)] = x;
+  }
+  __syncwarp();
+  // cursor[bin] is now the bin's end and hist[bin] its size
+  for (uint32_t q = lane; q < n; q += 32) {
+    const uint64_t x = t[q];
+    const uint32_t bin = kmax - packed_key(x);
+    const uint32_t e = cursor[bin], s0 = e - hist[bin];
+    if (s0 >= kk) continue;
+    uint32_t r = s0;
+    for (uint32_t j = s0; j < e; ++j) r += t[j] > x ? 1u : 0u;
+    if (r < kk) dst[r] = x;
+  }
+  __syncwarp();
+  return true;
+}
+
+// Row merge of the streaming path, one warp per row.
+//  1. The lanes start 16-byte async copies of the row's S * M candidate slots into the warp's
+//     shared memory (one L2 round trip for the whole row); lanes 0..S-1 load their slice's count
+//     word and threshold ladder meanwhile.
+//  2. A row-wide lower bound L* on the kk-th largest: slice s has at least n_j elements at or
+//     above its ladder key l_sj (n_j = ceil(kk/8), ceil(kk/4), ceil(kk/2), kk), so any t with
+//     sum_s max{n_j : l_sj >= t} >= kk has kk elements at or above it. L* is the largest such t
+//     among the ladder keys (32 or 64 of them, one or two per lane); L* >= every slice's own
+//     bound l_s3, so every element of the row's top kk is in the lists and >= L*.
+//  3. The listed candidates >= L* are compacted in place (ballots), usually a few dozen.
+//  4. Up to 192 of them are ranked directly; more take the histogram path (two 8-bit radix
+//     levels, tie cut, compaction) first. Then the tail shared with the cluster kernel.
 template <int DT>
 __global__ void __launch_bounds__(NT) fs_rowmerge_kernel(const Params p, const uint64_t* __restrict__ cand,
+                                                         const uint64_t* __restrict__ lad,
                                                          const uint32_t* __restrict__ cnt, int S, int B) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -1336,21 +1601,56 @@ __global__ void __launch_bounds__(NT) fs_rowmerge_kernel(const Params p, const u
   const int capn = p.cap;
   unsigned char* base = g_smem + merge_warp_bytes(capn, p.K) * warp;
   uint32_t* hist = reinterpret_cast<uint32_t*>(base);
-  uint32_t* offs_cnt = hist + 256;  // [0, 16): counts; [16, 32): exclusive offsets
-  uint64_t* g = reinterpret_cast<uint64_t*>(offs_cnt + 32);
+  uint32_t* cursor = hist + 256;
+  uint64_t* g = reinterpret_cast<uint64_t*>(cursor + 256);
   uint64_t* dst = g + capn;
   float* prob = reinterpret_cast<float*>(dst + p.K);
+
+  // 1. the row's S * M slots -> g (capn >= S * M), 16-byte async copies spread over the lanes
+  const size_t row0 = static_cast<size_t>(b) * S;
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(cand + row0 * M);
+    uint4* g4 = reinterpret_cast<uint4*>(g);
+    const uint32_t pairs = static_cast<uint32_t>(S) * M / 2u;
+    for (uint32_t q = lane; q < pairs; q += 32u) cp_async_16(g4 + q, src + q);
+  }
+  const uint32_t w = lane < S ? __ldcg(cnt + row0 + lane) : 0u;
+  const uint64_t lw = lane < S ? __ldcg(lad + row0 + lane) : 0ull;
 
   int kk;
   float pp;
   bool bad;
   row_params(p, b, &kk, &pp, &bad);
   const float u = row_uniform(p, b);
-  const uint32_t w = lane < S ? __ldcg(cnt + static_cast<size_t>(b) * S + lane) : 0u;
   const uint32_t c = min(w & kCountMask, M);  // (never above M; the clamp keeps reads in range)
-  const uint32_t inc = warp_incl_scan(c);
   const uint32_t f = __reduce_or_sync(0xFFFFFFFFu, w >> 24);
-  const uint32_t n = __shfl_sync(0xFFFFFFFFu, inc, 31);
+
+  // 2. L* from the ladders
+  const uint32_t ukk = static_cast<uint32_t>(kk);
+  const uint32_t n0 = (ukk + 7u) / 8u, n1 = (ukk + 3u) / 4u, n2 = (ukk + 1u) / 2u;
+  uint32_t lstar = 0u;
+  for (int e0 = 0; e0 < 4 * S; e0 += 32) {
+    const int e = e0 + lane;
+    const uint64_t own = __shfl_sync(0xFFFFFFFFu, lw, (e >> 2) & 31);
+    const uint32_t t = e < 4 * S ? static_cast<uint32_t>(own >> (16 * (e & 3))) & 0xFFFFu : 0u;
+    uint32_t sum = 0u;
+    for (int r = 0; r < S; ++r) {
+      const uint64_t x = __shfl_sync(0xFFFFFFFFu, lw, r);
+      const uint32_t l0 = static_cast<uint32_t>(x) & 0xFFFFu, l1 = static_cast<uint32_t>(x >> 16) & 0xFFFFu;
+      const uint32_t l2 = static_cast<uint32_t>(x >> 32) & 0xFFFFu, l3 = static_cast<uint32_t>(x >> 48);
+      sum += (l3 != 0u && l3 >= t)   ? ukk
+             : (l2 != 0u && l2 >= t) ? n2
+             : (l1 != 0u && l1 >= t) ? n1
+             : (l0 != 0u && l0 >= t) ? n0
+                                     : 0u;
+    }
+    if (t != 0u && sum >= ukk) lstar = max(lstar, t);
+  }
+  lstar = __reduce_max_sync(0xFFFFFFFFu, lstar);
+
+  // the copies land before anything else touches g, or the warp leaves
+  cp_async_wait_all();
+  __syncwarp();
   int st = FS_ROW_OK;
   if (bad) st = FS_ROW_BAD_PARAM;
   else if (f & kFlagNaN) st = FS_ROW_NAN;
@@ -1360,43 +1660,50 @@ __global__ void __launch_bounds__(NT) fs_rowmerge_kernel(const Params p, const u
     write_invalid_row(p, b, st, lane, 32);
     return;
   }
-  if (lane < 16) {
-    offs_cnt[lane] = c;
-    offs_cnt[16 + lane] = inc - c;
+
+  // 3. keep the listed candidates >= L*, compacted in place to g[0, n): a step writes below
+  // n + 64 <= the first slot it reads, and every lane has read before any lane writes
+  uint32_t n = 0u;
+  const ulonglong2* g2 = reinterpret_cast<const ulonglong2*>(g);
+  const unsigned lt = (1u << lane) - 1u;
+  for (int r = 0; r < S; ++r) {
+    const uint32_t cr = __shfl_sync(0xFFFFFFFFu, c, r);
+    for (uint32_t j0 = 0; j0 < cr; j0 += 64u) {
+      const uint32_t j = j0 + 2u * lane;
+      ulonglong2 x = make_ulonglong2(0ull, 0ull);
+      if (j < cr) x = g2[(static_cast<uint32_t>(r) * M + j) >> 1];
+      const bool k0 = j < cr && packed_key(x.x) >= lstar;
+      const bool k1 = j + 1u < cr && packed_key(x.y) >= lstar;
+      const unsigned b0 = __ballot_sync(0xFFFFFFFFu, k0), b1 = __ballot_sync(0xFFFFFFFFu, k1);
+      if (k0) g[n + __popc(b0 & lt)] = x.x;
+      if (k1) g[n + __popc(b0) + __popc(b1 & lt)] = x.y;
+      n += __popc(b0) + __popc(b1);
+    }
   }
+  __syncwarp();
+
+  // 4. the survivors' top kk: a counting sort on the key (room for a second copy after g[0..n)),
+  // else, for at most 192 of them, a rank by comparisons
+  bool ranked = false;
+  if (n >= ukk) {
+    if (2u * n <= static_cast<uint32_t>(capn)) ranked = warp_count_rank_top(g, n, ukk, hist, cursor, g + n, dst);
+    if (!ranked && n <= 192u) {
+      warp_rank_top(g, n, ukk, dst);
+      ranked = true;
+    }
+  }
+  if (ranked) {
+    if (write_selection(p, b, dst, kk, lane, 32)) return;
+    if (kk <= 32) sample_tail_warp<DT, 1>(p, b, dst, kk, pp, u, prob);
+    else if (kk <= 64) sample_tail_warp<DT, 2>(p, b, dst, kk, pp, u, prob);
+    else sample_tail_warp<DT, 8>(p, b, dst, kk, pp, u, prob);
+    return;
+  }
+  // otherwise the histogram path: high byte, then low byte inside the boundary bin
 #pragma unroll
   for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0u;
   __syncwarp();
-  // gather every slot in use and the high-byte histogram of the keys: pairs of slots (M is even)
-  // in batches of 8 independent 16-byte L2 loads per lane, issued before any is used
-  const uint64_t* rowc = cand + static_cast<size_t>(b) * S * M;
-  const ulonglong2* rc2 = reinterpret_cast<const ulonglong2*>(rowc);
-  const int mshift = __ffs(static_cast<int>(M)) - 1;
-  const uint32_t pairs = static_cast<uint32_t>(S) * M / 2u;
-  for (uint32_t base = 0; base < pairs; base += 32u * 8u) {
-    ulonglong2 x[8];
-    uint32_t rj[8];  // slice << 16 | slot in the slice, or ~0u for a pair not in use
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const uint32_t q = base + lane + 32u * u;
-      const uint32_t r = (2u * q) >> mshift, j = (2u * q) & (M - 1u);
-      const bool ok = q < pairs && j < offs_cnt[r & 15u];
-      rj[u] = ok ? (r << 16 | j) : ~0u;
-      if (ok) x[u] = __ldcg(rc2 + q);
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      if (rj[u] == ~0u) continue;
-      const uint32_t r = rj[u] >> 16, j = rj[u] & 0xFFFFu;
-      const uint32_t o = offs_cnt[16 + r] + j;
-      g[o] = x[u].x;
-      atomicAdd(&hist[packed_key(x[u].x) >> 8], 1u);
-      if (j + 1u < offs_cnt[r]) {
-        g[o + 1] = x[u].y;
-        atomicAdd(&hist[packed_key(x[u].y) >> 8], 1u);
-      }
-    }
-  }
+  for (uint32_t d = lane; d < n; d += 32) atomicAdd(&hist[packed_key(g[d]) >> 8], 1u);
   __syncwarp();
   uint32_t hb = 0u, above = 0u;
   warp_boundary_256(hist, static_cast<uint32_t>(kk), &hb, &above);
@@ -1431,13 +1738,7 @@ __global__ void __launch_bounds__(NT) fs_rowmerge_kernel(const Params p, const u
   }
   __syncwarp();
   // rank sort (packed values are distinct; nsel <= kk + 32): the top kk in order
-  for (uint32_t i = lane; i < nsel; i += 32) {
-    const uint64_t x = g[i];
-    uint32_t rank = 0u;
-    for (uint32_t j = 0; j < nsel; ++j) rank += g[j] > x ? 1u : 0u;
-    if (rank < static_cast<uint32_t>(kk)) dst[rank] = x;
-  }
-  __syncwarp();
+  warp_rank_top(g, nsel, static_cast<uint32_t>(kk), dst);
   if (write_selection(p, b, dst, kk, lane, 32)) return;
   if (kk <= 32) sample_tail_warp<DT, 1>(p, b, dst, kk, pp, u, prob);
   else if (kk <= 64) sample_tail_warp<DT, 2>(p, b, dst, kk, pp, u, prob);
@@ -1466,59 +1767,6 @@ constexpr int kStageElems = kStageChunks * NT * 8;  // 16384 logits
 constexpr int kStageBytes = kStageElems * 2;        // 32 KiB
 constexpr int kMaxRing = 6;
 constexpr int kRingOffset = 128;                    // mbarriers, then the stages (128-byte aligned)
-constexpr long long kWaitLimit = 1LL << 22;         // try_wait polls before a stage wait gives up
-
-__device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_init_fence() {
-  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-// One poll of the phase with the given parity; true once it has completed.
-__device__ __forceinline__ bool mbar_done(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0u;
-}
-
-// Bounded wait for a stage; false if it did not complete within kWaitLimit polls.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (long long i = 0; i < kWaitLimit; ++i) {
-    if (mbar_done(bar, parity)) return true;
-  }
-  return false;
-}
-
-// Orders this CTA's earlier generic-proxy accesses of shared memory before later bulk copies.
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-}
-
-// Global -> shared bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned),
-// completion signalled on `bar`.
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
 template <int DT>
 __global__ void __launch_bounds__(NT, 1) fs_rowstream_kernel(const Params p) {
   Shared& sh = *reinterpret_cast<Shared*>(g_smem);
@@ -2138,7 +2386,9 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t pat
     out->merge_cap = std::max(256, pow2_ceil(static_cast<int64_t>(S) * M));
     out->merge_smem = static_cast<int>(merge_warps(out->merge_cap, static_cast<int>(K)) *
                                        merge_warp_bytes(out->merge_cap, static_cast<int>(K)));
-    out->workspace = static_cast<uint64_t>(B) * S * M * sizeof(uint64_t) + static_cast<uint64_t>(B) * S * 4 + 256;
+    // candidates [B][S][M], ladders [B][S], count words [B][S]
+    out->workspace = static_cast<uint64_t>(B) * S * M * sizeof(uint64_t) + static_cast<uint64_t>(B) * S * 8 +
+                     static_cast<uint64_t>(B) * S * 4 + 256;
   }
   return FS_OK;
 }
@@ -2322,8 +2572,8 @@ KernelFn slice_kernel_for(int C) {
   }
 }
 
-using SliceFn = void (*)(const Params, uint64_t*, uint32_t*);
-using RowMergeFn = void (*)(const Params, const uint64_t*, const uint32_t*, int, int);
+using SliceFn = void (*)(const Params, uint64_t*, uint64_t*, uint32_t*);
+using RowMergeFn = void (*)(const Params, const uint64_t*, const uint64_t*, const uint32_t*, int, int);
 
 static fs_status launch_stream(const fs_sample_args* a, const PlanOut& plan, const Params& prm,
                                cudaStream_t stream) {
@@ -2335,7 +2585,8 @@ static fs_status launch_stream(const fs_sample_args* a, const PlanOut& plan, con
   }
   const uintptr_t base = (reinterpret_cast<uintptr_t>(a->workspace) + 255) & ~static_cast<uintptr_t>(255);
   uint64_t* cand = reinterpret_cast<uint64_t*>(base);
-  uint32_t* cnt = reinterpret_cast<uint32_t*>(cand + static_cast<size_t>(a->batch) * plan.splits * plan.slot);
+  uint64_t* lad = cand + static_cast<size_t>(a->batch) * plan.splits * plan.slot;
+  uint32_t* cnt = reinterpret_cast<uint32_t*>(lad + static_cast<size_t>(a->batch) * plan.splits);
   SliceFn sfn = reinterpret_cast<SliceFn>(a->dtype == FS_BF16 ? slice_kernel_for<1>(plan.chunks)
                                                                : slice_kernel_for<0>(plan.chunks));
   RowMergeFn mfn = a->dtype == FS_BF16 ? fs_rowmerge_kernel<1> : fs_rowmerge_kernel<0>;
@@ -2355,7 +2606,7 @@ static fs_status launch_stream(const fs_sample_args* a, const PlanOut& plan, con
   scfg.stream = stream;
   scfg.attrs = pdl;
   scfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&scfg, sfn, prm, cand, cnt);
+  cudaError_t e = cudaLaunchKernelEx(&scfg, sfn, prm, cand, lad, cnt);
   if (e != cudaSuccess) {
     set_error("slice launch: %s", cudaGetErrorString(e));
     return FS_ELAUNCH;
@@ -2374,7 +2625,8 @@ static fs_status launch_stream(const fs_sample_args* a, const PlanOut& plan, con
   mcfg.attrs = pdl;
   mcfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&mcfg, mfn, static_cast<const Params>(mp), static_cast<const uint64_t*>(cand),
-                         static_cast<const uint32_t*>(cnt), plan.splits, static_cast<int>(a->batch));
+                         static_cast<const uint64_t*>(lad), static_cast<const uint32_t*>(cnt), plan.splits,
+                         static_cast<int>(a->batch));
   if (e != cudaSuccess) {
     set_error("row-merge launch: %s", cudaGetErrorString(e));
     return FS_ELAUNCH;
