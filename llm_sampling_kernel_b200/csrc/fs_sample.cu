@@ -307,11 +307,13 @@ __device__ uint32_t kth_largest_key(const uint32_t* keys, int n, int kk, uint32_
 // to the last bin), the boundary found by one warp scan, L = the lower edge of the boundary bin.
 // With sh == 0 and the boundary below the last bin, L is exactly the want-th largest key. At
 // least `want` keys are >= L. Returns 0 when the CTA holds fewer than `want` keys.
-// When `ladder` is not null, thread 0 also stores there the same kind of bound for the wants
-// ceil(want/8), ceil(want/4), ceil(want/2) and want, in 16-bit fields 0..3; a field is 0 (no
-// bound) unless it lies above `floor`, so that every key counted above it is a real element's.
-// h: 256 shared words, zeroed by the caller before the call (the call's first barrier publishes
-// that); scratch: >= 9 shared words. Every thread of the CTA calls it; three barriers.
+// When `ladder` is not null, the CTA's last warp also stores there, after the last barrier, the
+// same kind of bound for the wants ceil(want/8), ceil(want/4), ceil(want/2) and want, in 16-bit
+// fields 0..3; a field is 0 (no bound) unless it lies above `floor`, so that every key counted
+// above it is a real element's. h: 256 shared words, zeroed by the caller before the call (the
+// call's first barrier publishes that), read by the last warp after the call returns to the
+// others: the caller must not write h before the CTA's next barrier. scratch: >= 9 shared words.
+// Every thread of the CTA calls it; three barriers.
 __device__ uint32_t anchored_threshold(const uint32_t (&keys)[8], int nk, int want, int sh, uint32_t* h,
                                        uint32_t* scratch, uint32_t floor, uint64_t* ladder) {
   const int t = threadIdx.x;
@@ -329,30 +331,32 @@ __device__ uint32_t anchored_threshold(const uint32_t (&keys)[8], int nk, int wa
   for (int i = 0; i < 8; ++i)
     if (i < nk) atomicAdd(&h[255u - min(255u, (kmax - keys[i]) >> sh)], 1u);  // top bin = largest key
   __syncthreads();
+  const uint32_t w = static_cast<uint32_t>(want);
+  // the lower edge of the bin where the count from the top reaches `wi` (0: no bound)
+  auto bound = [&](const WarpHistScan& hs, uint32_t wi) -> uint32_t {
+    uint32_t idx = 0u;
+    if (!hs.find(wi, &idx) || idx == 0u) return 0u;  // idx 0: the last, open-ended bin
+    const uint32_t hi = kmax - ((255u - idx) << sh);
+    const uint32_t width = (1u << sh) - 1u;
+    return hi > width ? hi - width : 0u;
+  };
   if (t < 32) {
-    const uint32_t w = static_cast<uint32_t>(want);
     const WarpHistScan hs(h);
-    uint64_t word = 0ull;
-    uint32_t L = 0u;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t wi = i == 0 ? (w + 7u) / 8u : i == 1 ? (w + 3u) / 4u : i == 2 ? (w + 1u) / 2u : w;
-      uint32_t idx = 0u;
-      L = 0u;
-      if (hs.find(wi, &idx) && idx != 0u) {  // idx 0: the last, open-ended bin
-        const uint32_t hi = kmax - ((255u - idx) << sh);
-        const uint32_t width = (1u << sh) - 1u;
-        L = hi > width ? hi - width : 0u;
-      }
-      word |= static_cast<uint64_t>(L > floor ? L : 0u) << (16 * i);
-    }
-    if (t == 0) {
-      scratch[8] = L;  // the bound for `want` itself
-      if (ladder != nullptr) *ladder = word;
-    }
+    const uint32_t L = bound(hs, w);
+    if (t == 0) scratch[8] = L;
   }
   __syncthreads();
-  return scratch[8];
+  const uint32_t L = scratch[8];
+  // the ladder, by the last warp while the others go on (h is left alone until they meet again)
+  if (ladder != nullptr && t >= NT - 32) {
+    const WarpHistScan hs(h);
+    const uint32_t l0 = bound(hs, (w + 7u) / 8u), l1 = bound(hs, (w + 3u) / 4u), l2 = bound(hs, (w + 1u) / 2u);
+    if (t == NT - 32) {
+      *ladder = static_cast<uint64_t>(l0 > floor ? l0 : 0u) | static_cast<uint64_t>(l1 > floor ? l1 : 0u) << 16 |
+                static_cast<uint64_t>(l2 > floor ? l2 : 0u) << 32 | static_cast<uint64_t>(L > floor ? L : 0u) << 48;
+    }
+  }
+  return L;
 }
 
 // The want-th largest of n 16-bit keys in shared memory by one warp (no block barrier):

@@ -267,3 +267,35 @@ def test_repeated_calls_reuse_no_state(path):
     b = abi.sample(x, 50, 0.9, seed=5, offset=6, path=path)
     assert torch.equal(a, b)
     assert torch.equal(a, abi.sample(x, 50, 0.9, seed=5, offset=6, path=CLUSTER))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("path", PATHS)
+def test_masked_vocabulary_regions(dtype, path):
+    """Whole slices of -inf (their threshold ladders carry no bound), rows with fewer finite
+    logits than k (-inf elements enter the top k), and rows finite in one slice only."""
+    B, V, k = 8, 151936, 50
+    x = dev_randn(B, V, 3.0, dtype, seed=31)
+    ninf = float("-inf")
+    x[0, : V // 2] = ninf                      # half the slices masked
+    x[1, 20480:] = ninf                        # one slice finite
+    x[2] = ninf
+    x[2, torch.randperm(V, generator=torch.Generator().manual_seed(2))[:30].cuda()] = 1.0  # 30 finite < k
+    x[3, ::2] = ninf                           # every other id masked
+    x[4, 20480 * 3: 20480 * 3 + 40] = 50.0     # a tight cluster inside one slice
+    ids_out = assert_paths_agree(x, k, 0.9, path, seed=5, offset=1)[1]
+    for r in range(B):
+        assert torch.equal(ids_out[r].cpu(), oracle_topk(x[r:r + 1], k)[0]), r
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_survivor_keys_spanning_more_than_256_values(path):
+    """fp16 keys of the top k spread over far more than 256 key values: the row merge's counting
+    sort declines and the comparison rank (or the histogram path) must give the same order."""
+    B, V = 4, 65536
+    g = torch.Generator().manual_seed(9)
+    x = (torch.rand(B, V, generator=g) * 2.0 ** torch.randint(-8, 8, (B, V), generator=g)).to(torch.float16).cuda()
+    for k in (20, 50, 128):
+        ids = assert_paths_agree(x, k, 1.0, path, seed=6, offset=k)[1]
+        for r in range(B):
+            assert torch.equal(ids[r].cpu(), oracle_topk(x[r:r + 1], k)[0])
