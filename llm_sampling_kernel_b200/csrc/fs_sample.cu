@@ -1171,6 +1171,11 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 
 constexpr uint32_t kCountMask = 0xFFFFFFu;
 
+// slice kernel: per-warp staging of marked chunks in dynamic shared memory after Shared
+constexpr int kMarkedPerWarp = 64;                         // chunks per warp
+constexpr int kMarkedBytesPerWarp = kMarkedPerWarp * 16;    // their data; then as many index words
+constexpr int kSliceStageBytes = (NT / 32) * kMarkedPerWarp * (16 + 4);
+
 // Exact top-kk of the span of `nchunks` CTA chunks starting at vector vbase (heavy ties), written
 // to slots[0..) (global or shared memory): two 8-bit radix levels over the span (re-read from
 // L1/L2) give the kk-th key T; the elements above T and the lowest-id ties at T (ranked in id
@@ -1375,30 +1380,31 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_slice_kernel(const Par
   const uint32_t l2 = lbits | (lbits << 16);
 
   // Filter: the per-chunk maxima mark the chunks of each thread that hold an element >= L (one
-  // packed compare per chunk). A lane then takes its marked chunks one at a time out of its
-  // registers, compares their 8 logits with L and reserves slots for the hits with one shared
-  // atomic per chunk; no warp-wide step.
+  // packed compare per chunk). The warp stages its marked chunks in shared memory (a scan of the
+  // lanes' counts, predicated 16-byte stores) and hands one to each lane, which compares its 8
+  // logits with L; one shared atomic per warp reserves the hits' slots. A warp with more marked
+  // chunks than its staging room (heavy ties) takes them out of its registers one at a time.
   uint64_t* slots = cand + (static_cast<size_t>(b) * S + s) * M;
   uint32_t cm = 0u;
 #pragma unroll
   for (int c = 0; c < C; ++c) cm |= (pair_ge_mask<DT>(cp[c], l2) != 0u ? 1u : 0u) << c;
-  while (cm != 0u) {
-    const int c = __ffs(cm) - 1;
-    cm &= cm - 1u;
-    uint4 x = v[0];
-#pragma unroll
-    for (int cc = 1; cc < C; ++cc)
-      if (c == cc) x = v[cc];
-    const int e0 = (vbase + c * NT + t) * 8;
-    uint32_t hits = 0u;  // bit 2w + h: half h of word w of the chunk is >= L
+  const int lane = t & 31;
+  const uint32_t nmine = static_cast<uint32_t>(__popc(cm));
+  const uint32_t incl = warp_incl_scan(nmine);
+  const uint32_t wtotal = __shfl_sync(0xFFFFFFFFu, incl, 31);
+  // the row's hits of one 8-logit chunk (bit 2w + h: half h of word w is >= L), past-the-end
+  // elements cleared
+  auto chunk_hits = [&](const uint4& x, int e0) -> uint32_t {
+    uint32_t hits = 0u;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const uint32_t m = pair_ge_mask<DT>(word_of(x, w), l2);
       hits |= ((m & 1u) | ((m >> 15) & 2u)) << (2 * w);
     }
-    if (e0 + 8 > V) hits &= (e0 < V) ? ((1u << (V - e0)) - 1u) : 0u;  // past the row end
-    if (hits == 0u) continue;
-    uint32_t j = atomicAdd(&sh.ctl[kCtlLocal], static_cast<uint32_t>(__popc(hits)));
+    if (e0 + 8 > V) hits &= (e0 < V) ? ((1u << (V - e0)) - 1u) : 0u;
+    return hits;
+  };
+  auto write_hits = [&](const uint4& x, int e0, uint32_t hits, uint32_t j) {
     while (hits != 0u) {
       const int bit = __ffs(hits) - 1;
       hits &= hits - 1u;
@@ -1406,6 +1412,52 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_slice_kernel(const Par
       const uint32_t word = w == 0 ? x.x : w == 1 ? x.y : w == 2 ? x.z : x.w;
       if (j < M) slots[j] = pack(order_key((word >> (16 * (bit & 1))) & 0xFFFFu), p.id_base + e0 + bit);
       ++j;
+    }
+  };
+  if (wtotal <= static_cast<uint32_t>(kMarkedPerWarp)) {
+    uint4* stg = reinterpret_cast<uint4*>(g_smem + sizeof(Shared)) + (t >> 5) * kMarkedPerWarp;
+    uint32_t* sidx = reinterpret_cast<uint32_t*>(g_smem + sizeof(Shared) + kMarkedBytesPerWarp * (NT / 32)) +
+                     (t >> 5) * kMarkedPerWarp;
+    uint32_t o = incl - nmine;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      if (cm & (1u << c)) {
+        stg[o] = v[c];
+        sidx[o] = static_cast<uint32_t>(c * NT + t);
+        ++o;
+      }
+    }
+    __syncwarp();
+    for (uint32_t i0 = 0; i0 < wtotal; i0 += 32u) {
+      const uint32_t i = i0 + static_cast<uint32_t>(lane);
+      uint4 x = make_uint4(0u, 0u, 0u, 0u);
+      int e0 = 0;
+      uint32_t hits = 0u;
+      if (i < wtotal) {
+        x = stg[i];
+        e0 = (vbase + static_cast<int>(sidx[i])) * 8;
+        hits = chunk_hits(x, e0);
+      }
+      const uint32_t nh = static_cast<uint32_t>(__popc(hits));
+      const uint32_t hincl = warp_incl_scan(nh);
+      const uint32_t htot = __shfl_sync(0xFFFFFFFFu, hincl, 31);
+      uint32_t hbase = 0u;
+      if (lane == 31 && htot != 0u) hbase = atomicAdd(&sh.ctl[kCtlLocal], htot);
+      hbase = __shfl_sync(0xFFFFFFFFu, hbase, 31);
+      write_hits(x, e0, hits, hbase + hincl - nh);
+    }
+  } else {
+    while (cm != 0u) {
+      const int c = __ffs(cm) - 1;
+      cm &= cm - 1u;
+      uint4 x = v[0];
+#pragma unroll
+      for (int cc = 1; cc < C; ++cc)
+        if (c == cc) x = v[cc];
+      const int e0 = (vbase + c * NT + t) * 8;
+      const uint32_t hits = chunk_hits(x, e0);
+      if (hits == 0u) continue;
+      write_hits(x, e0, hits, atomicAdd(&sh.ctl[kCtlLocal], static_cast<uint32_t>(__popc(hits))));
     }
   }
   __syncthreads();
@@ -2386,7 +2438,7 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t pat
     out->mgroup = 1;
     out->mcta = NT * out->mpt;
     out->slot = M;
-    out->smem = static_cast<int>(sizeof(Shared));
+    out->smem = static_cast<int>(sizeof(Shared)) + kSliceStageBytes;
     out->merge_cap = std::max(256, pow2_ceil(static_cast<int64_t>(S) * M));
     out->merge_smem = static_cast<int>(merge_warps(out->merge_cap, static_cast<int>(K)) *
                                        merge_warp_bytes(out->merge_cap, static_cast<int>(K)));
