@@ -2308,7 +2308,7 @@ static int pow2_floor(int64_t x) {
 
 constexpr int kMaxCap = 8192;
 constexpr int64_t kStreamMaxK = 256;     // streaming path: top-K bound
-constexpr int64_t kStreamMinBatch = 192;  // AUTO: rows from which the streaming path is used
+constexpr int64_t kStreamMinBatch = 96;   // AUTO: rows from which the streaming path is used
 constexpr int64_t kStreamAutoMaxK = 128;  // AUTO: largest k for which it is used
 constexpr size_t kPersistSmemBudget = 227 * 1024;  // opt-in dynamic shared memory per CTA
 

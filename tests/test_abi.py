@@ -122,6 +122,10 @@ def test_large_batches_plan_the_streaming_path_with_a_workspace():
     # [B, S, M] packed candidates (M >= 2k) + [B, S] counts + alignment slack
     assert big.workspace_bytes >= 1024 * big.splits * (2 * 50 * 8 + 4)
     assert abi.plan(1, 151936, 50).path == abi.FS_PATH_CLUSTER
+    # AUTO: the streaming path from 96 rows (measured crossover with the cluster path, k <= 128)
+    assert abi.plan(95, 151936, 50).path == abi.FS_PATH_CLUSTER
+    assert abi.plan(96, 151936, 50).path == abi.FS_PATH_STREAM
+    assert abi.plan(96, 151936, 129).path == abi.FS_PATH_CLUSTER
     assert abi.plan(1, 151936, 50).workspace_bytes == 0
     # beyond the streaming path's k the cluster path serves every batch size
     assert abi.plan(1024, 151936, 1024).path == abi.FS_PATH_CLUSTER

@@ -4,7 +4,7 @@ PERSIST (one CTA per SM streaming whole rows through bulk-copied shared-memory s
 Each must give exactly what the cluster path gives: the same top-k set and order (checked against
 the oracle), and, because all end in the same row tail over the same candidates, the same ids,
 keep mask, renormed probabilities and row status, bit for bit. `path=` forces a path at any batch
-(k <= 256); batches of 192 rows and more take STREAM by default when k <= 128.
+(k <= 256); batches of 96 rows and more take STREAM by default when k <= 128.
 """
 
 import numpy as np
