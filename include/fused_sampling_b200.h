@@ -95,7 +95,15 @@ typedef struct fs_sample_args {
   int32_t path;              /* FS_PATH_* (AUTO = 0 picks)                               */
   void* workspace;           /* device scratch for the streaming path (see below)        */
   uint64_t workspace_bytes;  /* its size; >= fs_workspace_size(args)                     */
+  float temperature;         /* softmax temperature T > 0; 0 or 1 = none (see below)     */
 } fs_sample_args;
+
+/* Temperature. The selected candidates' logits are divided by T in IEEE fp32 before the softmax,
+ * which is what sampling fp32 logits / T gives (the convention of a temperature warper applied to
+ * fp32 logits ahead of the top-k / top-p warpers). The selection itself is unchanged: fp32
+ * division by T > 0 is strictly increasing on 16-bit float inputs, so the top-k set and its order
+ * (value desc, id asc) are those of the raw logits. A row whose largest scaled logit overflows to
+ * +inf gets FS_ROW_POSINF, as an infinite logit would. T < 0, NaN or inf: FS_EINVAL. */
 
 /* Execution paths. CLUSTER: one launch, one thread-block cluster per row, no workspace (the
  * latency path). STREAM: two launches - independent CTAs per row slice write candidate lists to

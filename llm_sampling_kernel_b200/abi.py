@@ -86,6 +86,7 @@ class FsSampleArgs(ctypes.Structure):
         ("path", ctypes.c_int32),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_uint64),
+        ("temperature", ctypes.c_float),
     ]
 
 
@@ -230,7 +231,7 @@ def _stream(stream=None):
 def make_args(logits, top_k: int, top_p: float = 1.0, *, seed: int = 0, offset: int = 0, uniforms=None,
               top_k_rows=None, top_p_rows=None, id_base: int = 0, row_base: int = 0, splits: int = 0,
               out_ids=None, topk_ids=None, keep=None, renormed=None, row_status=None,
-              stop_phase: int = 0, path: int = FS_PATH_AUTO) -> FsSampleArgs:
+              stop_phase: int = 0, path: int = FS_PATH_AUTO, temperature: float = 1.0) -> FsSampleArgs:
     import torch
 
     a = FsSampleArgs()
@@ -259,6 +260,7 @@ def make_args(logits, top_k: int, top_p: float = 1.0, *, seed: int = 0, offset: 
     a.splits = splits
     a.stop_phase = stop_phase
     a.path = path
+    a.temperature = temperature
     return a
 
 
@@ -278,7 +280,7 @@ def attach_workspace(a: FsSampleArgs, device):
 
 def sample(logits, top_k: int, top_p: float, *, seed: int = 0, offset: int = 0, uniforms=None,
            top_k_rows=None, top_p_rows=None, splits: int = 0, id_base: int = 0, row_base: int = 0,
-           stages: bool = False, path: int = FS_PATH_AUTO, stream=None):
+           stages: bool = False, path: int = FS_PATH_AUTO, stream=None, temperature: float = 1.0):
     """fs_sample through ctypes. Returns ids, or (ids, topk_ids, keep, renormed, status)."""
     import torch
 
@@ -294,7 +296,7 @@ def sample(logits, top_k: int, top_p: float, *, seed: int = 0, offset: int = 0, 
         ren = torch.empty(B, K, dtype=torch.float32, device=dev)
     a = make_args(logits, top_k, top_p, seed=seed, offset=offset, uniforms=uniforms, top_k_rows=top_k_rows,
                   top_p_rows=top_p_rows, id_base=id_base, row_base=row_base, splits=splits, out_ids=out,
-                  topk_ids=ids, keep=keep, renormed=ren, row_status=status, path=path)
+                  topk_ids=ids, keep=keep, renormed=ren, row_status=status, path=path, temperature=temperature)
     ws = attach_workspace(a, dev)  # noqa: F841  (alive until the launches are enqueued)
     check(lib().fs_sample(ctypes.byref(a), _stream(stream)), "fs_sample")
     if stages:

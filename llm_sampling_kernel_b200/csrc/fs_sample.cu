@@ -80,6 +80,7 @@ struct Params {
   int32_t batch;       // rows (the persistent kernel walks them)
   int32_t ring;        // persistent kernel: shared-memory stages in the ring
   int32_t nst;         // persistent kernel: stages per row
+  float temperature;   // softmax temperature (1 = none): candidates' logits / T before the softmax
 };
 
 constexpr int kModeSample = 0;
@@ -456,16 +457,28 @@ __device__ void write_stages(const Params& p, int b, const uint64_t* cand, const
   }
 }
 
+// A candidate's logit as the softmax sees it: its 16-bit value in fp32, divided by the
+// temperature (IEEE fp32 division; none when it is 1).
+template <int DT>
+__device__ __forceinline__ float tail_logit(const Params& p, uint32_t key) {
+  const float x = key_to_float<DT>(key);
+  return p.temperature == 1.0f ? x : __fdiv_rn(x, p.temperature);
+}
+
 // Block-wide tail for more than kWarpPathMax candidates: FP32 softmax over the top kk sorted
 // candidates, exclusive-prefix top-p cut, inverse-CDF draw. All NT threads call it.
 template <int DT>
 __device__ void sample_tail_block(const Params& p, int b, const uint64_t* cand, int kk, float pp,
                                   float* prob, float* cum, double* dscr, int* iscr) {
   const int t = threadIdx.x;
-  const float m = key_to_float<DT>(packed_key(cand[0]));
+  const float m = tail_logit<DT>(p, packed_key(cand[0]));
+  if (m == INFINITY) {  // the scaled maximum overflowed
+    write_invalid_row(p, b, FS_ROW_POSINF, t, NT);
+    return;
+  }
   double part = 0.0;
   for (int i = t; i < kk; i += NT) {
-    const float w = expf(key_to_float<DT>(packed_key(cand[i])) - m);
+    const float w = expf(tail_logit<DT>(p, packed_key(cand[i])) - m);
     prob[i] = w;
     part += static_cast<double>(w);
   }
@@ -526,12 +539,16 @@ __device__ void sample_tail_warp(const Params& p, int b, const uint64_t* cand, i
     const int i = lane * R + r;
     v[r] = i < kk ? cand[i] : 0ull;
   }
-  const float m = key_to_float<DT>(packed_key(__shfl_sync(0xFFFFFFFFu, v[0], 0)));
+  const float m = tail_logit<DT>(p, packed_key(__shfl_sync(0xFFFFFFFFu, v[0], 0)));
+  if (m == INFINITY) {  // the scaled maximum overflowed
+    write_invalid_row(p, b, FS_ROW_POSINF, lane, 32);
+    return;
+  }
   float pr[R];
   double part = 0.0;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    pr[r] = (lane * R + r < kk) ? expf(key_to_float<DT>(packed_key(v[r])) - m) : 0.0f;
+    pr[r] = (lane * R + r < kk) ? expf(tail_logit<DT>(p, packed_key(v[r])) - m) : 0.0f;
     part += static_cast<double>(pr[r]);
   }
   const float z = static_cast<float>(warp_sum(part));
@@ -2580,6 +2597,10 @@ static fs_status check_top_p(const fs_sample_args* a) {
     set_error("top_p must be in (0, 1]");
     return FS_EINVAL;
   }
+  if (!(a->temperature >= 0.0f && a->temperature <= 3.0e38f)) {
+    set_error("temperature must be a finite value >= 0 (0 or 1: none)");
+    return FS_EINVAL;
+  }
   return FS_OK;
 }
 
@@ -2587,6 +2608,7 @@ static Params base_params(const fs_sample_args* a, int64_t K) {
   Params prm = {};
   prm.logits = static_cast<const uint16_t*>(a->logits);
   prm.row_stride = a->row_stride;
+  prm.temperature = a->temperature == 0.0f ? 1.0f : a->temperature;
   prm.vocab = static_cast<int32_t>(a->vocab);
   prm.K = static_cast<int32_t>(K);
   prm.id_base = static_cast<uint32_t>(a->id_base);

@@ -251,7 +251,8 @@ void fill_rows(fs_sample_args* a, const torch::Tensor& logits,
 std::vector<std::optional<torch::Tensor>> sample_ex(
     torch::Tensor logits, int64_t top_k, double top_p, std::optional<torch::Tensor> top_k_rows,
     std::optional<torch::Tensor> top_p_rows, std::optional<torch::Tensor> uniforms, int64_t seed,
-    int64_t offset, int64_t splits, int64_t id_base, int64_t row_base, bool return_stages, int64_t path) {
+    int64_t offset, int64_t splits, int64_t id_base, int64_t row_base, bool return_stages, int64_t path,
+    double temperature) {
   check_logits(logits);
   check_top_k(top_k);
   if (!top_p_rows.has_value()) check_top_p(top_p);
@@ -276,6 +277,7 @@ std::vector<std::optional<torch::Tensor>> sample_ex(
     a.renormed = ren->data_ptr<float>();
   }
   a.path = static_cast<int32_t>(path);
+  a.temperature = static_cast<float>(temperature);
   auto ws = attach_workspace(&a, logits);
   check(fs_sample(&a, current_stream()), "fs_sample");
   return {out, ids, keep, ren, status};
@@ -403,7 +405,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("logits"), py::arg("top_k"), py::arg("top_p"), py::arg("top_k_rows") = py::none(),
         py::arg("top_p_rows") = py::none(), py::arg("uniforms") = py::none(), py::arg("seed") = 0,
         py::arg("offset") = -1, py::arg("splits") = 0, py::arg("id_base") = 0,
-        py::arg("row_base") = 0, py::arg("return_stages") = false, py::arg("path") = 0);
+        py::arg("row_base") = 0, py::arg("return_stages") = false, py::arg("path") = 0,
+        py::arg("temperature") = 1.0);
   m.def("shard_candidates", &shard_candidates, "vocab-shard local top-k as packed candidates",
         py::arg("logits"), py::arg("top_k"), py::arg("id_base"), py::arg("splits") = 0);
   m.def("merge_sample", &merge_sample, "merge gathered shard candidates and sample",

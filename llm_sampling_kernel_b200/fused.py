@@ -62,6 +62,7 @@ def sample(
     row_base: int = 0,
     return_stages: bool = False,
     check_inputs: bool = False,
+    temperature: float = 1.0,
 ) -> SampleResult:
     """General sampler.
 
@@ -70,6 +71,9 @@ def sample(
     uniforms: optional float32 [B] tensor of caller-supplied u in [0, 1).
     check_inputs: raise ValueError (the reference's messages) for NaN / +inf / all -inf rows;
     this synchronises with the device, so keep it off in timed loops.
+    temperature: T > 0 divides the selected candidates' logits (IEEE fp32) before the softmax,
+    as sampling fp32 ``logits / T`` would; the top-k selection is that of the raw logits
+    (fp32 division by T > 0 keeps their order). 1 (or 0) means none.
     """
     k_rows = p_rows = None
     if isinstance(top_k, torch.Tensor):
@@ -88,7 +92,7 @@ def sample(
         uniforms = uniforms.to(device=logits.device, dtype=torch.float32).contiguous()
     ids, tk, keep, ren, status = ops().sample_ex(
         logits, k_bound, p_scalar, k_rows, p_rows, uniforms, int(seed), off, int(splits), int(id_base),
-        int(row_base), bool(return_stages))
+        int(row_base), bool(return_stages), 0, float(temperature))
     if check_inputs:
         bad = status[status != ROW_OK]
         if bad.numel():

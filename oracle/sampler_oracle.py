@@ -146,8 +146,13 @@ def _check_args(logits: torch.Tensor, top_k: int, top_p: float) -> None:
         raise ValueError(f"top_p must be in (0, 1], got {top_p}")
 
 
-def stages(logits: torch.Tensor, top_k: int, top_p: float, check_inputs: bool = False) -> Stages:
-    """Every intermediate of the reference pipeline, on CPU."""
+def stages(logits: torch.Tensor, top_k: int, top_p: float, check_inputs: bool = False,
+           temperature: float = 1.0) -> Stages:
+    """Every intermediate of the reference pipeline, on CPU.
+
+    temperature (not in the reference, which leaves it to the caller): the top-k logits are divided
+    by T in fp32 before the softmax, i.e. the pipeline run on fp32 ``logits / T``; the top-k order
+    is that of the raw logits, since fp32 division by T > 0 keeps the order of 16-bit values."""
     _check_args(logits, top_k, top_p)
     if check_inputs:
         validate_logits(logits)
@@ -155,6 +160,8 @@ def stages(logits: torch.Tensor, top_k: int, top_p: float, check_inputs: bool = 
     ids = torch.from_numpy(topk_ids_any(logits, k))
     x = logits.detach().cpu().float()
     topk_logits = x.gather(-1, ids)
+    if temperature != 1.0:
+        topk_logits = topk_logits / temperature
     probs = torch.softmax(topk_logits, dim=-1)
     cumsum = probs.cumsum(dim=-1)
     if top_p >= 1.0:
@@ -248,9 +255,10 @@ def sample(
     offset: int = 0,
     uniforms: np.ndarray | None = None,
     row_base: int = 0,
+    temperature: float = 1.0,
 ) -> Draw:
     """Token ids for the same per-row uniform the kernel draws (or the caller supplies)."""
-    st = stages(logits, top_k, top_p)
+    st = stages(logits, top_k, top_p, temperature=temperature)
     B = logits.shape[0]
     u = uniforms if uniforms is not None else splitmix_uniforms(seed, offset, B, row_base)
     return draw(st, np.asarray(u, dtype=np.float32), top_p)
