@@ -305,7 +305,7 @@ std::vector<torch::Tensor> merge_sample(torch::Tensor cand, bool bf16, int64_t t
                                         std::optional<torch::Tensor> top_k_rows,
                                         std::optional<torch::Tensor> top_p_rows,
                                         std::optional<torch::Tensor> uniforms, int64_t seed,
-                                        int64_t offset, int64_t row_base) {
+                                        int64_t offset, int64_t row_base, double temperature) {
   TORCH_CHECK(cand.is_cuda() && cand.dim() == 3 && cand.is_contiguous() &&
                   cand.scalar_type() == at::kLong,
               "cand must be a contiguous int64 cuda [parts, B, K + 1] tensor");
@@ -326,6 +326,7 @@ std::vector<torch::Tensor> merge_sample(torch::Tensor cand, bool bf16, int64_t t
   a.rng.row_base = row_base;
   a.out_ids = out.data_ptr<int64_t>();
   a.row_status = status.data_ptr<int32_t>();
+  a.temperature = static_cast<float>(temperature);
   check(fs_merge_sample(&a, reinterpret_cast<const uint64_t*>(cand.data_ptr<int64_t>()),
                         static_cast<int32_t>(parts), current_stream()),
         "fs_merge_sample");
@@ -339,7 +340,7 @@ std::vector<torch::Tensor> tp_merge(torch::Tensor local_cand, bool bf16, int64_t
                                     torch::Tensor recv, torch::Tensor flags, torch::Tensor peer_recv,
                                     torch::Tensor peer_flags, int64_t world, int64_t rank, int64_t epoch,
                                     std::optional<torch::Tensor> uniforms, int64_t seed, int64_t offset,
-                                    int64_t row_base, int64_t wait_polls) {
+                                    int64_t row_base, int64_t wait_polls, double temperature) {
   TORCH_CHECK(local_cand.is_cuda() && local_cand.dim() == 2 && local_cand.is_contiguous() &&
                   local_cand.scalar_type() == at::kLong && local_cand.size(1) == top_k + 1,
               "local_cand must be a contiguous int64 cuda [B, top_k + 1] tensor");
@@ -368,6 +369,7 @@ std::vector<torch::Tensor> tp_merge(torch::Tensor local_cand, bool bf16, int64_t
   a.rng.row_base = row_base;
   a.out_ids = out.data_ptr<int64_t>();
   a.row_status = status.data_ptr<int32_t>();
+  a.temperature = static_cast<float>(temperature);
   fs_tp_peers tp = {};
   tp.world = static_cast<int32_t>(world);
   tp.rank = static_cast<int32_t>(rank);
@@ -413,12 +415,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("cand"), py::arg("bf16"), py::arg("top_k"), py::arg("top_p"),
         py::arg("top_k_rows") = py::none(), py::arg("top_p_rows") = py::none(),
         py::arg("uniforms") = py::none(), py::arg("seed") = 0, py::arg("offset") = -1,
-        py::arg("row_base") = 0);
+        py::arg("row_base") = 0, py::arg("temperature") = 1.0);
   m.def("tp_merge", &tp_merge, "vocab-shard exchange over peer memory + merge + sample",
         py::arg("local_cand"), py::arg("bf16"), py::arg("top_k"), py::arg("top_p"), py::arg("recv"),
         py::arg("flags"), py::arg("peer_recv"), py::arg("peer_flags"), py::arg("world"), py::arg("rank"),
         py::arg("epoch"), py::arg("uniforms") = py::none(), py::arg("seed") = 0, py::arg("offset") = -1,
-        py::arg("row_base") = 0, py::arg("wait_polls") = 0);
+        py::arg("row_base") = 0, py::arg("wait_polls") = 0, py::arg("temperature") = 1.0);
   m.def("plan", &plan,
         "launch plan (splits, chunks, threads, capacity, maxima/thread, lanes/max, smem, path, workspace)");
   m.attr("NUM_PHASES") = FS_NUM_PHASES;

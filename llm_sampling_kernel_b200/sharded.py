@@ -206,8 +206,9 @@ class VocabShardedSampler:
         return self._gathered
 
     def sample(self, shard_logits: torch.Tensor, top_p: float, *, seed: int, offset: int,
-               uniforms: Optional[torch.Tensor] = None, row_base: int = 0):
-        """Returns (ids [B], status [B]); identical on every rank."""
+               uniforms: Optional[torch.Tensor] = None, row_base: int = 0, temperature: float = 1.0):
+        """Returns (ids [B], status [B]); identical on every rank. temperature: as in
+        ``fused.sample`` (the merged candidates' logits / T in fp32 before the softmax)."""
         if self.backend == "p2p":
             B = shard_logits.shape[0]
             if B > self.max_batch:
@@ -219,8 +220,8 @@ class VocabShardedSampler:
             cand = self.local_candidates(shard_logits)
             return self.ops.tp_merge(cand, self.bf16, self.top_k, top_p, st["recv"], st["flags"], st["peer_recv"],
                                      st["peer_flags"], self.world, self.rank, st["epoch"], uniforms, seed, offset,
-                                     row_base, self.wait_polls)
+                                     row_base, self.wait_polls, temperature=temperature)
         gathered = self.exchange(self.local_candidates(shard_logits))
         ids, status = self.ops.merge_sample(gathered, self.bf16, self.top_k, top_p, None, None, uniforms, seed,
-                                            offset, row_base)
+                                            offset, row_base, temperature=temperature)
         return ids, status

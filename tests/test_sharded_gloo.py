@@ -37,7 +37,8 @@ class OracleOps:
         status = orc.row_status(logits).astype(np.int64)[:, None]
         return torch.from_numpy(np.concatenate([packed, status], axis=1))
 
-    def merge_sample(self, cand, bf16, top_k, top_p, k_rows, p_rows, uniforms, seed, offset, row_base):
+    def merge_sample(self, cand, bf16, top_k, top_p, k_rows, p_rows, uniforms, seed, offset, row_base,
+                     temperature=1.0):
         c = cand.numpy()
         parts, B, _ = c.shape
         words = c[:, :, :top_k].transpose(1, 0, 2).reshape(B, parts * top_k).view(np.uint64)
@@ -51,7 +52,7 @@ class OracleOps:
         bits = np.where(neg, (~keys) & 0xFFFF, keys & 0x7FFF).astype(np.uint16)
         x = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16 if bf16 else torch.float16)
         u = uniforms.numpy() if uniforms is not None else orc.splitmix_uniforms(seed, offset, B, row_base)
-        d = orc.sample(x, top_k, top_p, uniforms=u)
+        d = orc.sample(x, top_k, top_p, uniforms=u, temperature=temperature)
         ids = gid[np.arange(B), d.ids]
         return torch.from_numpy(ids), torch.zeros(B, dtype=torch.int32)
 

@@ -74,3 +74,32 @@ def test_a_scaled_maximum_that_overflows_reports_posinf_and_bad_temperatures_are
     for T in (-1.0, float("nan"), float("inf")):
         with pytest.raises(RuntimeError, match="temperature"):
             fused.sample(x, 10, 1.0, seed=1, temperature=T)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T", [0.5, 2.0])
+def test_vocab_sharded_merge_applies_the_same_temperature(T):
+    """Two vocabulary shards merged on one GPU (the all-gather emulated by a stack) give the ids
+    of the unsharded tempered call; the peer-memory exchange with one rank does too."""
+    ops = fused.ops()
+    B, V, K = 16, 256000, 64
+    x = (torch.randn(B, V, generator=torch.Generator().manual_seed(12)) * 2.5).to(torch.bfloat16).cuda()
+    vs = V // 2
+    cands = torch.stack([ops.shard_candidates(x[:, r * vs:(r + 1) * vs].contiguous(), K, r * vs) for r in range(2)])
+    want = ops.sample_ex(x, K, 0.9, seed=3, offset=5, temperature=T)[0]
+    ids, status = ops.merge_sample(cands, True, K, 0.9, seed=3, offset=5, temperature=T)
+    assert torch.equal(ids, want) and (status == 0).all()
+    assert not torch.equal(want, ops.sample_ex(x, K, 0.9, seed=3, offset=5)[0])  # T changes the draws
+    recv, recv_ptr = abi.ipc_alloc((2, 1, B, K + 1), torch.int64)
+    flags, flags_ptr = abi.ipc_alloc((2, 1, B), torch.int32)
+    try:
+        cand = ops.shard_candidates(x, K, 0)
+        ptrs = torch.tensor([recv_ptr], dtype=torch.int64, device="cuda")
+        fptrs = torch.tensor([flags_ptr], dtype=torch.int64, device="cuda")
+        ids1, st1 = ops.tp_merge(cand, True, K, 0.9, recv, flags, ptrs, fptrs, 1, 0, 1, seed=3, offset=5,
+                                 temperature=T)
+        assert torch.equal(ids1, want) and (st1 == 0).all()
+    finally:
+        torch.cuda.synchronize()
+        abi.ipc_free(recv_ptr)
+        abi.ipc_free(flags_ptr)
