@@ -62,6 +62,11 @@ def _worker(rank, world, port):
                 others = [torch.empty_like(tids) for _ in range(world)]
                 dist.all_gather(others, tids)
                 assert all(torch.equal(o, tids) for o in others), "ranks disagree"
+            # a tempered step: the merged candidates' logits / T before the softmax
+            tids, status = tp.sample(full[:, c0:c1].contiguous(), 0.9, seed=11, offset=9, temperature=0.6)
+            ref = ops().sample_ex(full, 64, 0.9, None, None, None, 11, 9, 0, 0, 0, False, 0, 0.6)[0]
+            assert torch.equal(tids, ref), f"tempered vocab-sharded ids ({backend}) differ from the unsharded call"
+            assert (status == 0).all()
             tp.close()
         torch.cuda.synchronize()
         dist.barrier()
