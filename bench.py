@@ -15,8 +15,10 @@ the measured peak (the C3 config, reported in `roofline`).
   batch the call is the streaming path's two launches (slice kernel, then row merge); the time
   is the CUDA-event time of the whole call, so `achieved` (algorithmic bytes B*V*2 + B*8 over it)
   charges the row merge to the slice kernel. Peak: MEASURED_PEAKS.json's burst HBM copy bandwidth.
-* `cpu_baseline` / `--impl reference` time the reference semantics on the host CPU (the oracle
-  port of benchmarks/reference.py:sample_eager, all host threads) on a bounded sample.
+* `cpu_baseline` / `--impl reference` time the reference's own CPU implementation of the path,
+  benchmarks/reference.py:sample_eager(check_inputs=False) built into oracle/_ref by
+  `make -C oracle` (the oracle port of it when that is missing), on all host threads, on a
+  bounded sample of C1 calls.
 * N > 1 (torchrun, one process per GPU): weak scaling of the anchor (each rank samples its own
   B=1 row; value = max over ranks), plus the B=1024 batch-sharded config (rows split across
   ranks, no collective on the data path) and the vocab-sharded tensor-parallel config (B=32,
@@ -206,7 +208,9 @@ def max_over_ranks(x: float, world: int) -> float:
 
 def timed_steps(fn, steps, warmup, world):
     """Warm-up, then exactly `steps` calls between CUDA events on the current stream with a
-    barrier + synchronize on both sides. Returns the device ms of the timed region."""
+    barrier + synchronize on both sides. Returns the device ms of the timed region. Step indices
+    continue past the warm-up (fn(warmup + i)), so a timed step never reuses the input buffer of a
+    warm-up step."""
     for i in range(warmup):
         fn(i)
     torch.cuda.synchronize()
@@ -215,7 +219,7 @@ def timed_steps(fn, steps, warmup, world):
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for i in range(steps):
-        fn(i)
+        fn(warmup + i)
     e.record()
     torch.cuda.synchronize()
     barrier(world)
@@ -224,25 +228,52 @@ def timed_steps(fn, steps, warmup, world):
 
 
 # ---------------------------------------------------------------------------------------------
-# the CPU side (oracle port of the reference semantics)
+# the CPU side: the reference's own sample_eager (built into oracle/_ref by `make -C oracle`),
+# else the oracle port of it
 # ---------------------------------------------------------------------------------------------
 
 
-def cpu_reference_time(B, V, k, p, budget_s=10.0, min_calls=3):
-    """µs per call of the oracle port of benchmarks/reference.py:sample_eager on host cores."""
+def reference_cpu_impl():
+    """(fn(x, k, p), kind, description) of the CPU implementation to time: the reference's own
+    benchmarks/reference.py:sample_eager(check_inputs=False) when oracle/_ref holds it, else the
+    oracle's port of it."""
+    refpkg = ROOT / "oracle" / "_ref" / "refpkg"
+    if (refpkg / "benchmarks" / "reference.py").exists():
+        sys.path.insert(0, str(refpkg))
+        try:
+            from benchmarks.reference import sample_eager
+
+            return (lambda x, k, p, i: sample_eager(x, k, p, check_inputs=False), "reference",
+                    "benchmarks/reference.py:sample_eager(check_inputs=False), the reference's own code "
+                    "(torch CPU FP32 stable sort + softmax + cumsum + multinomial)")
+        except Exception as e:  # noqa: BLE001
+            log(f"reference sample_eager unavailable ({e}); timing the oracle port")
+        finally:
+            sys.path.remove(str(refpkg))
     sys.path.insert(0, str(ROOT))
     from oracle import sampler_oracle as orc
 
+    return (lambda x, k, p, i: orc.sample(x, k, p, seed=1, offset=i), "port",
+            "the oracle port of benchmarks/reference.py:sample_eager (oracle/_ref not built)")
+
+
+def cpu_reference_time(B, V, k, p, budget_s=10.0, min_calls=3):
+    """µs per call of the reference's CPU implementation on all host cores, on a bounded sample:
+    as many calls on the workload's logits as fit in budget_s (at least min_calls)."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import sampler_oracle as orc
+
+    fn, kind, what = reference_cpu_impl()
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     x = orc.anchor_logits(B=B, V=V, seed=1234) if B <= 64 else orc.zipf_logits(B, V, seed=7)
-    orc.sample(x, k, p, seed=1, offset=0)  # warm-up
+    fn(x, k, p, 0)  # warm-up
     n, t0 = 0, time.perf_counter()
     while n < min_calls or time.perf_counter() - t0 < budget_s:
-        orc.sample(x, k, p, seed=1, offset=n)
+        fn(x, k, p, n)
         n += 1
     dt = time.perf_counter() - t0
-    return dt / n * 1e6, threads, n
+    return dt / n * 1e6, threads, n, kind, what
 
 
 # ---------------------------------------------------------------------------------------------
@@ -393,10 +424,11 @@ def run_ours(args):
     if tp is not None:
         line["tp"] = tp
     if world == 1 and not args.no_cpu:
-        cpu_us, threads, n = cpu_reference_time(C1["B"], C1["V"], C1["k"], C1["p"], budget_s=args.cpu_budget)
-        line["cpu_baseline"] = {"value": round(cpu_us, 1), "unit": "µs/call", "cores": threads, "kind": "port",
-                                "sample": f"C1 row (B=1, V=151936, k=50, p=0.9) x {n} calls of the oracle port "
-                                          f"of benchmarks/reference.py:sample_eager (torch CPU, {threads} threads)"}
+        cpu_us, threads, n, kind, what = cpu_reference_time(C1["B"], C1["V"], C1["k"], C1["p"],
+                                                            budget_s=args.cpu_budget)
+        line["cpu_baseline"] = {"value": round(cpu_us, 1), "unit": "µs/call", "cores": threads, "kind": kind,
+                                "sample": f"C1 row (B=1, V=151936, k=50, p=0.9) x {n} calls of {what}, "
+                                          f"{threads} host threads"}
     print(json.dumps(line), flush=True)
 
 
@@ -461,8 +493,8 @@ def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    cpu_us, threads, n = cpu_reference_time(C1["B"], C1["V"], C1["k"], C1["p"],
-                                            budget_s=max(5.0, min(60.0, args.cpu_budget)))
+    cpu_us, threads, n, kind, what = cpu_reference_time(C1["B"], C1["V"], C1["k"], C1["p"],
+                                                        budget_s=max(5.0, min(60.0, args.cpu_budget)))
     line = {
         "metric": METRIC,
         "value": round(cpu_us, 1),
@@ -477,12 +509,12 @@ def run_reference(args):
         "dtype": "f32 (torch CPU)",
         "data": "synthetic (seeded)",
         "impl": "reference",
-        "config": {"workload": "C1 anchor: B=1, V=151936, k=50, p=0.9, BF16", "B": 1, "V": 151936,
-                   "top_k": 50, "top_p": 0.9},
-        "cpu_baseline": {"value": round(cpu_us, 1), "unit": "µs/call", "cores": threads, "kind": "port",
-                         "sample": f"{n} calls of the oracle port of benchmarks/reference.py:sample_eager "
-                                   f"(the reference's CPU implementation of the path; its Python package "
-                                   f"cannot travel to the GPU box), {threads} host threads"},
+        "config": {"workload": "C1 anchor: B=1 per GPU, V=151936, k=50, p=0.9, BF16 N(0,2^2) + 20 ids boosted by 8",
+                   "B_per_gpu": C1["B"], "V": C1["V"], "top_k": C1["k"], "top_p": C1["p"],
+                   "parallelism": f"dp{world} (rank 0 alone runs the host-CPU reference)"},
+        "cpu_baseline": {"value": round(cpu_us, 1), "unit": "µs/call", "cores": threads, "kind": kind,
+                         "sample": f"C1 row (B=1, V=151936, k=50, p=0.9) x {n} calls of {what}, "
+                                   f"{threads} host threads"},
         "e2e": {"value": round(cpu_us, 1), "unit": "µs/call", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }

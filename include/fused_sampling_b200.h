@@ -93,7 +93,7 @@ typedef struct fs_sample_args {
   int32_t splits;            /* 0 = auto; else CTAs per row (1..16, rounded up to 2^n)    */
   int32_t stop_phase;        /* 0 = full pipeline; 1..FS_NUM_PHASES ablation stop point  */
   int32_t path;              /* FS_PATH_* (AUTO = 0 picks)                               */
-  void* workspace;           /* device scratch for the streaming path (see below)        */
+  void* workspace;           /* device scratch for the streaming and wide paths (below)  */
   uint64_t workspace_bytes;  /* its size; >= fs_workspace_size(args)                     */
   float temperature;         /* softmax temperature T > 0; 0 or 1 = none (see below)     */
 } fs_sample_args;
@@ -107,17 +107,21 @@ typedef struct fs_sample_args {
 
 /* Execution paths. CLUSTER: one launch, one thread-block cluster per row, no workspace (the
  * latency path). STREAM: two launches - independent CTAs per row slice write candidate lists to
- * the workspace, one CTA per row merges them. PERSIST: one launch, one CTA per SM streaming
- * whole rows through a ring of shared-memory stages filled by bulk copies, no workspace (the
- * throughput path for large batches; needs 16-byte aligned rows and V % 8 == 0, otherwise AUTO
- * falls back to CLUSTER). AUTO picks by batch size and k. All compute the same result. */
-enum { FS_PATH_AUTO = 0, FS_PATH_CLUSTER = 1, FS_PATH_STREAM = 2, FS_PATH_PERSIST = 3 };
+ * the workspace, one warp per row merges them (the throughput path for large batches, k <= 256).
+ * WIDE: any top_k up to V (top-p only when top_k >= V); nothing is sorted: a per-key count
+ * histogram of each row (workspace: 256 KiB per row, cleared by the call) and exact fixed-point
+ * probability masses per key locate the cut and the draw (a memset and four launches). It
+ * produces token ids and row status only (no topk_ids / keep / renormed); AUTO takes it when
+ * top_k exceeds the 8192-candidate buffer of the other paths.
+ * AUTO picks by batch size and k. All paths compute the same ids. */
+enum { FS_PATH_AUTO = 0, FS_PATH_CLUSTER = 1, FS_PATH_STREAM = 2, FS_PATH_WIDE = 3 };
 
 #define FS_NUM_PHASES 7
 
 /* Bytes of device workspace the call described by args needs (0 when its path needs none).
- * The workspace holds per-call candidate lists only: no state persists between calls, and it
- * needs no initialisation. Calls that may run concurrently need separate workspaces. */
+ * The workspace holds per-call scratch only (candidate lists, key histograms): no state persists
+ * between calls, and it needs no initialisation. Calls that may run concurrently need separate
+ * workspaces. */
 FS_API uint64_t fs_workspace_size(const fs_sample_args* args);
 
 /* Fused top-k + top-p + sample, [B, V] -> [B].
@@ -239,7 +243,7 @@ typedef struct fs_plan_info {
   int32_t maxima_per_thread;
   int32_t lanes_per_max;
   int32_t smem_bytes;
-  int32_t path;              /* FS_PATH_CLUSTER, FS_PATH_STREAM or FS_PATH_PERSIST */
+  int32_t path;              /* FS_PATH_CLUSTER, FS_PATH_STREAM or FS_PATH_WIDE */
   uint64_t workspace_bytes;  /* 0 unless the path is FS_PATH_STREAM */
 } fs_plan_info;
 FS_API fs_status fs_plan(int64_t batch, int64_t vocab, int64_t top_k, int32_t splits, fs_plan_info* out);

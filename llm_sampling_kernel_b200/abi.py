@@ -48,7 +48,7 @@ EXPORTED = (
     "fs_ipc_close",
 )
 FS_IPC_HANDLE_BYTES = 64
-FS_PATH_AUTO, FS_PATH_CLUSTER, FS_PATH_STREAM, FS_PATH_PERSIST = 0, 1, 2, 3
+FS_PATH_AUTO, FS_PATH_CLUSTER, FS_PATH_STREAM, FS_PATH_WIDE = 0, 1, 2, 3
 
 
 class FsRng(ctypes.Structure):

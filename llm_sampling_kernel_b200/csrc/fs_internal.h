@@ -24,9 +24,7 @@ struct PlanOut {
   int merge_cap; // streaming: gathered-candidate capacity of the row merge (power of two)
   int merge_smem;
   uint64_t workspace;  // streaming: workspace bytes
-  int persist;   // 1: persistent row-streaming kernel (one CTA per SM)
-  int ring;      // persistent: shared-memory stages
-  int nst;       // persistent: stages per row
+  int wide;      // 1: wide path (top_k beyond the survivor buffer; ids and status only)
 };
 
 // printf-style message for fs_last_error() on this host thread.

@@ -77,9 +77,6 @@ struct Params {
   int32_t vec;         // 16-byte vector loads allowed
   int32_t stop;        // 0 = full pipeline, else ablation phase
   int32_t mode;        // kModeSample / kModeTopk / kModeShard
-  int32_t batch;       // rows (the persistent kernel walks them)
-  int32_t ring;        // persistent kernel: shared-memory stages in the ring
-  int32_t nst;         // persistent kernel: stages per row
   float temperature;   // softmax temperature (1 = none): candidates' logits / T before the softmax
 };
 
@@ -100,7 +97,7 @@ constexpr int kCtlScr0 = 5;     // two words of block-search results
 constexpr int kCtlHb = 8;       // fallback scratch
 constexpr int kCtlAbove = 9;
 constexpr int kCtlT = 10;
-constexpr int kCtlTmo = 12;     // persistent kernel: some thread's wait ran out
+constexpr int kCtlTmo = 12;     // TP exchange: some flag wait ran out
 constexpr int kCtlNgt = 11;
 
 constexpr uint32_t kFlagNaN = 1u, kFlagPosInf = 2u, kFlagAboveNegInf = 4u;
@@ -198,7 +195,6 @@ __device__ __forceinline__ uint32_t atom_add_dsmem(uint32_t addr, uint32_t v) {
 __device__ __forceinline__ void st_dsmem64(uint32_t addr, uint64_t v) {
   asm volatile("st.shared::cluster.u64 [%0], %1;\n" ::"r"(addr), "l"(v) : "memory");
 }
-
 // Warp-aggregated shared-memory histogram add: lanes with the same bin elect one adder.
 // All 32 lanes must call it.
 __device__ __forceinline__ void hist_add_warp(uint32_t* h, uint32_t bin, bool valid) {
@@ -1110,44 +1106,391 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
   cluster_wait();
 }
 
-// ---- mbarriers and bulk copies (row merge, persistent kernel) ----------------------------
+// ------------------------------------------------------------------------------------------
+// Wide path: top-k beyond the survivor buffer, up to k = V (top-p only). Nothing is sorted.
+// The probability of an element depends only on its 16-bit key, so the sorted order (value
+// desc, id asc) is a sequence of key groups, and every cumulative sum the tail needs is a sum of
+// (group size x group probability) over the groups above a point. Four launches (and a memset of
+// the histogram), plain CTAs, no cluster:
+//   fs_wide_hist_kernel  (S x B CTAs) one read of each row slice: the per-key element counts of
+//                        the row (a [B, 65536] histogram in the workspace; lanes holding the same
+//                        key add once), and the slice's maximum and row flags;
+//   fs_wide_row_kernel   (one 1024-thread CTA per row, 64 keys per thread, from the largest key
+//                        down) the k-th key T and the `need` lowest-id ties at T that the top-k
+//                        takes; Z = sum of n_g * expf(x_g - m) in a fixed order; per key the
+//                        probability p_g = fl(w_g / z), held as an integer in units of 2^-62
+//                        (exact for every p >= 2^-39, so the masses add exactly and in any order);
+//                        the cut: the exclusive-prefix condition !((c_i - p_i) < top_p), with c_i
+//                        the float rounding of the exact cumulative sum, holds from some element
+//                        on (c is non-decreasing and p non-increasing along the order): the first
+//                        group whose last element meets it, then a binary search in the group;
+//                        the draw: target = u * c_r and the first element with c_i >= target,
+//                        found the same way. Result: the drawn key and its rank j among the
+//                        elements holding that key (ids ascending);
+//   fs_wide_count_kernel (S x B CTAs) per slice, the elements holding the drawn key;
+//   fs_wide_pick_kernel  (S x B CTAs) the slice holding the j-th of them scans its chunks in id
+//                        order and writes the token id.
+// With p >= 2^-29 for every candidate the cumulative sums are the ones the one-warp tail
+// accumulates in double, so the ids equal the other paths' for the same k.
+// ------------------------------------------------------------------------------------------
 
-constexpr long long kWaitLimit = 1LL << 22;         // try_wait polls before a stage wait gives up
+constexpr int kKeys = 65536;                             // 16-bit order keys
+constexpr int kRowThreads = 1024;                        // fs_wide_row_kernel
+constexpr int kKeysPerThread = kKeys / kRowThreads;      // 64 consecutive keys per thread
+constexpr float kTwo62f = 4611686018427387904.0f;        // 2^62: fixed-point unit of a probability
+constexpr float kTwoM62f = 2.168404344971008868e-19f;    // 2^-62
+
+// Float rounding of an exact cumulative mass x (units of 2^-62).
+__device__ __forceinline__ float fixed_to_float(uint64_t x) { return __fmul_rn(__ull2float_rn(x), kTwoM62f); }
+// A probability in units of 2^-62 (exact for pr >= 2^-39).
+__device__ __forceinline__ uint64_t prob_to_fixed(float pr) { return __float2ull_rn(__fmul_rn(pr, kTwo62f)); }
+
+// Row slice of the wide path's S x B launches into registers (as the cluster kernel loads it).
+template <int DT, int C>
+__device__ __forceinline__ void load_slice(const Params& p, int b, int vbase, uint4 (&v)[C]) {
+  const uint16_t* row = p.logits + static_cast<int64_t>(b) * p.row_stride;
+  const int t = threadIdx.x;
+  if (p.vec && (vbase + C * NT) * 8 <= p.vocab) {
+    const uint4* rv = reinterpret_cast<const uint4*>(row) + vbase + t;
+#pragma unroll
+    for (int c = 0; c < C; ++c) v[c] = __ldg(rv + c * NT);
+  } else {
+#pragma unroll
+    for (int c = 0; c < C; ++c) v[c] = load_chunk<DT>(row, (vbase + c * NT + t) * 8, p.vocab, p.vec);
+  }
+}
+
+// Order key of element j (0..7) of a 16-byte chunk.
+__device__ __forceinline__ uint32_t chunk_key(const uint4& x, int j) {
+  return order_key((word_of(x, j >> 1) >> (16 * (j & 1))) & 0xFFFFu);
+}
+
+template <int DT, int C>
+__global__ void __launch_bounds__(NT, min_ctas_for(C))
+    fs_wide_hist_kernel(const Params p, uint32_t* __restrict__ hist, uint32_t* __restrict__ smax,
+                        uint32_t* __restrict__ sflag) {
+  __shared__ uint32_t wf[NT / 32], wm[NT / 32];
+  const int S = static_cast<int>(gridDim.x);
+  const int s = blockIdx.x;
+  const int b = blockIdx.y;
+  const int t = threadIdx.x;
+  const int lane = t & 31;
+  const int V = p.vocab;
+  const int vbase = s * C * NT;
+  uint4 v[C];
+  load_slice<DT, C>(p, b, vbase, v);
+  uint32_t* hrow = hist + static_cast<size_t>(b) * kKeys;
+  uint32_t acc = Fmt<DT>::kNegInf2;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    acc = pair_max_nan<DT>(acc, pair_max_nan<DT>(pair_max_nan<DT>(v[c].x, v[c].y), pair_max_nan<DT>(v[c].z, v[c].w)));
+    const int e0 = (vbase + c * NT + t) * 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const bool valid = e0 + j < V;
+      const uint32_t key = chunk_key(v[c], j);
+      const unsigned peers = __match_any_sync(0xFFFFFFFFu, valid ? key : 0xFFFFFFFFu);
+      if (valid && lane == __ffs(peers) - 1) atomicAdd(&hrow[key], static_cast<uint32_t>(__popc(peers)));
+    }
+  }
+  const uint32_t mbits = half_max_nan<DT>(acc & 0xFFFFu, acc >> 16);
+  uint32_t flags = 0u;
+  if (Fmt<DT>::is_nan(mbits)) {
+    flags |= kFlagNaN;
+  } else {
+    if (mbits == Fmt<DT>::kPosInf) flags |= kFlagPosInf;
+    if (mbits != Fmt<DT>::kNegInf) flags |= kFlagAboveNegInf;
+  }
+  const uint32_t f = __reduce_or_sync(0xFFFFFFFFu, flags);
+  const uint32_t m = __reduce_max_sync(0xFFFFFFFFu, Fmt<DT>::is_nan(mbits) ? 0u : order_key(mbits));
+  if (lane == 0) {
+    wf[t >> 5] = f;
+    wm[t >> 5] = m;
+  }
+  __syncthreads();
+  if (t == 0) {
+    uint32_t ff = 0u, mm = 0u;
+    for (int w = 0; w < NT / 32; ++w) {
+      ff |= wf[w];
+      mm = max(mm, wm[w]);
+    }
+    sflag[static_cast<size_t>(b) * S + s] = ff;
+    smax[static_cast<size_t>(b) * S + s] = mm;
+  }
+}
+
+// Per-row result of fs_wide_row_kernel: {row status, drawn key, its rank among the elements
+// holding that key (ids ascending), 1 when the locate kernels have work}.
+constexpr int kWideRes = 4;
+
+// Elements of key `key` in the top-k: all of them above T, `need` at T, none below.
+__device__ __forceinline__ uint32_t topk_count(uint32_t key, uint32_t count, uint32_t T, uint32_t need) {
+  return key > T ? count : (key == T ? need : 0u);
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kRowThreads, 1)
+    fs_wide_row_kernel(const Params p, const uint32_t* __restrict__ hist, const uint32_t* __restrict__ smax,
+                       const uint32_t* __restrict__ sflag, uint32_t* __restrict__ res, int S) {
+  __shared__ uint64_t qscr[40];
+  __shared__ double dscr[40];
+  __shared__ uint32_t uscr[40];
+  __shared__ int iscr[40];
+  __shared__ uint64_t found[4];
+  const int b = blockIdx.x;
+  const int t = threadIdx.x;
+  const int lane = t & 31;
+  int kk;
+  float pp;
+  bool bad;
+  row_params(p, b, &kk, &pp, &bad);
+  uint32_t F = 0u, mkey = 0u;
+  for (int r = 0; r < S; ++r) {
+    F |= sflag[static_cast<size_t>(b) * S + r];
+    mkey = max(mkey, smax[static_cast<size_t>(b) * S + r]);
+  }
+  int st = FS_ROW_OK;
+  if (bad) st = FS_ROW_BAD_PARAM;
+  else if (F & kFlagNaN) st = FS_ROW_NAN;
+  else if (F & kFlagPosInf) st = FS_ROW_POSINF;
+  else if (!(F & kFlagAboveNegInf)) st = FS_ROW_ALL_NEGINF;
+  const float mf = tail_logit<DT>(p, mkey);
+  if (st == FS_ROW_OK && mf == INFINITY) st = FS_ROW_POSINF;  // the scaled maximum overflowed
+  uint32_t* rr = res + static_cast<size_t>(b) * kWideRes;
+  if (st != FS_ROW_OK) {
+    if (t == 0) {
+      rr[0] = static_cast<uint32_t>(st);
+      rr[3] = 0u;
+    }
+    write_invalid_row(p, b, st, t, kRowThreads);
+    return;
+  }
+
+  // thread t: keys kh = 65535 - 64 t down to kh - 63, read as 16 vectors from the top one down
+  const uint32_t kl = static_cast<uint32_t>(kKeys - kKeysPerThread * (t + 1));
+  const uint4* h4 = reinterpret_cast<const uint4*>(hist + static_cast<size_t>(b) * kKeys + kl);
+
+  // ---- the k-th key T and the ties `need` at T ----
+  uint32_t csum = 0u;
+#pragma unroll 4
+  for (int q = kKeysPerThread / 4 - 1; q >= 0; --q) {
+    const uint4 w = h4[q];
+    csum += w.x + w.y + w.z + w.w;
+  }
+  uint32_t ctot = 0u;
+  const uint32_t cbase = block_incl_scan<uint32_t, kRowThreads>(csum, uscr, &ctot) - csum;
+  const uint32_t ukk = static_cast<uint32_t>(kk);
+  if (cbase < ukk && ukk <= cbase + csum) {
+    uint32_t run = cbase;
+    for (int q = kKeysPerThread / 4 - 1; q >= 0; --q) {
+      const uint4 w = h4[q];
+      const uint32_t cnt[4] = {w.w, w.z, w.y, w.x};
+      bool done = false;
+      for (int i = 0; i < 4; ++i) {
+        if (run + cnt[i] >= ukk) {
+          uscr[36] = kl + 4u * static_cast<uint32_t>(q) + 3u - static_cast<uint32_t>(i);
+          uscr[37] = ukk - run;
+          done = true;
+          break;
+        }
+        run += cnt[i];
+      }
+      if (done) break;
+    }
+  }
+  __syncthreads();
+  const uint32_t T = uscr[36], need = uscr[37];
+
+  // ---- Z over the top-k, in a fixed order ----
+  double part = 0.0;
+  for (int q = kKeysPerThread / 4 - 1; q >= 0; --q) {
+    const uint4 w = h4[q];
+    const uint32_t cnt[4] = {w.w, w.z, w.y, w.x};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t key = kl + 4u * static_cast<uint32_t>(q) + 3u - static_cast<uint32_t>(i);
+      const uint32_t n = topk_count(key, cnt[i], T, need);
+      if (n != 0u) part += static_cast<double>(n) * static_cast<double>(expf(tail_logit<DT>(p, key) - mf));
+    }
+  }
+  part = warp_sum(part);
+  if (lane == 0) dscr[t >> 5] = part;
+  __syncthreads();
+  if (t == 0) {
+    double zs = 0.0;
+    for (int w = 0; w < kRowThreads / 32; ++w) zs += dscr[w];
+    dscr[32] = zs;
+  }
+  __syncthreads();
+  const float z = static_cast<float>(dscr[32]);
+
+  // ---- the fixed-point mass above this thread's keys ----
+  uint64_t msum = 0ull;
+  for (int q = kKeysPerThread / 4 - 1; q >= 0; --q) {
+    const uint4 w = h4[q];
+    const uint32_t cnt[4] = {w.w, w.z, w.y, w.x};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t key = kl + 4u * static_cast<uint32_t>(q) + 3u - static_cast<uint32_t>(i);
+      const uint32_t n = topk_count(key, cnt[i], T, need);
+      if (n != 0u)
+        msum += static_cast<uint64_t>(n) * prob_to_fixed(__fdiv_rn(expf(tail_logit<DT>(p, key) - mf), z));
+    }
+  }
+  uint64_t mtot = 0ull;
+  const uint64_t mbase = block_incl_scan<uint64_t, kRowThreads>(msum, qscr, &mtot) - msum;
+
+  // The first group (from the largest key) of this thread's range whose end meets `pred(end
+  // mass, p)`: its key rank t * 64 + j (or kNone), and the mass before it in *start.
+  constexpr int kNone = 0x7FFFFFFF;
+  auto first_group = [&](int mode, float target, uint64_t* start, uint32_t* n_out, uint64_t* pf_out,
+                         float* pr_out) -> int {
+    uint64_t run = mbase;
+    for (int q = kKeysPerThread / 4 - 1; q >= 0; --q) {
+      const uint4 w = h4[q];
+      const uint32_t cnt[4] = {w.w, w.z, w.y, w.x};
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t key = kl + 4u * static_cast<uint32_t>(q) + 3u - static_cast<uint32_t>(i);
+        const uint32_t n = topk_count(key, cnt[i], T, need);
+        if (n == 0u) continue;
+        const float pr = __fdiv_rn(expf(tail_logit<DT>(p, key) - mf), z);
+        const uint64_t pf = prob_to_fixed(pr);
+        const uint64_t end = run + static_cast<uint64_t>(n) * pf;
+        const bool hit = mode == 0 ? !((fixed_to_float(end) - pr) < pp) : fixed_to_float(end) >= target;
+        if (hit) {
+          *start = run;
+          *n_out = n;
+          *pf_out = pf;
+          *pr_out = pr;
+          return t * kKeysPerThread + (kKeysPerThread - 1 - (4 * q + 3 - i));
+        }
+        run = end;
+      }
+    }
+    return kNone;
+  };
+
+  // ---- the cut: xr = the exact mass through r ----
+  uint64_t xr = mtot;
+  if (pp < 1.0f) {
+    uint64_t start = 0ull, pf = 0ull;
+    uint32_t n = 0u;
+    float pr = 0.0f;
+    const int mine = first_group(0, 0.0f, &start, &n, &pf, &pr);
+    const int gc = block_min<kRowThreads>(mine, iscr);
+    if (gc != kNone && mine == gc) {
+      // the first position j of the group that meets the condition (it holds at j = n - 1)
+      uint32_t lo = 0u, hi = n - 1u;
+      while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (!((fixed_to_float(start + static_cast<uint64_t>(mid + 1u) * pf) - pr) < pp)) hi = mid;
+        else lo = mid + 1u;
+      }
+      found[0] = start + static_cast<uint64_t>(lo) * pf;
+    }
+    __syncthreads();
+    if (gc != kNone) xr = found[0];
+  }
+  const float zp = fixed_to_float(xr);
+  const float target = __fmul_rn(row_uniform(p, b), zp);
+
+  // ---- the draw: the first element with c_i >= target ----
+  {
+    uint64_t start = 0ull, pf = 0ull;
+    uint32_t n = 0u;
+    float pr = 0.0f;
+    const int mine = first_group(1, target, &start, &n, &pf, &pr);
+    const int gd = block_min<kRowThreads>(mine, iscr);
+    if (mine == gd && gd != kNone) {
+      uint32_t lo = 0u, hi = n - 1u;
+      while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (fixed_to_float(start + static_cast<uint64_t>(mid + 1u) * pf) >= target) hi = mid;
+        else lo = mid + 1u;
+      }
+      rr[0] = static_cast<uint32_t>(FS_ROW_OK);
+      rr[1] = static_cast<uint32_t>(kKeys - 1 - gd);  // the key of rank gd from the top
+      rr[2] = lo;
+      rr[3] = 1u;
+    }
+    if (gd == kNone && t == 0) {  // (not reached: the last group with elements meets the draw)
+      rr[0] = static_cast<uint32_t>(FS_ROW_OK);
+      rr[3] = 0u;
+    }
+  }
+}
+
+template <int DT, int C>
+__global__ void __launch_bounds__(NT, min_ctas_for(C))
+    fs_wide_count_kernel(const Params p, const uint32_t* __restrict__ res, uint32_t* __restrict__ cnt) {
+  __shared__ uint32_t scr[40];
+  const int S = static_cast<int>(gridDim.x);
+  const int s = blockIdx.x;
+  const int b = blockIdx.y;
+  const int t = threadIdx.x;
+  const uint32_t* rr = res + static_cast<size_t>(b) * kWideRes;
+  if (rr[3] == 0u) {
+    if (t == 0) cnt[static_cast<size_t>(b) * S + s] = 0u;
+    return;
+  }
+  const uint32_t gkey = rr[1];
+  const int vbase = s * C * NT;
+  uint4 v[C];
+  load_slice<DT, C>(p, b, vbase, v);
+  uint32_t mine = 0u;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int e0 = (vbase + c * NT + t) * 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mine += (e0 + j < p.vocab && chunk_key(v[c], j) == gkey) ? 1u : 0u;
+  }
+  const uint32_t total = block_sum<uint32_t, NT>(mine, scr);
+  if (t == 0) cnt[static_cast<size_t>(b) * S + s] = total;
+}
+
+template <int DT, int C>
+__global__ void __launch_bounds__(NT, min_ctas_for(C))
+    fs_wide_pick_kernel(const Params p, const uint32_t* __restrict__ res, const uint32_t* __restrict__ cnt) {
+  __shared__ uint32_t scr[40];
+  const int S = static_cast<int>(gridDim.x);
+  const int s = blockIdx.x;
+  const int b = blockIdx.y;
+  const int t = threadIdx.x;
+  const uint32_t* rr = res + static_cast<size_t>(b) * kWideRes;
+  if (rr[3] == 0u) return;
+  const uint32_t gkey = rr[1], jpick = rr[2];
+  uint32_t before = 0u;
+  for (int r = 0; r < s; ++r) before += cnt[static_cast<size_t>(b) * S + r];
+  const uint32_t here = cnt[static_cast<size_t>(b) * S + s];
+  if (!(jpick >= before && jpick < before + here)) return;  // (the same in every thread)
+  const int vbase = s * C * NT;
+  uint4 v[C];
+  load_slice<DT, C>(p, b, vbase, v);
+  // chunks in id order: chunk c of every thread, threads in order, lanes in order
+  uint32_t chunk_base = before;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int e0 = (vbase + c * NT + t) * 8;
+    uint32_t hits = 0u;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (e0 + j < p.vocab && chunk_key(v[c], j) == gkey) hits |= 1u << j;
+    const uint32_t n = static_cast<uint32_t>(__popc(hits));
+    uint32_t ctot = 0u;
+    const uint32_t excl = block_incl_scan<uint32_t, NT>(n, scr, &ctot) - n;
+    if (jpick >= chunk_base + excl && jpick < chunk_base + excl + n) {
+      for (uint32_t r = chunk_base + excl; r < jpick; ++r) hits &= hits - 1u;
+      if (p.out != nullptr) p.out[b] = static_cast<int64_t>(p.id_base) + e0 + (__ffs(hits) - 1);
+      if (p.status != nullptr) p.status[b] = FS_ROW_OK;
+    }
+    chunk_base += ctot;
+  }
+}
+
+// ---- asynchronous copies (row merge) ------------------------------------------------------
 
 __device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_init_fence() {
-  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-// One poll of the phase with the given parity; true once it has completed.
-__device__ __forceinline__ bool mbar_done(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0u;
-}
-
-// Bounded wait for a stage; false if it did not complete within kWaitLimit polls.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (long long i = 0; i < kWaitLimit; ++i) {
-    if (mbar_done(bar, parity)) return true;
-  }
-  return false;
 }
 
 // Per-thread 16-byte global -> shared copy through L2 only (both addresses 16-byte aligned); the
@@ -1157,21 +1500,6 @@ __device__ __forceinline__ void cp_async_16(void* dst, const void* src) {
 }
 
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
-
-// Orders this CTA's earlier generic-proxy accesses of shared memory before later bulk copies.
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-}
-
-// Global -> shared bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned),
-// completion signalled on `bar`.
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
 
 // ------------------------------------------------------------------------------------------
 // Streaming path for large batches: two launches, no cross-CTA waiting.
@@ -1818,321 +2146,6 @@ __global__ void __launch_bounds__(NT) fs_rowmerge_kernel(const Params p, const u
   else sample_tail_warp<DT, 8>(p, b, dst, kk, pp, u, prob);
 }
 
-// ------------------------------------------------------------------------------------------
-// Persistent row-streaming path for large batches: one launch, one CTA per SM, no workspace.
-// CTA c takes rows c, c + G, c + 2G, ... (G = grid size) and streams each row through a ring of
-// `ring` shared-memory stages of kStageBytes. Thread 0 fills the stages with bulk copies
-// (cp.async.bulk, completion counted on one mbarrier per stage) up to `ring` stages ahead, across
-// row boundaries, so HBM keeps streaming while a stage is filtered and while a finished row is
-// sampled. Per row:
-//   stage 0: L = the kk-th largest of the stage's sub-chunk maxima (at least kk elements >= L);
-//   every stage: a thread whose maximum is >= L appends its elements >= L to the candidate
-//     buffer (shared memory); when the buffer passes half its capacity it is cut down to the
-//     elements >= its exact kk-th largest key, which also raises L;
-//   end: the exact kk-th key E of the candidates, the candidates >= E, and the common row tail.
-// L never exceeds the kk-th largest logit of the part of the row seen so far, so the candidates
-// always hold the row's top-kk. A row whose candidates overflow the buffer (heavy ties) is
-// re-read from L2/HBM by the exact radix select.
-// ------------------------------------------------------------------------------------------
-
-constexpr int kStageChunks = 8;                     // 16-byte vectors per thread per stage
-constexpr int kStageElems = kStageChunks * NT * 8;  // 16384 logits
-constexpr int kStageBytes = kStageElems * 2;        // 32 KiB
-constexpr int kMaxRing = 6;
-constexpr int kRingOffset = 128;                    // mbarriers, then the stages (128-byte aligned)
-template <int DT>
-__global__ void __launch_bounds__(NT, 1) fs_rowstream_kernel(const Params p) {
-  Shared& sh = *reinterpret_cast<Shared*>(g_smem);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(g_smem + sizeof(Shared));
-  uint4* ring = reinterpret_cast<uint4*>(g_smem + sizeof(Shared) + kRingOffset);
-  uint64_t* cand = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(ring) +
-                                               static_cast<size_t>(p.ring) * kStageBytes);
-  uint64_t* spare = cand + p.cap;
-  float* prob = reinterpret_cast<float*>(spare + p.cap);
-  float* cum = prob + p.cap;
-  uint8_t* pairs = reinterpret_cast<uint8_t*>(cum + p.cap);  // per warp: 32 * kStageChunks pairs
-
-  const int t = threadIdx.x;
-  const int G = static_cast<int>(gridDim.x);
-  const int V = p.vocab;
-  const int R = p.ring;
-  const int nst = p.nst;
-  const uint32_t cap = static_cast<uint32_t>(p.cap);
-  // past `high` candidates the buffer is cut back to about kk (the row end ranks up to NT directly)
-  const uint32_t high = min(cap / 2u, max(static_cast<uint32_t>(NT), 4u * static_cast<uint32_t>(p.K)));
-  const int nrows = (p.batch - static_cast<int>(blockIdx.x) + G - 1) / G;
-  const int total = nrows * nst;
-
-  // thread 0: stage q of this CTA = stage q % nst of its row q / nst, into ring slot q % R
-  auto issue = [&](int q) {
-    const int i = q / nst;
-    const int st = q - i * nst;
-    const int64_t b = static_cast<int64_t>(blockIdx.x) + static_cast<int64_t>(i) * G;
-    const int off = st * kStageElems;
-    const uint32_t bytes = static_cast<uint32_t>(min(kStageElems, V - off)) * 2u;
-    uint64_t* bar = &bars[q % R];
-    mbar_expect_tx(bar, bytes);
-    bulk_load(ring + static_cast<size_t>(q % R) * (kStageBytes / 16), p.logits + b * p.row_stride + off, bytes,
-              bar);
-  };
-
-  if (t == 0) {
-    for (int r = 0; r < R; ++r) mbar_init(&bars[r], 1u);
-    mbar_init_fence();
-  }
-  sh.h1[t] = 0u;
-  sh.h2[t] = 0u;
-  if (t < 16) sh.ctl[t] = 0u;
-  __syncthreads();
-  if (t == 0) {
-    for (int q = 0; q < min(R, total); ++q) issue(q);
-  }
-
-  bool timed_out = false;
-  int q = 0;
-  int i = 0;
-  for (; i < nrows; ++i) {
-    const int b = static_cast<int>(blockIdx.x) + i * G;
-    int kk;
-    float pp;
-    bool bad;
-    row_params(p, b, &kk, &pp, &bad);
-    const float u = t < 32 ? row_uniform(p, b) : 0.0f;
-    uint32_t lkey = 0u;
-    uint32_t rflags = 0u;
-    bool overflow = false;
-    bool hit_high = false;  // one of this thread's appends went past `high`
-    uint64_t* cbuf = cand;
-    uint64_t* sbuf = spare;
-
-    for (int st = 0; st < nst; ++st, ++q) {
-      const int slot = q % R;
-      if (!timed_out) timed_out = !mbar_wait(&bars[slot], static_cast<uint32_t>((q / R) & 1));
-      const int off = st * kStageElems;
-      const uint4* stage = ring + static_cast<size_t>(slot) * (kStageBytes / 16);
-      uint4 v[kStageChunks];
-      uint32_t validm = 0u;
-#pragma unroll
-      for (int c = 0; c < kStageChunks; ++c) {
-        const bool valid = off + (c * NT + t) * 8 < V;
-        v[c] = valid ? stage[c * NT + t] : make_uint4(Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2,
-                                                      Fmt<DT>::kNegInf2);
-        validm |= static_cast<uint32_t>(valid) << c;
-      }
-      uint32_t mx[4] = {Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2, Fmt<DT>::kNegInf2};
-#pragma unroll
-      for (int c = 0; c < kStageChunks; ++c) {
-#pragma unroll
-        for (int w = 0; w < 4; ++w) mx[w] = pair_max_nan<DT>(mx[w], word_of(v[c], w));
-      }
-      const uint32_t m2 = pair_max_nan<DT>(pair_max_nan<DT>(mx[0], mx[2]), pair_max_nan<DT>(mx[1], mx[3]));
-      const uint32_t mbits = half_max_nan<DT>(m2 & 0xFFFFu, m2 >> 16);
-      if (Fmt<DT>::is_nan(mbits)) {
-        rflags |= kFlagNaN;
-      } else {
-        if (mbits == Fmt<DT>::kPosInf) rflags |= kFlagPosInf;
-        if (mbits != Fmt<DT>::kNegInf) rflags |= kFlagAboveNegInf;
-      }
-      if (st == 0) {  // sub-chunk maxima for the first threshold
-        const int mpt = p.mpt;
-        if (mpt == 8) {
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            sh.mkeys[t * 8 + 2 * w] = order_key(mx[w] & 0xFFFFu);
-            sh.mkeys[t * 8 + 2 * w + 1] = order_key(mx[w] >> 16);
-          }
-        } else if (mpt == 4) {
-          const uint32_t a = pair_max_nan<DT>(mx[0], mx[2]), c2 = pair_max_nan<DT>(mx[1], mx[3]);
-          sh.mkeys[t * 4 + 0] = order_key(a & 0xFFFFu);
-          sh.mkeys[t * 4 + 1] = order_key(a >> 16);
-          sh.mkeys[t * 4 + 2] = order_key(c2 & 0xFFFFu);
-          sh.mkeys[t * 4 + 3] = order_key(c2 >> 16);
-        } else if (mpt == 2) {
-          sh.mkeys[t * 2 + 0] = order_key(m2 & 0xFFFFu);
-          sh.mkeys[t * 2 + 1] = order_key(m2 >> 16);
-        } else {
-          sh.mkeys[t] = order_key(mbits);
-        }
-      }
-      // S1: the previous stage is finished by every thread (its slot may be refilled) and its
-      // appends are complete. A timeout or a candidate buffer past `high` asks for attention;
-      // otherwise nothing else synchronises the stage.
-      const int attention = __syncthreads_or((timed_out || hit_high) ? 1 : 0);
-      if (t == 0 && q >= 1 && q - 1 + R < total) {
-        fence_proxy_async_smem();
-        issue(q - 1 + R);
-      }
-      if (attention) {
-        if (timed_out) sh.ctl[kCtlTmo] = 1u;
-        __syncthreads();
-        if (sh.ctl[kCtlTmo] != 0u) {
-          timed_out = true;
-          break;
-        }
-        hit_high = false;
-        const uint32_t n = sh.ctl[kCtlN];  // stable: no thread appends before the next barrier
-        if (n > cap) {
-          overflow = true;
-        } else if (n > high) {
-          for (uint32_t j = t; j < n; j += NT) sh.mkeys[j] = packed_key(cbuf[j]);
-          __syncthreads();
-          const uint32_t e = kth_largest_key(sh.mkeys, static_cast<int>(n), kk, sh.h1, sh.h2, &sh.ctl[kCtlScr0]);
-          sh.h1[t] = 0u;
-          sh.h2[t] = 0u;
-          for (uint32_t j = t; j < n; j += NT) {
-            if (sh.mkeys[j] >= e) sbuf[atomicAdd(&sh.ctl[kCtlLocal], 1u)] = cbuf[j];
-          }
-          __syncthreads();
-          const uint32_t kept = sh.ctl[kCtlLocal];
-          __syncthreads();
-          if (t == 0) {
-            sh.ctl[kCtlN] = kept;
-            sh.ctl[kCtlLocal] = 0u;
-          }
-          uint64_t* tmp = cbuf;
-          cbuf = sbuf;
-          sbuf = tmp;
-          lkey = max(lkey, e);
-        }
-        __syncthreads();
-      }
-      if (st == 0) {
-        const uint32_t kth = kth_largest_key(sh.mkeys, NT * p.mpt, kk, sh.h1, sh.h2, &sh.ctl[kCtlScr0]);
-        lkey = max(kth, order_key(Fmt<DT>::kNegInf));
-        sh.h1[t] = 0u;
-        sh.h2[t] = 0u;
-      }
-      // Filter, warp-cooperative: a lane whose maximum reaches L marks its chunks that hold an
-      // element >= L; the warp lists the marked (lane, chunk) pairs, hands one pair to each
-      // lane, which re-reads that chunk from the stage (refilled only after the next S1), and
-      // appends every hit with one shared atomic per warp.
-      if (!overflow) {
-        const bool hot = !Fmt<DT>::is_nan(mbits) && order_key(mbits) >= lkey;
-        if (__ballot_sync(0xFFFFFFFFu, hot) != 0u) {
-          const int lane = t & 31;
-          const uint32_t lbits = key_to_bits(lkey);
-          const uint32_t l2 = lbits | (lbits << 16);
-          uint32_t cm = 0u;
-          if (hot) {
-#pragma unroll
-            for (int c = 0; c < kStageChunks; ++c) {
-              const uint32_t any = pair_ge_mask<DT>(v[c].x, l2) | pair_ge_mask<DT>(v[c].y, l2) |
-                                   pair_ge_mask<DT>(v[c].z, l2) | pair_ge_mask<DT>(v[c].w, l2);
-              cm |= (any != 0u ? 1u : 0u) << c;
-            }
-            cm &= validm;
-          }
-          const int np = __popc(cm);
-          const int pincl = warp_incl_scan(np);
-          const int npairs = __shfl_sync(0xFFFFFFFFu, pincl, 31);
-          uint8_t* wp = pairs + (t >> 5) * (32 * kStageChunks);
-          int k = pincl - np;
-          while (cm != 0u) {
-            const int c = __ffs(cm) - 1;
-            cm &= cm - 1u;
-            wp[k++] = static_cast<uint8_t>((lane << 3) | c);
-          }
-          __syncwarp();
-          for (int base = 0; base < npairs; base += 32) {
-            const int pi = base + lane;
-            uint32_t hits = 0u;  // bit 2w + h: half h of word w of the chunk is >= L
-            uint4 x = make_uint4(0u, 0u, 0u, 0u);
-            int e0 = 0;
-            if (pi < npairs) {
-              const int pr = wp[pi];
-              const int owner = (t & ~31) + (pr >> 3);
-              const int c = pr & 7;
-              x = stage[c * NT + owner];
-              e0 = off + (c * NT + owner) * 8;
-#pragma unroll
-              for (int w = 0; w < 4; ++w) {
-                const uint32_t m = pair_ge_mask<DT>(word_of(x, w), l2);
-                hits |= ((m & 1u) | ((m >> 15) & 2u)) << (2 * w);
-              }
-            }
-            const int nh = __popc(hits);
-            const int hincl = warp_incl_scan(nh);
-            const int htot = __shfl_sync(0xFFFFFFFFu, hincl, 31);
-            uint32_t hbase = 0u;
-            if (lane == 31 && htot > 0) hbase = atomicAdd(&sh.ctl[kCtlN], static_cast<uint32_t>(htot));
-            hbase = __shfl_sync(0xFFFFFFFFu, hbase, 31);
-            uint32_t j = hbase + static_cast<uint32_t>(hincl - nh);
-            while (hits != 0u) {
-              const int bit = __ffs(hits) - 1;
-              hits &= hits - 1u;
-              const int w = bit >> 1;
-              const uint32_t word = w == 0 ? x.x : w == 1 ? x.y : w == 2 ? x.z : x.w;
-              const uint32_t h16 = (word >> (16 * (bit & 1))) & 0xFFFFu;
-              if (j < cap) cbuf[j] = pack(order_key(h16), p.id_base + e0 + bit);
-              hit_high |= j >= high;
-              ++j;
-            }
-          }
-        }
-      }
-    }
-    if (timed_out) break;
-
-    // ---- end of row ----
-    rflags = __reduce_or_sync(0xFFFFFFFFu, rflags);
-    if ((t & 31) == 0 && rflags != 0u) atomicOr(&sh.ctl[kCtlFlags], rflags);
-    __syncthreads();
-    const uint32_t n = sh.ctl[kCtlN];
-    const uint32_t f = sh.ctl[kCtlFlags];
-    __syncthreads();
-    if (t == 0) {
-      sh.ctl[kCtlN] = 0u;
-      sh.ctl[kCtlFlags] = 0u;
-    }
-    int status = FS_ROW_OK;
-    if (bad) status = FS_ROW_BAD_PARAM;
-    else if (f & kFlagNaN) status = FS_ROW_NAN;
-    else if (f & kFlagPosInf) status = FS_ROW_POSINF;
-    else if (!(f & kFlagAboveNegInf)) status = FS_ROW_ALL_NEGINF;
-    if (status != FS_ROW_OK) {
-      write_invalid_row(p, b, status);
-    } else if (overflow || n > cap) {
-      const uint16_t* row = p.logits + static_cast<int64_t>(b) * p.row_stride;
-      const int nchunks = (V + NT * 8 - 1) / (NT * 8);
-      const int got = span_exact_topk<DT>(sh, row, V, p.vec, p.id_base, 0, nchunks, kk, sbuf);
-      __syncthreads();
-      sh.ctl[kCtlLocal] = 0u;  // (every thread writes the same value; read only after a barrier)
-      finish_row<DT>(p, b, sbuf, got, cbuf, kk, pp, u, prob, cum, sh);
-    } else if (n <= static_cast<uint32_t>(NT)) {
-      // every candidate is ranked against all others: the top kk come out sorted
-      finish_row<DT>(p, b, cbuf, static_cast<int>(n), sbuf, kk, pp, u, prob, cum, sh);
-    } else {
-      for (uint32_t j = t; j < n; j += NT) sh.mkeys[j] = packed_key(cbuf[j]);
-      __syncthreads();
-      const uint32_t e = kth_largest_key(sh.mkeys, static_cast<int>(n), kk, sh.h1, sh.h2, &sh.ctl[kCtlScr0]);
-      sh.h1[t] = 0u;
-      sh.h2[t] = 0u;
-      for (uint32_t j = t; j < n; j += NT) {
-        if (sh.mkeys[j] >= e) sbuf[atomicAdd(&sh.ctl[kCtlLocal], 1u)] = cbuf[j];
-      }
-      __syncthreads();
-      const int nsel = static_cast<int>(sh.ctl[kCtlLocal]);
-      __syncthreads();
-      if (t == 0) sh.ctl[kCtlLocal] = 0u;
-      finish_row<DT>(p, b, sbuf, nsel, cbuf, kk, pp, u, prob, cum, sh);
-    }
-    // the next row reuses the buffers and histograms
-    __syncthreads();
-    sh.h1[t] = 0u;
-    sh.h2[t] = 0u;
-  }
-
-  if (timed_out) {
-    // rows this CTA did not finish get no result; then give the copies in flight a bounded
-    // chance to land before the CTA's shared memory is released
-    for (int r = i; r < nrows; ++r) write_invalid_row(p, static_cast<int>(blockIdx.x) + r * G, FS_ROW_TIMEOUT);
-    if (t == 0) {
-      const int last = min(total, q + R + 1);
-      for (int qq = q; qq < last; ++qq) (void)mbar_wait(&bars[qq % R], static_cast<uint32_t>((qq / R) & 1));
-    }
-  }
-}
-
 // Merge of per-shard candidate blocks [parts, B, K + 1] for vocab-sharded tensor parallelism:
 // one CTA per row, exact top-k over parts*K packed candidates, then the same tail.
 template <int DT>
@@ -2327,12 +2340,11 @@ constexpr int kMaxCap = 8192;
 constexpr int64_t kStreamMaxK = 256;     // streaming path: top-K bound
 constexpr int64_t kStreamMinBatch = 96;   // AUTO: rows from which the streaming path is used
 constexpr int64_t kStreamAutoMaxK = 128;  // AUTO: largest k for which it is used
-constexpr size_t kPersistSmemBudget = 227 * 1024;  // opt-in dynamic shared memory per CTA
 
 // Plan of one call: cluster size, chunks per thread, survivor capacity, maxima granularity.
 fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t path, PlanOut* out) {
-  if (path < FS_PATH_AUTO || path > FS_PATH_PERSIST) {
-    set_error("path must be one of FS_PATH_AUTO, FS_PATH_CLUSTER, FS_PATH_STREAM, FS_PATH_PERSIST; got %d", path);
+  if (path < FS_PATH_AUTO || path > FS_PATH_WIDE) {
+    set_error("path must be one of FS_PATH_AUTO, FS_PATH_CLUSTER, FS_PATH_STREAM, FS_PATH_WIDE; got %d", path);
     return FS_EINVAL;
   }
   const int64_t per_cta_chunk = static_cast<int64_t>(NT) * 8;  // elements per chunk per CTA
@@ -2378,8 +2390,11 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t pat
   }
   int cap = std::max(1024, pow2_ceil(4 * K));
   cap = std::min(cap, kMaxCap);
-  if (cap < K) {
-    set_error("top_k of %lld exceeds the %d-candidate capacity of this build",
+  // top_k beyond the survivor buffer takes the wide path (token ids and row status only)
+  const bool wide = path == FS_PATH_WIDE || (path == FS_PATH_AUTO && K > kMaxCap);
+  if (!wide && cap < K) {
+    set_error("top_k of %lld exceeds the %d-candidate capacity of the cluster and streaming paths "
+              "(FS_PATH_AUTO or FS_PATH_WIDE take any top_k for token ids)",
               static_cast<long long>(K), kMaxCap);
     return FS_EUNSUPPORTED;
   }
@@ -2396,32 +2411,13 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t pat
   out->merge_cap = 0;
   out->merge_smem = 0;
   out->workspace = 0;
-  out->persist = 0;
-  out->ring = 0;
-  out->nst = 0;
-
-  // persistent row-streaming path: whole rows through a ring of shared-memory stages
-  const bool want_persist = path == FS_PATH_PERSIST;
-  if (path == FS_PATH_PERSIST && K > kStreamMaxK) {
-    set_error("the persistent path supports top_k <= %lld", static_cast<long long>(kStreamMaxK));
-    return FS_EUNSUPPORTED;
-  }
-  if (want_persist) {
-    const int pcap = std::max(1024, pow2_ceil(8 * K));
-    const size_t fixed = sizeof(Shared) + kRingOffset + static_cast<size_t>(pcap) * 24 + NT * kStageChunks;
-    const int ring = static_cast<int>(
-        std::min<size_t>(kMaxRing, (kPersistSmemBudget - fixed) / static_cast<size_t>(kStageBytes)));
-    out->persist = 1;
-    out->ring = ring;
-    out->nst = static_cast<int>((V + kStageElems - 1) / kStageElems);
-    out->splits = 1;
-    out->chunks = kStageChunks;
-    out->capacity = pcap;
-    out->mpt = static_cast<int>(std::min<int64_t>(8, pow2_ceil((4 * K + NT - 1) / NT)));
-    out->mgroup = 1;
-    out->mcta = NT * out->mpt;
-    out->slot = 0;
-    out->smem = static_cast<int>(fixed + static_cast<size_t>(ring) * kStageBytes);
+  out->wide = wide ? 1 : 0;
+  if (wide) {
+    // per-key counts [B][65536], slice maxima and flags [B][S] x 2, locate counts [B][S], row
+    // results [B][4]
+    out->smem = 0;
+    out->workspace = static_cast<uint64_t>(B) * kKeys * 4 + static_cast<uint64_t>(B) * S * 12 +
+                     static_cast<uint64_t>(B) * kWideRes * 4 + 256;
     return FS_OK;
   }
 
@@ -2466,50 +2462,55 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t pat
   return FS_OK;
 }
 
-// Per-kernel attribute state: the dynamic shared memory limit already granted and whether
-// non-portable cluster sizes were enabled. Set once per kernel and size, not on every launch.
+// Kernel attribute state of one (kernel, device) pair: the dynamic shared memory limit already
+// granted and whether non-portable cluster sizes were enabled. Function attributes are per
+// device, so a process that drives several GPUs keeps one record per device; each is set once
+// per kernel and size, not on every launch.
 struct KernelState {
   const void* fn;
+  int dev;
   int smem_granted;
   bool nonportable;
 };
 
+constexpr int kMaxKernelStates = 512;
+
+// The record of (fn, dev), created on first use; null when the table is full.
+KernelState* kernel_state(const void* fn, int dev) {
+  static KernelState states[kMaxKernelStates];
+  static int n_states = 0;
+  for (int i = 0; i < n_states; ++i)
+    if (states[i].fn == fn && states[i].dev == dev) return &states[i];
+  if (n_states == kMaxKernelStates) return nullptr;
+  states[n_states] = KernelState{fn, dev, 0, false};
+  return &states[n_states++];
+}
+
 static fs_status prepare_kernel(KernelFn fn, int S, int smem) {
   static std::mutex mu;
-  static KernelState states[64];
-  static int n_states = 0;
   const void* f = reinterpret_cast<const void*>(fn);
-  std::lock_guard<std::mutex> lock(mu);
-  KernelState* ks = nullptr;
-  for (int i = 0; i < n_states; ++i)
-    if (states[i].fn == f) ks = &states[i];
-  if (ks == nullptr) {
-    if (n_states == 64) {
-      set_error("kernel state table full");
-      return FS_ELAUNCH;
-    }
-    ks = &states[n_states++];
-    *ks = KernelState{f, 0, false};
-  }
-  // the attribute is per device; re-grant when the current device has not seen this size
   int dev = 0;
-  cudaGetDevice(&dev);
-  static unsigned long long seen_devices[64] = {};
-  const int idx = static_cast<int>(ks - states);
-  const bool new_device = (seen_devices[idx] & (1ull << (dev & 63))) == 0;
-  if (new_device || smem > ks->smem_granted) {
-    const int grant = std::max(smem, ks->smem_granted);
-    cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, grant);
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_error("cudaGetDevice: %s", cudaGetErrorString(e));
+    return FS_ELAUNCH;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  KernelState* ks = kernel_state(f, dev);
+  if (ks == nullptr) {
+    set_error("kernel state table full (%d kernel x device pairs)", kMaxKernelStates);
+    return FS_ELAUNCH;
+  }
+  if (smem > ks->smem_granted) {
+    e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) {
-      set_error("cudaFuncSetAttribute(max dynamic smem %d): %s", grant, cudaGetErrorString(e));
+      set_error("cudaFuncSetAttribute(max dynamic smem %d): %s", smem, cudaGetErrorString(e));
       return FS_ELAUNCH;
     }
-    ks->smem_granted = grant;
-    if (new_device) ks->nonportable = false;
-    seen_devices[idx] |= 1ull << (dev & 63);
+    ks->smem_granted = smem;
   }
   if (S > 8 && !ks->nonportable) {
-    cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    e = cudaFuncSetAttribute(f, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) {
       set_error("cudaFuncSetAttribute(non-portable cluster): %s", cudaGetErrorString(e));
       return FS_ELAUNCH;
@@ -2548,6 +2549,73 @@ static fs_status launch_cluster(int dtype, const PlanOut& plan, int64_t B, const
   if (e != cudaSuccess) {
     set_error("cluster launch (splits=%d chunks=%d smem=%d B=%lld): %s", plan.splits, plan.chunks,
               plan.smem, static_cast<long long>(B), cudaGetErrorString(e));
+    return FS_ELAUNCH;
+  }
+  return FS_OK;
+}
+
+template <int DT, int C>
+struct WideKernels {
+  static fs_status launch(const fs_sample_args* a, const PlanOut& plan, const Params& prm, uint32_t* hist,
+                          uint32_t* smax, uint32_t* sflag, uint32_t* cnt, uint32_t* res, cudaStream_t stream) {
+    const dim3 grid(plan.splits, static_cast<unsigned>(a->batch), 1);
+    fs_wide_hist_kernel<DT, C><<<grid, NT, 0, stream>>>(prm, hist, smax, sflag);
+    fs_wide_row_kernel<DT><<<static_cast<unsigned>(a->batch), kRowThreads, 0, stream>>>(prm, hist, smax, sflag, res,
+                                                                                          plan.splits);
+    fs_wide_count_kernel<DT, C><<<grid, NT, 0, stream>>>(prm, res, cnt);
+    fs_wide_pick_kernel<DT, C><<<grid, NT, 0, stream>>>(prm, res, cnt);
+    return FS_OK;
+  }
+};
+
+template <int DT>
+static fs_status launch_wide_dt(const fs_sample_args* a, const PlanOut& plan, const Params& prm, uint32_t* hist,
+                                uint32_t* smax, uint32_t* sflag, uint32_t* cnt, uint32_t* res, cudaStream_t st) {
+  switch (plan.chunks) {
+    case 1: return WideKernels<DT, 1>::launch(a, plan, prm, hist, smax, sflag, cnt, res, st);
+    case 2: return WideKernels<DT, 2>::launch(a, plan, prm, hist, smax, sflag, cnt, res, st);
+    case 3: return WideKernels<DT, 3>::launch(a, plan, prm, hist, smax, sflag, cnt, res, st);
+    case 4: return WideKernels<DT, 4>::launch(a, plan, prm, hist, smax, sflag, cnt, res, st);
+    case 5: return WideKernels<DT, 5>::launch(a, plan, prm, hist, smax, sflag, cnt, res, st);
+    case 6: return WideKernels<DT, 6>::launch(a, plan, prm, hist, smax, sflag, cnt, res, st);
+    case 8: return WideKernels<DT, 8>::launch(a, plan, prm, hist, smax, sflag, cnt, res, st);
+    case 10: return WideKernels<DT, 10>::launch(a, plan, prm, hist, smax, sflag, cnt, res, st);
+    case 12: return WideKernels<DT, 12>::launch(a, plan, prm, hist, smax, sflag, cnt, res, st);
+    case 16: return WideKernels<DT, 16>::launch(a, plan, prm, hist, smax, sflag, cnt, res, st);
+    default:
+      set_error("no wide-path kernels for %d chunks", plan.chunks);
+      return FS_EUNSUPPORTED;
+  }
+}
+
+// The wide path's launches: the histogram is cleared first (the workspace needs no
+// initialisation from the caller), then the four kernels, stream-ordered.
+static fs_status launch_wide(const fs_sample_args* a, const PlanOut& plan, const Params& prm, cudaStream_t stream) {
+  if (a->workspace == nullptr || a->workspace_bytes < plan.workspace) {
+    set_error("the wide path needs %llu bytes of workspace (got %llu)",
+              static_cast<unsigned long long>(plan.workspace),
+              static_cast<unsigned long long>(a->workspace == nullptr ? 0 : a->workspace_bytes));
+    return FS_EWORKSPACE;
+  }
+  const uintptr_t base = (reinterpret_cast<uintptr_t>(a->workspace) + 255) & ~static_cast<uintptr_t>(255);
+  const size_t B = static_cast<size_t>(a->batch), S = static_cast<size_t>(plan.splits);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(base);
+  uint32_t* smax = hist + B * kKeys;
+  uint32_t* sflag = smax + B * S;
+  uint32_t* cnt = sflag + B * S;
+  uint32_t* res = cnt + B * S;
+  cudaError_t e = cudaMemsetAsync(hist, 0, B * kKeys * sizeof(uint32_t), stream);
+  if (e != cudaSuccess) {
+    set_error("wide path histogram clear: %s", cudaGetErrorString(e));
+    return FS_ELAUNCH;
+  }
+  const fs_status st = a->dtype == FS_BF16 ? launch_wide_dt<1>(a, plan, prm, hist, smax, sflag, cnt, res, stream)
+                                           : launch_wide_dt<0>(a, plan, prm, hist, smax, sflag, cnt, res, stream);
+  if (st != FS_OK) return st;
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("wide path launch (splits=%d chunks=%d B=%lld): %s", plan.splits, plan.chunks,
+              static_cast<long long>(a->batch), cudaGetErrorString(e));
     return FS_ELAUNCH;
   }
   return FS_OK;
@@ -2712,43 +2780,6 @@ static fs_status launch_stream(const fs_sample_args* a, const PlanOut& plan, con
   return FS_OK;
 }
 
-// SMs of the current device (cached per device).
-static int sm_count() {
-  static int counts[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
-  if (counts[dev] == 0) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
-    counts[dev] = n;
-  }
-  return counts[dev];
-}
-
-static fs_status launch_persist(int dtype, const PlanOut& plan, int64_t B, Params prm, cudaStream_t stream) {
-  KernelFn fn = dtype == FS_BF16 ? reinterpret_cast<KernelFn>(fs_rowstream_kernel<1>)
-                                 : reinterpret_cast<KernelFn>(fs_rowstream_kernel<0>);
-  fs_status st = prepare_kernel(fn, 1, plan.smem);
-  if (st != FS_OK) return st;
-  const int nsm = sm_count();
-  if (nsm <= 0) {
-    set_error("could not read the SM count of the current device");
-    return FS_ELAUNCH;
-  }
-  prm.batch = static_cast<int32_t>(B);
-  prm.ring = plan.ring;
-  prm.nst = plan.nst;
-  const int grid = static_cast<int>(std::min<int64_t>(B, nsm));
-  using PersistFn = void (*)(const Params);
-  reinterpret_cast<PersistFn>(fn)<<<grid, NT, plan.smem, stream>>>(prm);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    set_error("persistent launch: %s", cudaGetErrorString(e));
-    return FS_ELAUNCH;
-  }
-  return FS_OK;
-}
-
 fs_status run_cluster(const fs_sample_args* a, int mode, uint64_t* cand_out, cudaStream_t stream) {
   const int64_t K = std::min<int64_t>(a->top_k, a->vocab);
   PlanOut plan;
@@ -2757,15 +2788,6 @@ fs_status run_cluster(const fs_sample_args* a, int mode, uint64_t* cand_out, cud
   fs_status st = make_plan(a->batch, a->vocab, K, a->splits, path, &plan);
   if (st != FS_OK) return st;
   Params prm = base_params(a, K);
-  if (plan.persist && !(prm.vec && a->vocab % 8 == 0)) {
-    // bulk copies need 16-byte aligned rows of whole 16-byte vectors
-    if (path == FS_PATH_PERSIST) {
-      set_error("the persistent path needs 16-byte aligned rows and a vocabulary that is a multiple of 8");
-      return FS_EUNSUPPORTED;
-    }
-    st = make_plan(a->batch, a->vocab, K, a->splits, FS_PATH_CLUSTER, &plan);
-    if (st != FS_OK) return st;
-  }
   prm.cand_out = cand_out;
   prm.cap = plan.capacity;
   prm.mpt = plan.mpt;
@@ -2774,7 +2796,16 @@ fs_status run_cluster(const fs_sample_args* a, int mode, uint64_t* cand_out, cud
   prm.slot = plan.slot;
   prm.stop = a->stop_phase;
   prm.mode = mode;
-  if (plan.persist) return launch_persist(a->dtype, plan, a->batch, prm, stream);
+  if (plan.wide) {
+    if (mode != kModeSample || a->topk_ids != nullptr || a->keep != nullptr || a->renormed != nullptr ||
+        a->stop_phase != 0) {
+      set_error("the wide path (top_k > %d, or FS_PATH_WIDE) produces token ids and row status only: no top-k "
+                "ids, keep, renormed, shard candidates or phase probes",
+                kMaxCap);
+      return FS_EUNSUPPORTED;
+    }
+    return launch_wide(a, plan, prm, stream);
+  }
   if (plan.stream) return launch_stream(a, plan, prm, stream);
   return launch_cluster(a->dtype, plan, a->batch, prm, stream);
 }
@@ -2785,7 +2816,7 @@ uint64_t workspace_size(const fs_sample_args* a) {
   const int32_t path = a->stop_phase != 0 ? FS_PATH_CLUSTER : a->path;
   if (make_plan(a->batch, a->vocab, std::min<int64_t>(a->top_k, a->vocab), a->splits, path, &plan) != FS_OK)
     return 0;
-  return plan.stream ? plan.workspace : 0;
+  return (plan.stream || plan.wide) ? plan.workspace : 0;
 }
 
 fs_status run_merge(const fs_sample_args* a, const uint64_t* cand, int parts, cudaStream_t stream) {
@@ -2884,12 +2915,15 @@ void append_cluster_attrs(std::vector<fs_kernel_attr>& rows) {
     }
     {
       fs_kernel_attr r = {};
-      std::snprintf(r.name, sizeof(r.name), "fs_rowstream_kernel<%s>", dt ? "bf16" : "fp16");
-      r.param = 0;
+      std::snprintf(r.name, sizeof(r.name), "fs_wide_hist_kernel<%s>", dt ? "bf16" : "fp16");
+      r.param = 5;
       r.block = NT;
-      fill_attr(reinterpret_cast<const void*>(dt ? fs_rowstream_kernel<1> : fs_rowstream_kernel<0>), NT,
-                static_cast<int>(sizeof(Shared) + kRingOffset + 5 * kStageBytes + 1024 * 24 + NT * kStageChunks),
-                &r);
+      fill_attr(reinterpret_cast<const void*>(dt ? fs_wide_hist_kernel<1, 5> : fs_wide_hist_kernel<0, 5>), NT, 0, &r);
+      rows.push_back(r);
+      std::snprintf(r.name, sizeof(r.name), "fs_wide_row_kernel<%s>", dt ? "bf16" : "fp16");
+      r.param = 0;
+      r.block = kRowThreads;
+      fill_attr(reinterpret_cast<const void*>(dt ? fs_wide_row_kernel<1> : fs_wide_row_kernel<0>), kRowThreads, 0, &r);
       rows.push_back(r);
     }
     {
@@ -3111,7 +3145,7 @@ extern "C" fs_status fs_plan(int64_t batch, int64_t vocab, int64_t top_k, int32_
   out->maxima_per_thread = p.mpt;
   out->lanes_per_max = p.mgroup;
   out->smem_bytes = p.smem;
-  out->path = p.persist ? FS_PATH_PERSIST : p.stream ? FS_PATH_STREAM : FS_PATH_CLUSTER;
+  out->path = p.wide ? FS_PATH_WIDE : p.stream ? FS_PATH_STREAM : FS_PATH_CLUSTER;
   out->workspace_bytes = p.workspace;
   return FS_OK;
 }

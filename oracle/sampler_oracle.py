@@ -204,19 +204,23 @@ class Draw:
     stages: Stages
 
 
-def draw(st: Stages, u: np.ndarray, top_p: float | np.ndarray, rel_tol: float = 1e-6) -> Draw:
+def draw(st: Stages, u: np.ndarray, top_p: float | np.ndarray, rel_tol: float | np.ndarray = 1e-6,
+         cut_tol: float | np.ndarray | None = None) -> Draw:
     """Inverse-CDF draw with the reference kernel's rule over the oracle's stages.
 
     r is the last index of the exclusive-prefix keep mask, Z_p = cumsum[r], target = u * Z_p,
     pick = first i <= r with cumsum[i] >= target. A row is flagged near a boundary when the
     target is within rel_tol * Z_p of cumsum[pick] or cumsum[pick - 1], or when some exclusive
-    prefix lies within 4 ulp of top_p (the cut itself is then rounding-sensitive).
+    prefix lies within cut_tol of top_p (default 4 ulp of top_p: the cut itself is then
+    rounding-sensitive). rel_tol and cut_tol may be per-row arrays.
     """
     cum = st.cumsum.numpy().astype(np.float32)
     probs = st.probs.numpy().astype(np.float32)
     keep = st.keep.numpy()
     B, K = cum.shape
     p_rows = np.broadcast_to(np.asarray(top_p, dtype=np.float64), (B,))
+    rel_rows = np.broadcast_to(np.asarray(rel_tol, dtype=np.float64), (B,))
+    cut_rows = None if cut_tol is None else np.broadcast_to(np.asarray(cut_tol, dtype=np.float64), (B,))
     ids = np.empty(B, dtype=np.int64)
     picks = np.empty(B, dtype=np.int64)
     near = np.zeros(B, dtype=bool)
@@ -233,7 +237,7 @@ def draw(st: Stages, u: np.ndarray, top_p: float | np.ndarray, rel_tol: float = 
         pick = int(hits[0]) if hits.size else r
         picks[b] = pick
         ids[b] = topk_ids[b, pick]
-        tol = rel_tol * float(zp)
+        tol = float(rel_rows[b]) * float(zp)
         if abs(float(cum[b, pick]) - float(target)) <= tol:
             near[b] = True
         if pick > 0 and abs(float(cum[b, pick - 1]) - float(target)) <= tol:
@@ -241,9 +245,102 @@ def draw(st: Stages, u: np.ndarray, top_p: float | np.ndarray, rel_tol: float = 
         if p_rows[b] < 1.0:
             excl = (cum[b] - probs[b]).astype(np.float32)
             pf = np.float32(p_rows[b])
-            ulp = np.spacing(pf)
-            if np.any(np.abs(excl.astype(np.float64) - float(pf)) <= 4 * ulp):
+            window = 4 * float(np.spacing(pf)) if cut_rows is None else max(4 * float(np.spacing(pf)), float(cut_rows[b]))
+            if np.any(np.abs(excl.astype(np.float64) - float(pf)) <= window):
                 near[b] = True
+    return Draw(ids, picks, near, st)
+
+
+def fp32_cumsum_error(st: Stages) -> np.ndarray:
+    """Per row, the largest relative deviation of the stages' FP32 cumulative sum (torch's CPU
+    softmax over the top-k, then cumsum) from the same quantity in FP64. Over tens of thousands of
+    candidates torch's FP32 softmax normaliser drifts by several 1e-6, so this bounds how far the
+    reference's own CDF can sit from any other correct implementation's."""
+    x = st.topk_logits.double()
+    p64 = torch.softmax(x, dim=-1)
+    c64 = p64.cumsum(dim=-1)
+    c32 = st.cumsum.double()
+    rel = ((c32 - c64).abs() / c64.clamp_min(1e-300)).max(dim=-1).values
+    return rel.numpy()
+
+
+def pick_consistent(st: Stages, ids: np.ndarray, u: np.ndarray, top_p: float | np.ndarray,
+                    rel_tol: float | np.ndarray = 1e-6, fp64: bool = True) -> np.ndarray:
+    """Per row: is token ids[b] a pick the draw rule allows up to rounding? With k near V the
+    CDF steps near the target are far below any useful tolerance, so comparing picks by index
+    says little; this checks the pick's CDF interval instead. With c the cumulative sum (FP64 of
+    the same top-k logits when fp64, else the stages' FP32 one) and the cut r (first i >= 1 with
+    c_i - p_i >= top_p, minus 1), allowing every r whose exclusive prefix is within 4 ulp (FP32)
+    of top_p plus rel_tol * top_p: the token is in the top-k at a position pos <= the largest
+    allowed r, and c[pos-1] - tol <= u * Z_p and c[pos] + tol >= u * Z_p for some allowed Z_p,
+    with tol = rel_tol * Z_p."""
+    if fp64:
+        p = torch.softmax(st.topk_logits.double(), dim=-1).numpy()
+        c = np.cumsum(p, axis=-1)
+    else:
+        p = st.probs.numpy().astype(np.float64)
+        c = st.cumsum.numpy().astype(np.float64)
+    B, K = c.shape
+    p_rows = np.broadcast_to(np.asarray(top_p, dtype=np.float64), (B,))
+    rel_rows = np.broadcast_to(np.asarray(rel_tol, dtype=np.float64), (B,))
+    topk_ids = st.topk_ids.numpy()
+    ok = np.zeros(B, dtype=bool)
+    for b in range(B):
+        where = np.nonzero(topk_ids[b] == ids[b])[0]
+        if where.size != 1:
+            continue
+        pos = int(where[0])
+        if p_rows[b] >= 1.0:
+            r_lo = r_hi = K - 1
+        else:
+            excl = c[b] - p[b]
+            band = 4 * float(np.spacing(np.float32(p_rows[b]))) + rel_rows[b] * p_rows[b]
+            lo_fail = np.nonzero(excl[1:] >= p_rows[b] - band)[0]  # earliest possible cut
+            hi_fail = np.nonzero(excl[1:] >= p_rows[b] + band)[0]  # latest possible cut
+            r_lo = int(lo_fail[0]) if lo_fail.size else K - 1
+            r_hi = int(hi_fail[0]) if hi_fail.size else K - 1
+        if pos > r_hi:
+            continue
+        z_lo, z_hi = c[b, r_lo], c[b, r_hi]
+        tol = rel_rows[b] * z_hi
+        t_lo, t_hi = float(u[b]) * z_lo, float(u[b]) * z_hi
+        below = c[b, pos - 1] if pos > 0 else 0.0
+        ok[b] = below - tol <= t_hi and c[b, pos] + tol >= t_lo
+    return ok
+
+
+def draw_fp64(st: Stages, u: np.ndarray, top_p: float | np.ndarray, rel_tol: float = 1e-6) -> Draw:
+    """The same cut and draw over FP64 probabilities of the same top-k logits (the exact
+    distribution the reference's FP32 arithmetic approximates). A row is flagged when the target
+    lies within rel_tol * Z_p of a CDF step, or some exclusive prefix within 4 ulp (FP32) of
+    top_p."""
+    x = st.topk_logits.double()
+    p64 = torch.softmax(x, dim=-1).numpy()
+    c64 = np.cumsum(p64, axis=-1)
+    B, K = c64.shape
+    p_rows = np.broadcast_to(np.asarray(top_p, dtype=np.float64), (B,))
+    ids = np.empty(B, dtype=np.int64)
+    picks = np.empty(B, dtype=np.int64)
+    near = np.zeros(B, dtype=bool)
+    topk_ids = st.topk_ids.numpy()
+    for b in range(B):
+        excl = c64[b] - p64[b]
+        r = K - 1
+        if p_rows[b] < 1.0:
+            fails = np.nonzero(excl[1:] >= p_rows[b])[0]
+            if fails.size:
+                r = int(fails[0])  # (index fails[0] + 1) - 1
+            if np.any(np.abs(excl - p_rows[b]) <= 4 * float(np.spacing(np.float32(p_rows[b])))):
+                near[b] = True
+        zp = c64[b, r]
+        target = float(u[b]) * zp
+        hits = np.nonzero(c64[b, : r + 1] >= target)[0]
+        pick = int(hits[0]) if hits.size else r
+        picks[b] = pick
+        ids[b] = topk_ids[b, pick]
+        tol = rel_tol * zp
+        if abs(c64[b, pick] - target) <= tol or (pick > 0 and abs(c64[b, pick - 1] - target) <= tol):
+            near[b] = True
     return Draw(ids, picks, near, st)
 
 

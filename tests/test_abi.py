@@ -77,13 +77,20 @@ def test_plan_table():
         for V in (2000, 4001, 32000, 128256, 151936, 256000):
             for k in (1, 50, 256, 1024):
                 pl = abi.plan(B, V, k)
-                if pl.path == abi.FS_PATH_PERSIST:  # rows stream through 32 KiB stages
-                    assert pl.chunks * pl.threads * 8 == 16384 and pl.splits == 1
-                    assert pl.capacity >= 4 * min(k, V) and pl.smem_bytes <= 227 * 1024
-                else:
-                    assert pl.splits * pl.chunks * pl.threads * 8 >= V
-                    assert 1 <= pl.splits <= 16
+                assert pl.splits * pl.chunks * pl.threads * 8 >= V
+                assert 1 <= pl.splits <= 16
                 assert pl.capacity >= min(k, V)
+
+
+def test_top_k_beyond_the_survivor_buffer_plans_the_wide_path():
+    for B in (1, 8, 64, 1024):
+        for V, k in ((151936, 151936), (151936, 8193), (128256, 20000), (256000, 1 << 20)):
+            pl = abi.plan(B, V, k)
+            assert pl.path == abi.FS_PATH_WIDE, (B, V, k)
+            # a [B, 65536] per-key count histogram and a few words per row and slice
+            assert B * 65536 * 4 < pl.workspace_bytes < B * 65536 * 4 + B * 1024 + 4096
+            assert pl.splits * pl.chunks * pl.threads * 8 >= V
+    assert abi.plan(8, 151936, 8192).path == abi.FS_PATH_CLUSTER
 
 
 def test_plan_rejects_a_vocabulary_beyond_the_register_budget():
@@ -148,8 +155,8 @@ def test_workspace_size_follows_the_plan_and_the_path_override():
     assert lib.fs_workspace_size(ctypes.byref(a)) == abi.plan(1024, 151936, 50).workspace_bytes > 0
     a.path = abi.FS_PATH_CLUSTER
     assert lib.fs_workspace_size(ctypes.byref(a)) == 0
-    a.path = abi.FS_PATH_PERSIST
-    assert lib.fs_workspace_size(ctypes.byref(a)) == 0
+    a.path = abi.FS_PATH_WIDE
+    assert lib.fs_workspace_size(ctypes.byref(a)) >= 1024 * 65536 * 4
     a.path, a.batch = abi.FS_PATH_STREAM, 1
     assert lib.fs_workspace_size(ctypes.byref(a)) > 0
     assert lib.fs_workspace_size(None) == 0
@@ -178,12 +185,20 @@ def test_unknown_paths_and_unsupported_forced_paths_are_rejected():
     a.path = 9
     assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EINVAL
     assert "path" in lib.fs_last_error().decode()
-    a.path, a.top_k = abi.FS_PATH_PERSIST, 1024
+    # k beyond the survivor buffer: the cluster and streaming paths refuse it, AUTO goes wide
+    a.path, a.top_k = abi.FS_PATH_CLUSTER, 151936
     assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EUNSUPPORTED
-    # rows that bulk copies cannot move (odd vocabulary) are refused by the forced path
-    a.top_k, a.vocab, a.row_stride = 50, 151935, 151935
+    assert "capacity" in lib.fs_last_error().decode()
+    a.path = abi.FS_PATH_STREAM
     assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EUNSUPPORTED
-    assert "multiple of 8" in lib.fs_last_error().decode()
+    # the wide path produces token ids and row status only
+    a.path, a.topk_ids = abi.FS_PATH_AUTO, 0x3000
+    assert lib.fs_sample(ctypes.byref(a), None) == abi.FS_EUNSUPPORTED
+    assert "wide path" in lib.fs_last_error().decode()
+    a.topk_ids, a.top_k, a.path = None, 50, abi.FS_PATH_WIDE
+    assert lib.fs_topk(ctypes.byref(a), None) == abi.FS_EINVAL  # (topk_ids is required)
+    a.topk_ids = 0x3000
+    assert lib.fs_topk(ctypes.byref(a), None) == abi.FS_EUNSUPPORTED
 
 
 def test_peer_exchange_arguments_are_checked_before_any_launch():

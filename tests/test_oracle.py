@@ -171,3 +171,19 @@ def test_order_keys_match_the_reference_except_the_negative_zero_fold():
     # the reference keys -0 (0x8000) as 0x7FFF, one below +0; the oracle folds it onto +0
     assert diff.tolist() == [0x8000]
     assert ref[0x8000] == 0x7FFF and ours[0x8000] == 0x8000
+
+
+def test_pick_consistency_accepts_the_oracle_pick_and_rejects_far_neighbours():
+    """The interval check used at k near V: the oracle's own FP32 pick lies inside the exact
+    (FP64) CDF interval of the target, a token 50 places later does not, and the FP32 drift of
+    torch's softmax over ~1.5e5 candidates is measured in the 1e-7..1e-5 range."""
+    x = orc.adversarial_logits(2, B=4, V=151936, seed=2)
+    u = orc.splitmix_uniforms(0x5EED, 0, 4)
+    d = orc.sample(x, 151936, 0.5, uniforms=u)
+    assert orc.pick_consistent(d.stages, d.ids, u, 0.5).all()
+    far = d.stages.topk_ids.numpy()[np.arange(4), d.pick + 50]
+    assert not orc.pick_consistent(d.stages, far, u, 0.5).any()
+    err = orc.fp32_cumsum_error(d.stages)
+    assert (err > 0).all() and (err < 1e-4).all()
+    d64 = orc.draw_fp64(d.stages, u, 0.5)
+    assert orc.pick_consistent(d.stages, d64.ids, u, 0.5).all()

@@ -42,8 +42,7 @@ class OracleOps:
         c = cand.numpy()
         parts, B, _ = c.shape
         words = c[:, :, :top_k].transpose(1, 0, 2).reshape(B, parts * top_k).view(np.uint64)
-        order = np.argsort(-words.astype(np.float64), axis=1, kind="stable")  # keys fit in 53 bits? no
-        # exact descending order of uint64 words
+        # exact descending order of the uint64 words
         order = np.argsort(~words, axis=1, kind="stable")
         best = np.take_along_axis(words, order, axis=1)[:, :top_k]
         keys = (best >> np.uint64(32)).astype(np.uint32)

@@ -1,7 +1,6 @@
-"""CUDA parity tests of the large-batch paths: STREAM (slice launch + row-merge launch) and
-PERSIST (one CTA per SM streaming whole rows through bulk-copied shared-memory stages).
+"""CUDA parity tests of the large-batch path: STREAM (slice launch + row-merge launch).
 
-Each must give exactly what the cluster path gives: the same top-k set and order (checked against
+It must give exactly what the cluster path gives: the same top-k set and order (checked against
 the oracle), and, because all end in the same row tail over the same candidates, the same ids,
 keep mask, renormed probabilities and row status, bit for bit. `path=` forces a path at any batch
 (k <= 256); batches of 96 rows and more take STREAM by default when k <= 128.
@@ -18,8 +17,8 @@ from oracle import sampler_oracle as orc
 pytestmark = pytest.mark.gpu
 
 DTYPES = [torch.float16, torch.bfloat16]
-CLUSTER, STREAM, PERSIST = abi.FS_PATH_CLUSTER, abi.FS_PATH_STREAM, abi.FS_PATH_PERSIST
-PATHS = [STREAM, PERSIST]
+CLUSTER, STREAM = abi.FS_PATH_CLUSTER, abi.FS_PATH_STREAM
+PATHS = [STREAM]
 
 
 def dev_randn(B, V, scale, dtype, seed=0):
@@ -50,10 +49,6 @@ def assert_paths_agree(x, top_k, top_p, path=STREAM, **kw):
 @pytest.mark.parametrize("path", PATHS)
 def test_streaming_candidate_set_matches_the_oracle_exactly(vocab, top_k, dtype, path):
     x = dev_randn(24, vocab, 4.0, dtype, seed=vocab + top_k)
-    if path == PERSIST and vocab % 8:  # bulk copies move whole 16-byte vectors only
-        with pytest.raises(abi.FsError):
-            abi.topk(x, top_k, path=path)
-        return
     got = abi.topk(x, top_k, path=path).cpu()
     assert torch.equal(got, oracle_topk(x, top_k))
 
@@ -174,53 +169,33 @@ def test_strided_unaligned_and_odd_vocab_rows():
     assert_paths_agree(odd, 50, 0.9, uniforms=u)
 
 
-def test_persistent_path_refuses_rows_bulk_copies_cannot_move_and_auto_falls_back():
-    base = dev_randn(160, 151936 + 24, 3.0, torch.bfloat16, seed=13)
-    odd = base[:, 3:3 + 151936]  # rows not 16-byte aligned
-    with pytest.raises(abi.FsError) as e:
-        abi.topk(odd, 50, path=PERSIST)
-    assert e.value.status == abi.FS_EUNSUPPORTED
-    assert torch.equal(abi.topk(odd, 50).cpu(), oracle_topk(odd.contiguous(), 50))
-    y = dev_randn(160, 100003, 3.0, torch.float16, seed=14)  # V % 8 != 0
-    with pytest.raises(abi.FsError):
-        abi.topk(y, 50, path=PERSIST)
-    u = torch.rand(160, generator=torch.Generator().manual_seed(5)).cuda()
-    a = run(y, 50, 0.9, abi.FS_PATH_AUTO, uniforms=u)
-    b = run(y, 50, 0.9, CLUSTER, uniforms=u)
-    for p, q in zip(a, b):
-        assert torch.equal(p, q)
-    view = base[:, 8:8 + 151936]  # aligned view with a padded stride
-    assert torch.equal(abi.topk(view, 50, path=PERSIST).cpu(), oracle_topk(view.contiguous(), 50))
-
-
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("batch", [1, 149, 300, 1024])
-def test_persistent_rows_spread_over_the_grid(batch, dtype):
-    # more rows than SMs: each CTA walks several rows and its ring crosses row boundaries
+def test_streaming_batches_up_to_the_large_batch_config(batch, dtype):
+    # more rows than SMs; 1024 rows is the large-batch config's batch
     x = dev_randn(batch, 151936, 3.0, dtype, seed=batch)
     u = torch.rand(batch, generator=torch.Generator().manual_seed(batch)).cuda()
-    assert_paths_agree(x, 50, 0.9, PERSIST, uniforms=u)
+    assert_paths_agree(x, 50, 0.9, STREAM, uniforms=u)
     rows = torch.arange(0, batch, max(1, batch // 7))
-    assert torch.equal(abi.topk(x, 50, path=PERSIST).cpu()[rows], oracle_topk(x[rows], 50))
+    assert torch.equal(abi.topk(x, 50, path=STREAM).cpu()[rows], oracle_topk(x[rows], 50))
 
 
 @pytest.mark.parametrize("top_k", [1, 50, 128, 256])
-def test_rising_rows_force_candidate_compaction(top_k):
-    # every stage lifts the row by about one sigma, so each stage adds hundreds of candidates
-    # above the running threshold and the buffer is cut back to the exact k-th key repeatedly
+def test_rising_rows_concentrate_candidates_in_the_last_slices(top_k):
+    # the row rises by about one sigma every 16384 ids: the last slices hold every candidate
     B, V = 8, 151936
     g = torch.Generator().manual_seed(top_k)
     trend = torch.arange(V, dtype=torch.float32) // 16384 * 0.95
     x = (torch.randn(B, V, generator=g) + trend).to(torch.bfloat16).cuda()
-    assert torch.equal(abi.topk(x, top_k, path=PERSIST).cpu(), oracle_topk(x, top_k))
+    assert torch.equal(abi.topk(x, top_k, path=STREAM).cpu(), oracle_topk(x, top_k))
     u = torch.rand(B, generator=g).cuda()
-    assert_paths_agree(x, top_k, 0.9, PERSIST, uniforms=u)
+    assert_paths_agree(x, top_k, 0.9, STREAM, uniforms=u)
     steep = (torch.randn(B, V, generator=g) * 0.3 + trend * 3).to(torch.float16).cuda()
-    assert torch.equal(abi.topk(steep, top_k, path=PERSIST).cpu(), oracle_topk(steep, top_k))
+    assert torch.equal(abi.topk(steep, top_k, path=STREAM).cpu(), oracle_topk(steep, top_k))
 
 
 def test_late_stage_ties_overflow_into_the_exact_fallback():
-    # a tie block in the last stages: the candidate buffer overflows mid-row
+    # a tie block in the last slices: their candidate slots overflow
     x = torch.randn(4, 151936, generator=torch.Generator().manual_seed(1))
     x[:, 140000:] = 3.5
     x[1, 5] = 9.0
@@ -228,19 +203,19 @@ def test_late_stage_ties_overflow_into_the_exact_fallback():
     for dtype in DTYPES:
         xd = x.to(dtype).cuda()
         for k in (1, 50, 256):
-            assert torch.equal(abi.topk(xd, k, path=PERSIST).cpu(), oracle_topk(xd, k))
+            assert torch.equal(abi.topk(xd, k, path=STREAM).cpu(), oracle_topk(xd, k))
         u = torch.rand(4, generator=torch.Generator().manual_seed(2)).cuda()
-        assert_paths_agree(xd, 50, 0.9, PERSIST, uniforms=u)
+        assert_paths_agree(xd, 50, 0.9, STREAM, uniforms=u)
 
 
-def test_nan_and_inf_in_a_late_stage_are_reported():
+def test_nan_and_inf_in_the_last_slices_are_reported():
     x = dev_randn(6, 151936, 2.0, torch.bfloat16, seed=15)
     x[0, 151000] = float("nan")
     x[1, 140001] = float("inf")
     x[2, :] = float("-inf")
-    x[3, :150000] = float("-inf")  # finite values only in the last stage
+    x[3, :150000] = float("-inf")  # finite values only in the last slice
     x[4, 16384 * 3 + 7] = float("-inf")
-    out = assert_paths_agree(x, 50, 0.9, PERSIST, seed=3, offset=4)
+    out = assert_paths_agree(x, 50, 0.9, STREAM, seed=3, offset=4)
     assert out[4].cpu().tolist() == orc.row_status(x.cpu()).tolist()
     assert out[4].cpu().tolist()[:4] == [1, 2, 3, 0]
 
