@@ -521,6 +521,133 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------------------------
+# comparison rungs (B200): the reference's own CUDA kernel and FlashInfer's sampler
+# ---------------------------------------------------------------------------------------------
+
+
+def reference_kernel_module():
+    """The reference's CUDA extension compiled unchanged for sm_100a into oracle/_ref by
+    oracle/build_ref_kernel.py (None when it was not built)."""
+    import glob
+    import importlib.util
+
+    found = sorted(glob.glob(str(ROOT / "oracle" / "_ref" / "fused_sampling_ref*.so")))
+    if not found:
+        return None
+    spec = importlib.util.spec_from_file_location("fused_sampling_ref", found[0])
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def flashinfer_sampling():
+    """FlashInfer's sampling module, loaded from the JIT build kept in oracle/_ref/flashinfer
+    (FLASHINFER_WORKSPACE_BASE), or None."""
+    base = ROOT / "oracle" / "_ref" / "flashinfer"
+    if not base.exists():
+        return None
+    os.environ.setdefault("FLASHINFER_WORKSPACE_BASE", str(base))
+    os.environ.setdefault("FLASHINFER_CUDA_ARCH_LIST", "10.0")
+    try:
+        import flashinfer.sampling as fis
+
+        fis.get_sampling_module()
+        return fis
+    except Exception as e:  # noqa: BLE001
+        log(f"flashinfer unavailable: {e}")
+        return None
+
+
+def rungs(args, device):
+    """µs per call of the comparison rungs at C1 (cold L2, rotating buffers) and C3 (B=1024):
+    this repository's operator, the reference's own kernel (k <= 128; its semantics), and
+    FlashInfer's top_k_top_p_sampling_from_probs on a precomputed full-vocabulary softmax
+    ("from_probs", the reference's bar) and with that softmax inside the timed region. FlashInfer
+    samples by rejection on the full-vocabulary distribution: a different rule from the
+    reference's (exactly-k top-k, renormalised softmax, exclusive-prefix cut, inverse CDF), timed
+    here as a rung, not compared for ids."""
+    import llm_sampling_kernel_b200 as pkg
+
+    ops = pkg.ops()
+    out = {}
+    steps = max(20, min(args.steps, 2000))
+    warm = max(3, args.warmup)
+    per = C1["V"] * 2
+    nbuf = max(2, (2 * L2_BYTES) // per + 1)
+    bufs = anchor_buffers(nbuf, 1, C1["V"], device, seed=4321)
+    big = zipf_buffers(2, C3["B"], C3["V"], device, seed=9)
+
+    def c1(fn):
+        return timed_steps(lambda i: fn(bufs[i % nbuf]), steps, warm, 1) * 1000.0 / steps
+
+    def c3(fn):
+        n = max(3, min(steps, 50))
+        return timed_steps(lambda i: fn(big[i % 2]), n, warm, 1) * 1000.0 / n
+
+    out["ours"] = {"c1_us": round(c1(lambda x: ops.sample_fused(x, 50, 0.9, 0x5EED, 1, 0)), 3),
+                   "c3_us": round(c3(lambda x: ops.sample_fused(x, 50, 0.95, 0x5EED, 1, 0)), 3)}
+    ref = None
+    try:
+        ref = reference_kernel_module()
+    except Exception as e:  # noqa: BLE001
+        out["reference_kernel"] = {"unavailable": str(e)[:200]}
+    if ref is not None:
+        sys.path.insert(0, str(ROOT))
+        from oracle import sampler_oracle as orc
+
+        x = bufs[0]
+        want = orc.topk_order(orc.bits16(x.cpu()), 50)
+        same = bool(np.array_equal(ref.topk_fused(x, 50, 0).cpu().numpy(), want))
+        out["reference_kernel"] = {
+            "c1_us": round(c1(lambda x: ref.sample_fused(x, 50, 0.9, 0x5EED, 1, 0)), 3),
+            "c3_us": round(c3(lambda x: ref.sample_fused(x, 50, 0.95, 0x5EED, 1, 0)), 3),
+            "topk_matches_oracle_c1": same,
+            "what": "the reference's csrc/ (topk_partial_kernel + merge_sample_kernel) compiled unchanged "
+                    "for sm_100a by oracle/build_ref_kernel.py",
+        }
+    elif "reference_kernel" not in out:
+        out["reference_kernel"] = {"unavailable": "oracle/_ref/fused_sampling_ref*.so not built"}
+    fis = flashinfer_sampling()
+    if fis is None:
+        out["flashinfer"] = {"unavailable": "no FlashInfer sampling build in oracle/_ref/flashinfer"}
+    else:
+        probs1 = [torch.softmax(b.float(), dim=-1) for b in bufs[:64]]
+        probs3 = [torch.softmax(b.float(), dim=-1) for b in big]
+
+        def fp1(i):
+            fis.top_k_top_p_sampling_from_probs(probs1[i % len(probs1)], 50, 0.9)
+
+        def fp3(i):
+            fis.top_k_top_p_sampling_from_probs(probs3[i % 2], 50, 0.95)
+
+        n3 = max(3, min(steps, 50))
+        out["flashinfer"] = {
+            "from_probs_c1_us": round(timed_steps(fp1, steps, warm, 1) * 1000.0 / steps, 3),
+            "from_probs_c3_us": round(timed_steps(fp3, n3, warm, 1) * 1000.0 / n3, 3),
+            "from_logits_c1_us": round(c1(lambda x: fis.top_k_top_p_sampling_from_probs(
+                torch.softmax(x.float(), dim=-1), 50, 0.9)), 3),
+            "from_logits_c3_us": round(c3(lambda x: fis.top_k_top_p_sampling_from_probs(
+                torch.softmax(x.float(), dim=-1), 50, 0.95)), 3),
+            "version": getattr(sys.modules.get("flashinfer"), "__version__", "?"),
+            "semantics": "rejection sampling over the full-vocabulary distribution (top_k_first); "
+                         "from_probs: softmax precomputed outside the timed region (48 MB of fp32 probs "
+                         "per C1 buffer set: L2-warm)",
+        }
+    del bufs, big
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_rungs(args):
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    line = {"rungs": rungs(args, device), "steps": args.steps, "warmup": args.warmup,
+            "unit": "µs/call", "config": {"c1": "B=1, V=151936, k=50, p=0.9, BF16 (cold L2)",
+                                          "c3": "B=1024, V=151936, k=50, p=0.95, BF16 Zipf rows"}}
+    print(json.dumps(line), flush=True)
+
+
 def run_profile_case(args):
     """A few launches of one configuration, untimed: the target of the ncu captures in profiles/.
     c1 = the anchor (B=1), c3 = the B=1024 HBM-bound launch."""
@@ -549,11 +676,16 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--rungs", action="store_true",
+                    help="time the comparison rungs (reference kernel, FlashInfer) and exit")
     ap.add_argument("--profile-case", choices=["c1", "c3"], default=None,
                     help="run three untimed launches of one configuration (ncu target) and exit")
     args = ap.parse_args()
     if args.profile_case:
         run_profile_case(args)
+        return
+    if args.rungs:
+        run_rungs(args)
         return
     if args.warmup < 3:
         args.warmup = 3

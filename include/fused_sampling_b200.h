@@ -170,14 +170,20 @@ FS_API fs_status fs_merge_sample(const fs_sample_args* args, const uint64_t* can
  * peer-to-peer form of the all-gather + fs_merge_sample pair): every rank pushes its [B, K + 1] candidate
  * block (from fs_shard_candidates) into every rank's receive buffer over NVLink and raises one
  * flag per (row, source rank) there, then waits for its own flags and merges. All ranks call it
- * with the same epoch (1, 2, 3, ... per call). Buffers, set up once per process group:
+ * with the same epoch (1, 2, 3, ... per call), or each with its own epoch_counter (below).
+ * Buffers, set up once per process group:
  *   recv  : device [2][world][max_batch][K + 1] uint64, flags: device [2][world][max_batch]
  *           uint32 (zeroed before the first call),
  *   peer_recv / peer_flags: device arrays of `world` pointers to every rank's recv / flags
  *           (this rank's own included), mapped with fs_ipc_open.
  * A flag that does not arrive within wait_polls polls (0 = the default, about a second) marks
- * the row FS_ROW_TIMEOUT (id -1). Uses args: dtype, batch, top_k (K), top_p, rng, out_ids,
- * row_status. */
+ * the row FS_ROW_TIMEOUT (id -1); the exchange is then out of step between the ranks: tear the
+ * buffers down and set them up again before the next call. Uses args: dtype, batch, top_k (K),
+ * top_p, rng, out_ids, row_status.
+ * epoch_counter (optional): device memory of 2 uint32 on this rank's GPU, zeroed before the first
+ * call. When set, `epoch` is ignored: each call reads its epoch from the counter and the launch
+ * advances it (1, 2, ..., 2^32 - 1, then 2, 3, ...), so nothing changes between calls on the host
+ * and the launch can be captured in a CUDA graph and replayed. */
 typedef struct fs_tp_peers {
   int32_t world;
   int32_t rank;
@@ -188,6 +194,7 @@ typedef struct fs_tp_peers {
   uint32_t* flags;
   uint64_t* const* peer_recv;
   uint32_t* const* peer_flags;
+  uint32_t* epoch_counter;
 } fs_tp_peers;
 FS_API fs_status fs_tp_merge_sample(const fs_sample_args* args, const uint64_t* local_cand,
                                     const fs_tp_peers* tp, fs_stream_t stream);

@@ -101,6 +101,7 @@ class FsTpPeers(ctypes.Structure):
         ("flags", ctypes.c_void_p),
         ("peer_recv", ctypes.c_void_p),
         ("peer_flags", ctypes.c_void_p),
+        ("epoch_counter", ctypes.c_void_p),
     ]
 
 

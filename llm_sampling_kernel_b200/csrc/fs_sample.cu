@@ -2200,12 +2200,16 @@ __global__ void __launch_bounds__(NT) fs_merge_kernel(const Params p, const uint
 // Receive buffers and flags are double-buffered by call parity: a rank can only be one call
 // ahead of a peer (its merge needs the peer's push of the same call, and the peer pushes a call
 // only after its previous merge has finished), so a slot is never overwritten while being read.
+// The call's epoch is either a launch argument or, with a device counter, read from the counter
+// at launch and written back (advanced) by the launch's last CTA: then the host passes nothing
+// per call and the launches can be captured in a CUDA graph and replayed.
 // ------------------------------------------------------------------------------------------
 
 struct TpPeers {
   int32_t world, rank;
   int64_t max_batch;
   uint32_t epoch;                  // this call's number (>= 1); its slot is epoch & 1
+  uint32_t* ectr;                  // optional device counter {last epoch, CTAs done}: overrides `epoch`
   long long wait_polls;            // bound on the polls of one flag
   uint64_t* recv;                  // local [2][world][max_batch][K + 1]
   uint32_t* flags;                 // local [2][world][max_batch]
@@ -2222,9 +2226,14 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* ptr) {
   return v;
 }
 
+// The epoch after `e` on the device counter: never 0 (flags start at 0) and always of the other
+// parity (the slot alternates): after 2^32 - 1 it wraps to 2.
+__device__ __forceinline__ uint32_t next_epoch(uint32_t e) { return e == 0xFFFFFFFFu ? 2u : e + 1u; }
+
+// The exchange, wait and merge of one row; returns when the row's outputs are written.
 template <int DT>
-__global__ void __launch_bounds__(NT) fs_tp_merge_kernel(const Params p, const uint64_t* __restrict__ local_cand,
-                                                         const TpPeers tp) {
+__device__ void tp_merge_row(const Params& p, const uint64_t* __restrict__ local_cand, const TpPeers& tp,
+                             uint32_t epoch) {
   Shared& sh = *reinterpret_cast<Shared*>(g_smem);
   uint64_t* surv = reinterpret_cast<uint64_t*>(g_smem + sizeof(Shared));
   float* prob = reinterpret_cast<float*>(surv + p.cap);
@@ -2234,7 +2243,7 @@ __global__ void __launch_bounds__(NT) fs_tp_merge_kernel(const Params p, const u
   const int t = threadIdx.x;
   const int W = tp.world;
   const int K1 = p.K + 1;
-  const uint32_t slot = tp.epoch & 1u;
+  const uint32_t slot = epoch & 1u;
   // 1. push this rank's row to every rank, then raise the row's flag there
   for (int i = t; i < K1; i += NT) {
     const uint64_t x = local_cand[static_cast<size_t>(b) * K1 + i];
@@ -2243,7 +2252,7 @@ __global__ void __launch_bounds__(NT) fs_tp_merge_kernel(const Params p, const u
   }
   __threadfence_system();
   __syncthreads();
-  if (t < W) st_release_sys(&tp.peer_flags[t][(static_cast<size_t>(slot) * W + tp.rank) * tp.max_batch + b], tp.epoch);
+  if (t < W) st_release_sys(&tp.peer_flags[t][(static_cast<size_t>(slot) * W + tp.rank) * tp.max_batch + b], epoch);
   // 2. wait for every rank's row (bounded)
   if (t < 32) {
     bool ok = true;
@@ -2251,7 +2260,7 @@ __global__ void __launch_bounds__(NT) fs_tp_merge_kernel(const Params p, const u
       const uint32_t* f = &tp.flags[(static_cast<size_t>(slot) * W + t) * tp.max_batch + b];
       ok = false;
       for (long long i = 0; i < tp.wait_polls; ++i) {
-        if (ld_acquire_sys(f) == tp.epoch) {
+        if (ld_acquire_sys(f) == epoch) {
           ok = true;
           break;
         }
@@ -2298,6 +2307,27 @@ __global__ void __launch_bounds__(NT) fs_tp_merge_kernel(const Params p, const u
     return;
   }
   finish_row<DT>(p, b, tmp, n, surv, kk, pp, u, prob, cum, sh);
+}
+
+template <int DT>
+__global__ void __launch_bounds__(NT) fs_tp_merge_kernel(const Params p, const uint64_t* __restrict__ local_cand,
+                                                         const TpPeers tp) {
+  // with a device counter every CTA reads the last epoch before any CTA writes it back: the
+  // write-back comes from the CTA that finishes last, after every CTA has started
+  uint32_t epoch = tp.epoch;
+  if (tp.ectr != nullptr) epoch = next_epoch(*reinterpret_cast<volatile const uint32_t*>(&tp.ectr[0]));
+  tp_merge_row<DT>(p, local_cand, tp, epoch);
+  if (tp.ectr != nullptr) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(&tp.ectr[1], 1u) == gridDim.x - 1u) {
+        tp.ectr[1] = 0u;
+        *reinterpret_cast<volatile uint32_t*>(&tp.ectr[0]) = epoch;
+        __threadfence();
+      }
+    }
+  }
 }
 
 // ------------------------------------------------------------------------------------------
@@ -2866,6 +2896,7 @@ fs_status run_tp_merge(const fs_sample_args* a, const uint64_t* local_cand, cons
   tp.rank = tpa->rank;
   tp.max_batch = tpa->max_batch;
   tp.epoch = tpa->epoch;
+  tp.ectr = tpa->epoch_counter;
   tp.wait_polls = tpa->wait_polls > 0 ? tpa->wait_polls : (1LL << 22);
   tp.recv = tpa->recv;
   tp.flags = tpa->flags;
@@ -3046,9 +3077,10 @@ extern "C" fs_status fs_tp_merge_sample(const fs_sample_args* a, const uint64_t*
   if (st != FS_OK) return st;
   if (local_cand == nullptr || tp == nullptr || tp->world < 1 || tp->world > 32 || tp->rank < 0 ||
       tp->rank >= tp->world || tp->recv == nullptr || tp->flags == nullptr || tp->peer_recv == nullptr ||
-      tp->peer_flags == nullptr || tp->epoch == 0u || a->batch > tp->max_batch) {
+      tp->peer_flags == nullptr || (tp->epoch == 0u && tp->epoch_counter == nullptr) ||
+      a->batch > tp->max_batch) {
     fsb::set_error("invalid tensor-parallel exchange arguments (world 1..32, rank < world, buffers set, "
-                   "epoch >= 1, batch <= max_batch)");
+                   "epoch >= 1 or an epoch counter, batch <= max_batch)");
     return FS_EINVAL;
   }
   if (a->out_ids == nullptr) {

@@ -335,12 +335,14 @@ std::vector<torch::Tensor> merge_sample(torch::Tensor cand, bool bf16, int64_t t
 
 // Peer-to-peer exchange + merge (fs_tp_merge_sample): local_cand [B, K + 1] from
 // shard_candidates; recv [2, world, max_batch, K + 1] int64 and flags [2, world, max_batch] int32
-// on this rank's GPU; peer_recv / peer_flags: int64 cuda [world] tensors of device pointers.
+// on this rank's GPU; peer_recv / peer_flags: int64 cuda [world] tensors of device pointers;
+// epoch_counter: optional int32 [2] on this GPU (zeroed once), which replaces `epoch`.
 std::vector<torch::Tensor> tp_merge(torch::Tensor local_cand, bool bf16, int64_t top_k, double top_p,
                                     torch::Tensor recv, torch::Tensor flags, torch::Tensor peer_recv,
                                     torch::Tensor peer_flags, int64_t world, int64_t rank, int64_t epoch,
                                     std::optional<torch::Tensor> uniforms, int64_t seed, int64_t offset,
-                                    int64_t row_base, int64_t wait_polls, double temperature) {
+                                    int64_t row_base, int64_t wait_polls, double temperature,
+                                    std::optional<torch::Tensor> epoch_counter) {
   TORCH_CHECK(local_cand.is_cuda() && local_cand.dim() == 2 && local_cand.is_contiguous() &&
                   local_cand.scalar_type() == at::kLong && local_cand.size(1) == top_k + 1,
               "local_cand must be a contiguous int64 cuda [B, top_k + 1] tensor");
@@ -375,6 +377,13 @@ std::vector<torch::Tensor> tp_merge(torch::Tensor local_cand, bool bf16, int64_t
   tp.rank = static_cast<int32_t>(rank);
   tp.max_batch = recv.size(2);
   tp.epoch = static_cast<uint32_t>(epoch);
+  if (epoch_counter.has_value()) {
+    const auto& c = *epoch_counter;
+    TORCH_CHECK(c.is_cuda() && c.scalar_type() == at::kInt && c.numel() >= 2 && c.is_contiguous() &&
+                    c.device() == local_cand.device(),
+                "epoch_counter must be a contiguous int32 cuda tensor of 2 words on the candidates' device");
+    tp.epoch_counter = reinterpret_cast<uint32_t*>(c.data_ptr<int32_t>());
+  }
   tp.wait_polls = wait_polls;
   tp.recv = reinterpret_cast<uint64_t*>(recv.data_ptr<int64_t>());
   tp.flags = reinterpret_cast<uint32_t*>(flags.data_ptr<int32_t>());
@@ -420,7 +429,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("local_cand"), py::arg("bf16"), py::arg("top_k"), py::arg("top_p"), py::arg("recv"),
         py::arg("flags"), py::arg("peer_recv"), py::arg("peer_flags"), py::arg("world"), py::arg("rank"),
         py::arg("epoch"), py::arg("uniforms") = py::none(), py::arg("seed") = 0, py::arg("offset") = -1,
-        py::arg("row_base") = 0, py::arg("wait_polls") = 0, py::arg("temperature") = 1.0);
+        py::arg("row_base") = 0, py::arg("wait_polls") = 0, py::arg("temperature") = 1.0,
+        py::arg("epoch_counter") = py::none());
   m.def("plan", &plan,
         "launch plan (splits, chunks, threads, capacity, maxima/thread, lanes/max, smem, path, workspace)");
   m.attr("NUM_PHASES") = FS_NUM_PHASES;

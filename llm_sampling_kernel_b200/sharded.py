@@ -81,7 +81,10 @@ class VocabShardedSampler:
     backend="p2p": one kernel per rank pushes its block into every rank's receive buffer over
     NVLink (CUDA IPC mappings made once, at the first call, for up to `max_batch` rows), raises a
     flag per row there, waits for its own flags (bounded) and merges; no collective library on the
-    data path. Call close() (every rank) before destroying the process group.
+    data path. The call epoch is a device counter, so the step (two launches, no host state) can be
+    captured in a CUDA graph. A row with status FS_ROW_TIMEOUT (5) means a peer's push did not
+    arrive in time and the ranks' exchanges are out of step: close() and build a new sampler
+    before the next call. Call close() (every rank) before destroying the process group.
     """
 
     vocab: int
@@ -166,8 +169,11 @@ class VocabShardedSampler:
             raise
         # every rank has mapped every buffer before any rank pushes into one
         dist.barrier(group=self.group)
+        # the call epoch lives on the device: the launch reads and advances it, so a step of
+        # shard top-k + exchange-merge can be captured in a CUDA graph and replayed
+        epoch_counter = torch.zeros(2, dtype=torch.int32, device=device)
         self._p2p = dict(recv=recv, flags=flags, own=(recv_ptr, flags_ptr), opened=opened,
-                         peer_recv=peer_recv, peer_flags=peer_flags, epoch=0)
+                         peer_recv=peer_recv, peer_flags=peer_flags, epoch_counter=epoch_counter)
 
     def close(self):
         """Unmaps the peers' buffers and frees this rank's (p2p backend); collective."""
@@ -216,11 +222,11 @@ class VocabShardedSampler:
             if self._p2p is None:
                 self._setup_p2p(shard_logits.device)
             st = self._p2p
-            st["epoch"] += 1
             cand = self.local_candidates(shard_logits)
             return self.ops.tp_merge(cand, self.bf16, self.top_k, top_p, st["recv"], st["flags"], st["peer_recv"],
-                                     st["peer_flags"], self.world, self.rank, st["epoch"], uniforms, seed, offset,
-                                     row_base, self.wait_polls, temperature=temperature)
+                                     st["peer_flags"], self.world, self.rank, 0, uniforms, seed, offset,
+                                     row_base, self.wait_polls, temperature=temperature,
+                                     epoch_counter=st["epoch_counter"])
         gathered = self.exchange(self.local_candidates(shard_logits))
         ids, status = self.ops.merge_sample(gathered, self.bf16, self.top_k, top_p, None, None, uniforms, seed,
                                             offset, row_base, temperature=temperature)

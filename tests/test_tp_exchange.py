@@ -85,3 +85,52 @@ def test_one_rank_exchange_equals_the_plain_sampler():
         torch.cuda.synchronize()
         abi.ipc_free(recv_ptr)
         abi.ipc_free(flags_ptr)
+
+
+def test_the_device_epoch_counter_advances_per_call_wraps_and_replays_in_a_graph():
+    """With an epoch counter the launch reads its epoch from device memory and advances it, so a
+    step (shard top-k + exchange-merge) captured in a CUDA graph runs a new epoch on every replay."""
+    B, V = 8, 151936
+    x, recv, recv_ptr, flags, flags_ptr = setup(1, B, V)
+    try:
+        ops = fused.ops()
+        ctr = torch.zeros(2, dtype=torch.int32, device="cuda")
+        ptrs = torch.tensor([recv_ptr], dtype=torch.int64, device="cuda")
+        fptrs = torch.tensor([flags_ptr], dtype=torch.int64, device="cuda")
+        want = fused.sample_fused(x, K, 0.95, seed=1, offset=2)
+
+        def step():
+            cand = ops.shard_candidates(x, K, 0)
+            return ops.tp_merge(cand, True, K, 0.95, recv, flags, ptrs, fptrs, 1, 0, 0, seed=1, offset=2,
+                                epoch_counter=ctr)
+
+        for k in (1, 2, 3):
+            ids, status = step()
+            assert torch.equal(ids, want) and (status == 0).all()
+            assert ctr.tolist() == [k, 0]
+            assert (flags[k & 1, 0] == k).all()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(g, stream=side):
+                ids_g, status_g = step()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        assert ctr.tolist() == [3, 0]  # capture runs nothing
+        for k in (4, 5, 6):
+            g.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(ids_g, want) and (status_g == 0).all()
+            assert ctr.tolist() == [k, 0]
+        del g
+        # after 2^32 - 1 the epoch wraps to 2 (never 0, and the slot parity still alternates)
+        ctr.copy_(torch.tensor([-1, 0], dtype=torch.int32))
+        ids, status = step()
+        assert torch.equal(ids, want) and (status == 0).all()
+        assert ctr.tolist() == [2, 0]
+        assert (flags[0, 0] == 2).all()
+    finally:
+        torch.cuda.synchronize()
+        abi.ipc_free(recv_ptr)
+        abi.ipc_free(flags_ptr)
