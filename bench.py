@@ -465,6 +465,24 @@ def run_tp(ops, world, rank, device, args):
         ms = timed_steps(step, steps, max(3, args.warmup), world)
         us = max_over_ranks(ms * 1000.0 / steps, world)
         launches += 2 * steps
+        if backend == "p2p":
+            # the same step replayed from a CUDA graph (the exchange epoch lives on the device):
+            # 32 steps per graph, no host work between them
+            per_graph = 32
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(side):
+                with torch.cuda.graph(g, stream=side):
+                    for j in range(per_graph):
+                        sampler.sample(shard, p, seed=0x5EED, offset=j)
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            replays = max(3, min(args.steps, 200) // per_graph)
+            msg = timed_steps(lambda i: g.replay(), replays, 3, world)
+            out["graph_us_per_call"] = round(max_over_ranks(msg * 1000.0 / (replays * per_graph), world), 3)
+            launches += 2 * per_graph * replays
+            del g
         ids, status = sampler.sample(shard, p, seed=0x5EED, offset=0)
         all_ids = [torch.empty_like(ids) for _ in range(world)]
         dist.all_gather(all_ids, ids)
@@ -481,6 +499,14 @@ def run_tp(ops, world, rank, device, args):
     out["nccl_us_per_call"] = round(results["nccl"][0], 3)
     out["ranks_agree"] = all(r[1] for r in results.values())
     out["launches"] = launches
+    # per rank: its logit columns read once + the candidate blocks it sends and receives
+    lo_hi = VocabShardedSampler(vocab=V, top_k=k, ops=ops).cols
+    alg = B * (lo_hi[1] - lo_hi[0]) * 2 + B * (k + 1) * 8 * world * 2
+    best = out.get("graph_us_per_call", out["us_per_call"])
+    peak, _ = measured_peaks()
+    out["roofline"] = {"algorithmic_bytes_per_rank": alg, "us": best,
+                       "achieved_gbs": round(alg / (best * 1e-6) / 1e9, 1),
+                       "frac_of_hbm": round(alg / (best * 1e-6) / 1e9 / peak, 4)}
     return out
 
 

@@ -130,12 +130,13 @@ FS_API uint64_t fs_workspace_size(const fs_sample_args* args);
 FS_API fs_status fs_sample(const fs_sample_args* args, fs_stream_t stream);
 
 /* fs_sample without a caller workspace (no counterpart in the reference). For callers that
- * cannot allocate device memory at call time. The streaming path's scratch is one static device
- * array of FS_STATIC_SCRATCH_BYTES per device; a call that needs more returns FS_EWORKSPACE.
- * args->workspace is ignored. The first call on a device looks the array up
- * (cudaGetSymbolAddress): make it before any stream capture. Nothing is allocated, freed or
- * zeroed per call. Calls that overlap in time (other streams, other host threads) share the array
- * and race: serialise them. */
+ * cannot allocate device memory at call time. The scratch of the streaming and wide paths is one
+ * static device array of FS_STATIC_SCRATCH_BYTES per device; a call that needs more returns
+ * FS_EWORKSPACE. args->workspace is ignored. The first call on a device (and the first after a
+ * cudaDeviceReset, which loads the module again) looks the array up (cudaGetSymbolAddress): make
+ * it before any stream capture. Nothing is allocated or freed per call (the wide path clears its
+ * part of the array on the stream). Calls that overlap in time (other streams, other host
+ * threads) share the array and race: serialise them. */
 #define FS_STATIC_SCRATCH_BYTES (16ull << 20)
 FS_API fs_status fs_sample_noalloc(const fs_sample_args* args, fs_stream_t stream);
 

@@ -77,3 +77,20 @@ def _worker(rank, world, port):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_two_gpu_batch_and_vocab_sharding_match_one_gpu():
     mp.spawn(_worker, args=(2, _free_port()), nprocs=2, join=True)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_one_process_driving_two_gpus_grants_kernel_attributes_per_device():
+    """Function attributes (dynamic shared memory, non-portable cluster size) are per device: a
+    size granted on one GPU must not be assumed on the other. The order below (small on GPU 0,
+    large on GPU 1, then large on GPU 0, small on GPU 1) is the one a single per-kernel record
+    would get wrong."""
+    from llm_sampling_kernel_b200 import fused
+    from oracle import sampler_oracle as orc
+
+    xs = {d: orc.anchor_logits(B=4, V=151936, seed=d) for d in (0, 1)}
+    for d, k in ((0, 50), (1, 2048), (0, 2048), (1, 50), (1, 8192)):
+        with torch.cuda.device(d):
+            got = fused.topk_fused(xs[d].cuda(d), k).cpu()
+        want = torch.from_numpy(orc.topk_order(orc.bits16(xs[d]), k))
+        assert torch.equal(got, want), (d, k)
