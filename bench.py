@@ -674,6 +674,55 @@ def run_rungs(args):
     print(json.dumps(line), flush=True)
 
 
+def run_sweep(args):
+    """CTAs per row (S) against batch, vocabulary and k, on both the cluster and the streaming
+    path: CUDA-event µs per call over rotating input buffers (> 2x L2), one JSON line. The plan's
+    measured split table (make_plan) is read off these numbers."""
+    import llm_sampling_kernel_b200 as pkg
+    from llm_sampling_kernel_b200 import abi
+
+    ops = pkg.ops()
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    rows = []
+    for V in (128256, 151936):
+        for B in (1, 4, 16, 32, 64, 96, 128, 256):
+            per = B * V * 2
+            nbuf = max(2, (2 * L2_BYTES) // per + 1)
+            g = torch.Generator(device=device).manual_seed(B + V)
+            x = (torch.randn(nbuf * B, V, generator=g, device=device) * 2.0).to(torch.bfloat16)
+            bufs = [x[i * B:(i + 1) * B] for i in range(nbuf)]
+            for k in (1, 50, 256, 1024):
+                for path in (abi.FS_PATH_CLUSTER, abi.FS_PATH_STREAM):
+                    if path == abi.FS_PATH_STREAM and k > 256:
+                        continue
+                    for S in (4, 8, 16):
+                        try:
+                            pl = ops.plan(B, V, k, S)
+                        except RuntimeError:
+                            continue
+                        if pl[0] != S:  # raised to hold the row in registers: not this split
+                            continue
+                        m_slots = max(64, 1 << max(0, (2 * k - 1).bit_length()))
+                        if path == abi.FS_PATH_STREAM and S * m_slots > 4096:
+                            continue  # the streaming plan would use fewer slices
+
+                        def call(i, S=S, path=path, k=k):
+                            ops.sample_ex(bufs[i % nbuf], k, 0.9, None, None, None, 0x5EED, i, S, 0, 0, False, path)
+
+                        try:
+                            n = 60
+                            ms = timed_steps(call, n, 5, 1)
+                        except RuntimeError as e:
+                            rows.append({"V": V, "B": B, "k": k, "path": path, "S": S, "error": str(e)[:80]})
+                            continue
+                        rows.append({"V": V, "B": B, "k": k, "path": path, "S": S, "us": round(ms * 1000.0 / n, 3)})
+            del x, bufs
+            torch.cuda.empty_cache()
+    print(json.dumps({"sweep": rows, "dtype": "bf16", "top_p": 0.9, "l2": "cold (rotating buffers > 2x L2)"}),
+          flush=True)
+
+
 def run_profile_case(args):
     """A few launches of one configuration, untimed: the target of the ncu captures in profiles/.
     c1 = the anchor (B=1), c3 = the B=1024 HBM-bound launch."""
@@ -702,6 +751,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--sweep", action="store_true",
+                    help="time both paths over CTAs per row x batch x vocabulary x k and exit")
     ap.add_argument("--rungs", action="store_true",
                     help="time the comparison rungs (reference kernel, FlashInfer) and exit")
     ap.add_argument("--profile-case", choices=["c1", "c3"], default=None,
@@ -712,6 +763,9 @@ def main():
         return
     if args.rungs:
         run_rungs(args)
+        return
+    if args.sweep:
+        run_sweep(args)
         return
     if args.warmup < 3:
         args.warmup = 3

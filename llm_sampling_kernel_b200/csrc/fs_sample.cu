@@ -2368,8 +2368,36 @@ static int pow2_floor(int64_t x) {
 
 constexpr int kMaxCap = 8192;
 constexpr int64_t kStreamMaxK = 256;     // streaming path: top-K bound
-constexpr int64_t kStreamMinBatch = 96;   // AUTO: rows from which the streaming path is used
-constexpr int64_t kStreamAutoMaxK = 128;  // AUTO: largest k for which it is used
+
+// Cluster path: CTAs per row, measured best on B200 (bench.py --sweep; bf16, cold L2) for
+// [vocabulary class][batch bucket][k bucket]. Vocabulary class 0: rows that 4 CTAs can hold in
+// registers (V <= 131072; measured at 128256), 1: larger (measured at 151936, where 8 and 16 are
+// the choices). Batch buckets: 1, 4, 16, 32, 64, 96, 128, 256 rows (the largest not above B);
+// k buckets: 1, <= 128, <= 512, larger. A value the row cannot use is raised to the smallest
+// split that holds it (or lowered to one chunk per CTA for small rows).
+constexpr int kSplitBatch[8] = {1, 4, 16, 32, 64, 96, 128, 256};
+constexpr unsigned char kClusterSplits[2][8][4] = {
+    {{16, 16, 16, 8}, {8, 8, 16, 16}, {8, 8, 8, 4}, {8, 8, 4, 4}, {4, 4, 4, 4}, {4, 4, 4, 4}, {4, 4, 4, 4},
+     {4, 4, 4, 4}},
+    {{16, 16, 16, 16}, {16, 16, 16, 16}, {8, 8, 8, 8}, {8, 8, 8, 8}, {8, 8, 8, 8}, {8, 8, 8, 8}, {8, 8, 8, 8},
+     {8, 8, 8, 8}},
+};
+
+static int split_bucket_b(int64_t B) {
+  int i = 0;
+  while (i + 1 < 8 && B >= kSplitBatch[i + 1]) ++i;
+  return i;
+}
+static int split_bucket_k(int64_t K) { return K <= 1 ? 0 : K <= 128 ? 1 : K <= 512 ? 2 : 3; }
+
+// AUTO takes the streaming path from this many rows (measured crossover with the cluster path at
+// its measured split): k <= 128 from 96 rows; 128 < k <= 256 from 64 rows when the row needs 8
+// or more CTAs, else from 96.
+static bool auto_stream(int64_t B, int64_t K, int64_t min_s) {
+  if (K <= 128) return B >= 96;
+  if (K <= kStreamMaxK) return B >= (min_s > 4 ? 64 : 96);
+  return false;
+}
 
 // Plan of one call: cluster size, chunks per thread, survivor capacity, maxima granularity.
 fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t path, PlanOut* out) {
@@ -2386,7 +2414,7 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t pat
     S = static_cast<int>(std::min<int64_t>(kMaxSplits, std::max<int64_t>(splits, min_s)));
     S = std::min(kMaxSplits, pow2_ceil(S));  // powers of two keep the slot arithmetic to shifts
   } else {
-    S = (B <= 32) ? 16 : 8;
+    S = kClusterSplits[min_s > 4 ? 1 : 0][split_bucket_b(B)][split_bucket_k(K)];
     // small rows need fewer CTAs
     const int64_t one_chunk = (V + per_cta_chunk - 1) / per_cta_chunk;
     S = static_cast<int>(std::min<int64_t>(S, std::max<int64_t>(1, one_chunk)));
@@ -2451,10 +2479,11 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t pat
     return FS_OK;
   }
 
-  // streaming path: slices keep their own top-K in M slots; the row merge gathers S * M
+  // streaming path: slices keep their own top-K in M slots; the row merge gathers S * M. The
+  // fewest slices that hold the row measured fastest at every batch (a requested split is kept)
   const int M = std::max(64, pow2_ceil(2 * K));
+  int Ss = splits > 0 ? S : std::min(kMaxSplits, pow2_ceil(min_s));
   // fewer, longer slices when S * M candidates would not fit the row merge's key buffer
-  int Ss = S;
   while (Ss > 1 && static_cast<int64_t>(Ss) * M > kMaxMaxima) Ss /= 2;
   int Cs = 0;
   for (int opt : kChunkOptions) {
@@ -2465,8 +2494,7 @@ fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t pat
   }
   // (the slice launch puts rows on grid.y, at most 65535)
   const bool stream_fits = K <= kStreamMaxK && static_cast<int64_t>(Ss) * M <= kMaxMaxima && Cs > 0 && B <= 65535;
-  const bool want_stream =
-      path == FS_PATH_STREAM || (path == FS_PATH_AUTO && B >= kStreamMinBatch && K <= kStreamAutoMaxK);
+  const bool want_stream = path == FS_PATH_STREAM || (path == FS_PATH_AUTO && auto_stream(B, K, min_s));
   if (path == FS_PATH_STREAM && !stream_fits) {
     set_error("the streaming path supports top_k <= %lld with splits * slots <= %d and batch <= 65535",
               static_cast<long long>(kStreamMaxK), kMaxMaxima);

@@ -129,14 +129,35 @@ def test_large_batches_plan_the_streaming_path_with_a_workspace():
     # [B, S, M] packed candidates (M >= 2k) + [B, S] counts + alignment slack
     assert big.workspace_bytes >= 1024 * big.splits * (2 * 50 * 8 + 4)
     assert abi.plan(1, 151936, 50).path == abi.FS_PATH_CLUSTER
-    # AUTO: the streaming path from 96 rows (measured crossover with the cluster path, k <= 128)
+    # AUTO (measured crossovers with the cluster path at its measured split): k <= 128 from 96
+    # rows; 128 < k <= 256 from 64 rows when the row needs 8 or more CTAs, else from 96
     assert abi.plan(95, 151936, 50).path == abi.FS_PATH_CLUSTER
     assert abi.plan(96, 151936, 50).path == abi.FS_PATH_STREAM
-    assert abi.plan(96, 151936, 129).path == abi.FS_PATH_CLUSTER
+    assert abi.plan(63, 151936, 200).path == abi.FS_PATH_CLUSTER
+    assert abi.plan(64, 151936, 200).path == abi.FS_PATH_STREAM
+    assert abi.plan(64, 128256, 200).path == abi.FS_PATH_CLUSTER
+    assert abi.plan(96, 128256, 256).path == abi.FS_PATH_STREAM
+    assert abi.plan(1024, 151936, 256).path == abi.FS_PATH_STREAM
     assert abi.plan(1, 151936, 50).workspace_bytes == 0
     # beyond the streaming path's k the cluster path serves every batch size
     assert abi.plan(1024, 151936, 1024).path == abi.FS_PATH_CLUSTER
-    assert abi.plan(1024, 151936, 256).path == abi.FS_PATH_CLUSTER
+
+
+def test_the_split_table_follows_the_measured_sweep():
+    """CTAs per row from the B200 sweep: more CTAs only while the batch leaves SMs idle, the
+    fewest that hold the row once it does (4 for V <= 131072, else 8); the streaming path always
+    takes the fewest slices that hold the row."""
+    assert abi.plan(1, 151936, 50).splits == 16
+    assert abi.plan(16, 151936, 50).splits == 8
+    assert abi.plan(32, 128256, 50).splits == 8
+    assert abi.plan(32, 128256, 256).splits == 4
+    assert abi.plan(64, 128256, 50).splits == 4
+    assert abi.plan(64, 151936, 50).splits == 8
+    assert abi.plan(16, 128256, 1024).splits == 4
+    assert abi.plan(1024, 151936, 50).splits == 8     # streaming
+    assert abi.plan(1024, 128256, 50).splits == 4     # streaming
+    assert abi.plan(4, 2000, 50).splits == 1          # one chunk per CTA covers the row
+    assert abi.plan(8, 151936, 50, 4).splits == 8     # a request the registers cannot hold is raised
 
 
 def test_the_forced_streaming_path_plans_a_workspace():
