@@ -42,11 +42,17 @@ void fill_attr(const void* fn, int block, int smem, fs_kernel_attr* row) {
   row->local_bytes = static_cast<int32_t>(a.localSizeBytes);
   row->static_smem = static_cast<int32_t>(a.sharedSizeBytes);
   int blocks = 0;
-  if (smem > 48 * 1024) cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  // The occupancy query needs the function's dynamic shared memory limit to cover `smem`; the
+  // limit is raised for the query only and put back afterwards, so that the limits the launch
+  // paths granted (and remember granting) stay as they were.
+  const int granted = a.maxDynamicSharedSizeBytes;
+  const bool raise = smem > granted;
+  if (raise) cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, block, smem) != cudaSuccess) {
     cudaGetLastError();
     blocks = -1;
   }
+  if (raise) cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, granted);
   row->blocks_per_sm = blocks;
 }
 

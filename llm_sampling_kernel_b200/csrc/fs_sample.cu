@@ -2400,7 +2400,35 @@ static bool auto_stream(int64_t B, int64_t K, int64_t min_s) {
 }
 
 // Plan of one call: cluster size, chunks per thread, survivor capacity, maxima granularity.
+static fs_status make_plan_uncached(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t path, PlanOut* out);
+
+// make_plan with a small per-thread cache: a serving loop asks for the same few plans on every
+// call, and the plan is on the host's critical path of a B=1 call (about as long as the kernel).
 fs_status make_plan(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t path, PlanOut* out) {
+  struct Entry {
+    int64_t B, V, K;
+    int32_t splits, path;
+    bool valid;
+    PlanOut plan;
+  };
+  constexpr int kEntries = 8;
+  thread_local Entry cache[kEntries] = {};
+  thread_local int next = 0;
+  for (const Entry& e : cache) {
+    if (e.valid && e.B == B && e.V == V && e.K == K && e.splits == splits && e.path == path) {
+      *out = e.plan;
+      return FS_OK;
+    }
+  }
+  const fs_status st = make_plan_uncached(B, V, K, splits, path, out);
+  if (st == FS_OK) {
+    cache[next] = Entry{B, V, K, splits, path, true, *out};
+    next = (next + 1) % kEntries;
+  }
+  return st;
+}
+
+static fs_status make_plan_uncached(int64_t B, int64_t V, int64_t K, int32_t splits, int32_t path, PlanOut* out) {
   if (path < FS_PATH_AUTO || path > FS_PATH_WIDE) {
     set_error("path must be one of FS_PATH_AUTO, FS_PATH_CLUSTER, FS_PATH_STREAM, FS_PATH_WIDE; got %d", path);
     return FS_EINVAL;
@@ -2553,6 +2581,12 @@ static fs_status prepare_kernel(KernelFn fn, int S, int smem) {
     set_error("cudaGetDevice: %s", cudaGetErrorString(e));
     return FS_ELAUNCH;
   }
+  // the calling thread's last kernel already prepared for at least this much: no lock (grants
+  // only ever grow, so a remembered grant stays valid)
+  thread_local const void* last_fn = nullptr;
+  thread_local int last_dev = -1, last_smem = 0;
+  thread_local bool last_nonportable = false;
+  if (f == last_fn && dev == last_dev && smem <= last_smem && (S <= 8 || last_nonportable)) return FS_OK;
   std::lock_guard<std::mutex> lock(mu);
   KernelState* ks = kernel_state(f, dev);
   if (ks == nullptr) {
@@ -2575,6 +2609,10 @@ static fs_status prepare_kernel(KernelFn fn, int S, int smem) {
     }
     ks->nonportable = true;
   }
+  last_fn = f;
+  last_dev = dev;
+  last_smem = ks->smem_granted;
+  last_nonportable = ks->nonportable;
   return FS_OK;
 }
 

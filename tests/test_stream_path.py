@@ -274,3 +274,13 @@ def test_survivor_keys_spanning_more_than_256_values(path):
         ids = assert_paths_agree(x, k, 1.0, path, seed=6, offset=k)[1]
         for r in range(B):
             assert torch.equal(ids[r].cpu(), oracle_topk(x[r:r + 1], k)[0])
+
+
+def test_kernel_attribute_queries_leave_the_granted_launch_limits_alone():
+    """kernel_attrs computes occupancy at a typical shared-memory size; it must not lower the
+    limit a launch path granted (and remembers granting) for a larger row merge."""
+    x = dev_randn(24, 151936, 2.0, torch.bfloat16, seed=41)
+    assert torch.equal(abi.topk(x, 256, path=STREAM).cpu(), oracle_topk(x, 256))
+    fused.ops().kernel_attrs()
+    assert torch.equal(abi.topk(x, 256, path=STREAM).cpu(), oracle_topk(x, 256))
+    assert torch.equal(abi.topk(x, 100, path=STREAM).cpu(), oracle_topk(x, 100))
