@@ -363,6 +363,14 @@ def run_ours(args):
         del big
         torch.cuda.empty_cache()
 
+        # ---- LM-head producer (one GPU): logits GEMM in L2-sized vocabulary chunks, each chunk's
+        # top-k taken while it is in L2, one merge -- against the GEMM writing [B, V] logits to
+        # HBM and the sampler reading them back ----
+        lm_head = None
+        if world == 1:
+            lm_head = run_lm_head(ops, device, args)
+            launches += lm_head.pop("launches")
+
         # ---- C4 vocab-sharded tensor parallel (N > 1) ----
         tp = None
         if world > 1:
@@ -423,6 +431,8 @@ def run_ours(args):
     }
     if tp is not None:
         line["tp"] = tp
+    if lm_head is not None:
+        line["lm_head"] = lm_head
     if world == 1 and not args.no_cpu:
         cpu_us, threads, n, kind, what = cpu_reference_time(C1["B"], C1["V"], C1["k"], C1["p"],
                                                             budget_s=args.cpu_budget)
@@ -430,6 +440,49 @@ def run_ours(args):
                                 "sample": f"C1 row (B=1, V=151936, k=50, p=0.9) x {n} calls of {what}, "
                                           f"{threads} host threads"}
     print(json.dumps(line), flush=True)
+
+
+def run_lm_head(ops, device, args):
+    """B=1024 rows of H=4096 hidden states through a [151936, 4096] bf16 LM head: the GEMM alone,
+    the GEMM writing [B, V] logits to HBM followed by the sampler (k=50, p=0.95), and the chunked
+    pipeline (llm_sampling_kernel_b200.lm_head.LMHeadSampler). Synthetic random weights."""
+    from llm_sampling_kernel_b200.lm_head import LMHeadSampler
+
+    B, H, V, k, p = 1024, 4096, 151936, 50, 0.95
+    g = torch.Generator(device=device).manual_seed(17)
+    w = (torch.randn(V, H, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    h = (torch.randn(B, H, generator=g, device=device)).to(torch.bfloat16)
+    logits = torch.empty(B, V, dtype=torch.bfloat16, device=device)
+    lm = LMHeadSampler(w, k, max_batch=B)
+    steps = max(3, min(args.steps, 20))
+    warm = max(3, args.warmup)
+
+    def gemm(i):
+        torch.matmul(h, w.t(), out=logits)
+
+    def unfused(i):
+        torch.matmul(h, w.t(), out=logits)
+        ops.sample_fused(logits, k, p, 0x5EED, i, 0)
+
+    def pipelined(i):
+        lm.sample(h, p, seed=0x5EED, offset=i)
+
+    out = {}
+    for name, fn in (("gemm_only_us", gemm), ("unfused_us", unfused), ("pipelined_us", pipelined)):
+        out[name] = round(timed_steps(fn, steps, warm, 1) * 1000.0 / steps, 3)
+    flops = 2.0 * B * H * V
+    out.update({
+        "B": B, "H": H, "V": V, "top_k": k, "top_p": p, "chunk": lm.chunk, "parts": lm.parts,
+        "gemm_tflops": round(flops / (out["gemm_only_us"] * 1e-6) / 1e12, 1),
+        "sampling_overhead_unfused_us": round(out["unfused_us"] - out["gemm_only_us"], 3),
+        "sampling_overhead_pipelined_us": round(out["pipelined_us"] - out["gemm_only_us"], 3),
+        "launches": steps * (2 + 1 + 3 * lm.parts + 1),
+        "what": "bf16 GEMM (cuBLAS via torch.matmul) into L2-sized chunks, shard top-k per chunk, "
+                "one candidate merge + draw; [B, V] logits never written to HBM",
+    })
+    del w, h, logits, lm
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_tp(ops, world, rank, device, args):

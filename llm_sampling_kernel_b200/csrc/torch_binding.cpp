@@ -284,13 +284,24 @@ std::vector<std::optional<torch::Tensor>> sample_ex(
 }
 
 // Vocab-shard local half: [B, K + 1] packed candidates (uint64 bit patterns in an int64 tensor).
-torch::Tensor shard_candidates(torch::Tensor logits, int64_t top_k, int64_t id_base, int64_t splits) {
+// `out`, when given, is a contiguous int64 cuda [B, top_k + 1] tensor (e.g. one part of a
+// [parts, B, top_k + 1] block) that receives the candidates.
+torch::Tensor shard_candidates(torch::Tensor logits, int64_t top_k, int64_t id_base, int64_t splits,
+                               std::optional<torch::Tensor> out) {
   check_logits(logits);
   check_top_k(top_k);
   c10::cuda::CUDAGuard guard(logits.device());
   const int64_t B = logits.size(0);
   TORCH_CHECK(top_k <= logits.size(1), "shard top_k must not exceed the shard vocabulary");
-  auto cand = empty_i64(logits, {B, top_k + 1});
+  torch::Tensor cand;
+  if (out.has_value()) {
+    cand = *out;
+    TORCH_CHECK(cand.is_cuda() && cand.device() == logits.device() && cand.scalar_type() == at::kLong &&
+                    cand.dim() == 2 && cand.size(0) == B && cand.size(1) == top_k + 1 && cand.is_contiguous(),
+                "out must be a contiguous int64 cuda [B, top_k + 1] tensor on the logits' device");
+  } else {
+    cand = empty_i64(logits, {B, top_k + 1});
+  }
   fs_sample_args a = base_args(logits, top_k, 1.0, splits);
   a.id_base = id_base;
   auto ws = attach_workspace(&a, logits);
@@ -419,7 +430,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("row_base") = 0, py::arg("return_stages") = false, py::arg("path") = 0,
         py::arg("temperature") = 1.0);
   m.def("shard_candidates", &shard_candidates, "vocab-shard local top-k as packed candidates",
-        py::arg("logits"), py::arg("top_k"), py::arg("id_base"), py::arg("splits") = 0);
+        py::arg("logits"), py::arg("top_k"), py::arg("id_base"), py::arg("splits") = 0,
+        py::arg("out") = py::none());
   m.def("merge_sample", &merge_sample, "merge gathered shard candidates and sample",
         py::arg("cand"), py::arg("bf16"), py::arg("top_k"), py::arg("top_p"),
         py::arg("top_k_rows") = py::none(), py::arg("top_p_rows") = py::none(),
