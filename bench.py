@@ -778,7 +778,8 @@ def run_sweep(args):
 
 def run_profile_case(args):
     """A few launches of one configuration, untimed: the target of the ncu captures in profiles/.
-    c1 = the anchor (B=1), c3 = the B=1024 HBM-bound launch."""
+    c1 = the anchor (B=1), c3 = the B=1024 HBM-bound launch, c5w = the top-p-only wide path
+    (B=8, k=V)."""
     sys.path.insert(0, str(ROOT))
     import llm_sampling_kernel_b200 as pkg
 
@@ -787,6 +788,11 @@ def run_profile_case(args):
     if args.profile_case == "c1":
         x = anchor_buffers(1, C1["B"], C1["V"], device)[0]
         k, p = C1["k"], C1["p"]
+    elif args.profile_case == "c5w":
+        # the adversarial top-p-only case: B=8, V=151936 FP16 N(0, 0.1^2), k=V, p=0.5 (wide path)
+        g = torch.Generator(device=device).manual_seed(2)
+        x = (torch.randn(8, C1["V"], generator=g, device=device) * 0.1).to(torch.float16)
+        k, p = C1["V"], 0.5
     else:
         x = zipf_buffers(1, C3["B"], C3["V"], device)[0]
         k, p = C3["k"], C3["p"]
@@ -808,7 +814,7 @@ def main():
                     help="time both paths over CTAs per row x batch x vocabulary x k and exit")
     ap.add_argument("--rungs", action="store_true",
                     help="time the comparison rungs (reference kernel, FlashInfer) and exit")
-    ap.add_argument("--profile-case", choices=["c1", "c3"], default=None,
+    ap.add_argument("--profile-case", choices=["c1", "c3", "c5w"], default=None,
                     help="run three untimed launches of one configuration (ncu target) and exit")
     args = ap.parse_args()
     if args.profile_case:

@@ -1181,6 +1181,7 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C))
   load_slice<DT, C>(p, b, vbase, v);
   uint32_t* hrow = hist + static_cast<size_t>(b) * kKeys;
   uint32_t acc = Fmt<DT>::kNegInf2;
+  uint32_t kmin = 0xFFFFu;
 #pragma unroll
   for (int c = 0; c < C; ++c) {
     acc = pair_max_nan<DT>(acc, pair_max_nan<DT>(pair_max_nan<DT>(v[c].x, v[c].y), pair_max_nan<DT>(v[c].z, v[c].w)));
@@ -1191,6 +1192,7 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C))
       const uint32_t key = chunk_key(v[c], j);
       const unsigned peers = __match_any_sync(0xFFFFFFFFu, valid ? key : 0xFFFFFFFFu);
       if (valid && lane == __ffs(peers) - 1) atomicAdd(&hrow[key], static_cast<uint32_t>(__popc(peers)));
+      if (valid) kmin = min(kmin, key);
     }
   }
   const uint32_t mbits = half_max_nan<DT>(acc & 0xFFFFu, acc >> 16);
@@ -1203,18 +1205,21 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C))
   }
   const uint32_t f = __reduce_or_sync(0xFFFFFFFFu, flags);
   const uint32_t m = __reduce_max_sync(0xFFFFFFFFu, Fmt<DT>::is_nan(mbits) ? 0u : order_key(mbits));
+  const uint32_t mn = __reduce_min_sync(0xFFFFFFFFu, kmin);
   if (lane == 0) {
-    wf[t >> 5] = f;
+    wf[t >> 5] = f | (mn << 16);
     wm[t >> 5] = m;
   }
   __syncthreads();
   if (t == 0) {
-    uint32_t ff = 0u, mm = 0u;
+    uint32_t ff = 0u, mm = 0u, mnn = 0xFFFFu;
     for (int w = 0; w < NT / 32; ++w) {
-      ff |= wf[w];
+      ff |= wf[w] & 0xFFFFu;
+      mnn = min(mnn, wf[w] >> 16);
       mm = max(mm, wm[w]);
     }
-    sflag[static_cast<size_t>(b) * S + s] = ff;
+    // row flags in the low half, the slice's smallest key in the high half
+    sflag[static_cast<size_t>(b) * S + s] = ff | (mnn << 16);
     smax[static_cast<size_t>(b) * S + s] = mm;
   }
 }
@@ -1244,9 +1249,11 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   float pp;
   bool bad;
   row_params(p, b, &kk, &pp, &bad);
-  uint32_t F = 0u, mkey = 0u;
+  uint32_t F = 0u, mkey = 0u, kmin = 0xFFFFu;
   for (int r = 0; r < S; ++r) {
-    F |= sflag[static_cast<size_t>(b) * S + r];
+    const uint32_t w = sflag[static_cast<size_t>(b) * S + r];
+    F |= w & 0xFFFFu;
+    kmin = min(kmin, w >> 16);
     mkey = max(mkey, smax[static_cast<size_t>(b) * S + r]);
   }
   int st = FS_ROW_OK;
@@ -1266,53 +1273,72 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     return;
   }
 
-  // thread t: keys kh = 65535 - 64 t down to kh - 63, read as 16 vectors from the top one down
-  const uint32_t kl = static_cast<uint32_t>(kKeys - kKeysPerThread * (t + 1));
-  const uint4* h4 = reinterpret_cast<const uint4*>(hist + static_cast<size_t>(b) * kKeys + kl);
-
-  // ---- the k-th key T and the ties `need` at T ----
-  uint32_t csum = 0u;
-#pragma unroll 4
-  for (int q = kKeysPerThread / 4 - 1; q >= 0; --q) {
-    const uint4 w = h4[q];
-    csum += w.x + w.y + w.z + w.w;
-  }
-  uint32_t ctot = 0u;
-  const uint32_t cbase = block_incl_scan<uint32_t, kRowThreads>(csum, uscr, &ctot) - csum;
-  const uint32_t ukk = static_cast<uint32_t>(kk);
-  if (cbase < ukk && ukk <= cbase + csum) {
-    uint32_t run = cbase;
-    for (int q = kKeysPerThread / 4 - 1; q >= 0; --q) {
-      const uint4 w = h4[q];
-      const uint32_t cnt[4] = {w.w, w.z, w.y, w.x};
-      bool done = false;
-      for (int i = 0; i < 4; ++i) {
-        if (run + cnt[i] >= ukk) {
-          uscr[36] = kl + 4u * static_cast<uint32_t>(q) + 3u - static_cast<uint32_t>(i);
-          uscr[37] = ukk - run;
-          done = true;
-          break;
+  // The keys holding elements span [kmin, mkey]; thread t takes an equal share of that span
+  // (rounded to whole 16-byte vectors), from the top down, so that the per-key work is spread over
+  // every thread however narrow the span. each_key(fn) calls fn(key, count, rank) for the
+  // thread's keys in descending order (rank = 65535 - key: ascending in the sorted order),
+  // reading the counts in batches of eight 16-byte loads issued together; fn returns true to stop.
+  const uint32_t top = mkey | 3u, bot = min(kmin, mkey) & ~3u;
+  const uint32_t span = top - bot + 1u;
+  const uint32_t share = (((span + kRowThreads - 1) / kRowThreads) + 3u) & ~3u;
+  const uint32_t mine_hi = static_cast<uint32_t>(t) * share < span ? top - static_cast<uint32_t>(t) * share : 0u;
+  const uint32_t mine_lo = mine_hi >= bot + share - 1u ? mine_hi - share + 1u : bot;
+  const int nvec = static_cast<uint32_t>(t) * share < span ? static_cast<int>((mine_hi - mine_lo + 1u) / 4u) : 0;
+  const uint4* h4 = reinterpret_cast<const uint4*>(hist + static_cast<size_t>(b) * kKeys + mine_lo);
+  auto each_key = [&](auto&& fn) {
+#pragma unroll 1
+    for (int v0 = nvec - 1; v0 >= 0; v0 -= 8) {
+      uint4 w[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[i] = v0 - i >= 0 ? h4[v0 - i] : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (v0 - i < 0) return;
+        const uint32_t cnt[4] = {w[i].w, w[i].z, w[i].y, w[i].x};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t key = mine_lo + 4u * static_cast<uint32_t>(v0 - i) + 3u - static_cast<uint32_t>(j);
+          if (fn(key, cnt[j], static_cast<int>(65535u - key))) return;
         }
-        run += cnt[i];
       }
-      if (done) break;
     }
+  };
+
+  // ---- the k-th key T and the ties `need` at T (k >= V: every element, T = 0) ----
+  const uint32_t ukk = static_cast<uint32_t>(kk);
+  uint32_t T = 0u, need = 0u;
+  if (kk < p.vocab) {
+    uint32_t csum = 0u;
+    each_key([&](uint32_t, uint32_t n, int) {
+      csum += n;
+      return false;
+    });
+    uint32_t ctot = 0u;
+    const uint32_t cbase = block_incl_scan<uint32_t, kRowThreads>(csum, uscr, &ctot) - csum;
+    if (cbase < ukk && ukk <= cbase + csum) {
+      uint32_t run = cbase;
+      each_key([&](uint32_t key, uint32_t n, int) {
+        if (run + n >= ukk) {
+          uscr[36] = key;
+          uscr[37] = ukk - run;
+          return true;
+        }
+        run += n;
+        return false;
+      });
+    }
+    __syncthreads();
+    T = uscr[36];
+    need = uscr[37];
   }
-  __syncthreads();
-  const uint32_t T = uscr[36], need = uscr[37];
 
   // ---- Z over the top-k, in a fixed order ----
   double part = 0.0;
-  for (int q = kKeysPerThread / 4 - 1; q >= 0; --q) {
-    const uint4 w = h4[q];
-    const uint32_t cnt[4] = {w.w, w.z, w.y, w.x};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t key = kl + 4u * static_cast<uint32_t>(q) + 3u - static_cast<uint32_t>(i);
-      const uint32_t n = topk_count(key, cnt[i], T, need);
-      if (n != 0u) part += static_cast<double>(n) * static_cast<double>(expf(tail_logit<DT>(p, key) - mf));
-    }
-  }
+  each_key([&](uint32_t key, uint32_t cnt, int) {
+    const uint32_t n = topk_count(key, cnt, T, need);
+    if (n != 0u) part += static_cast<double>(n) * static_cast<double>(expf(tail_logit<DT>(p, key) - mf));
+    return false;
+  });
   part = warp_sum(part);
   if (lane == 0) dscr[t >> 5] = part;
   __syncthreads();
@@ -1324,61 +1350,62 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   __syncthreads();
   const float z = static_cast<float>(dscr[32]);
 
-  // ---- the fixed-point mass above this thread's keys ----
+  // ---- the fixed-point mass above this thread's keys, and the probability of its last group ----
   uint64_t msum = 0ull;
-  for (int q = kKeysPerThread / 4 - 1; q >= 0; --q) {
-    const uint4 w = h4[q];
-    const uint32_t cnt[4] = {w.w, w.z, w.y, w.x};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t key = kl + 4u * static_cast<uint32_t>(q) + 3u - static_cast<uint32_t>(i);
-      const uint32_t n = topk_count(key, cnt[i], T, need);
-      if (n != 0u)
-        msum += static_cast<uint64_t>(n) * prob_to_fixed(__fdiv_rn(expf(tail_logit<DT>(p, key) - mf), z));
+  float last_pr = 0.0f;
+  bool has = false;
+  each_key([&](uint32_t key, uint32_t cnt, int) {
+    const uint32_t n = topk_count(key, cnt, T, need);
+    if (n != 0u) {
+      last_pr = __fdiv_rn(expf(tail_logit<DT>(p, key) - mf), z);
+      msum += static_cast<uint64_t>(n) * prob_to_fixed(last_pr);
+      has = true;
     }
-  }
+    return false;
+  });
   uint64_t mtot = 0ull;
   const uint64_t mbase = block_incl_scan<uint64_t, kRowThreads>(msum, qscr, &mtot) - msum;
+  const uint64_t mend = mbase + msum;  // the exact mass through this thread's last element
 
-  // The first group (from the largest key) of this thread's range whose end meets `pred(end
-  // mass, p)`: its key rank t * 64 + j (or kNone), and the mass before it in *start.
+  // Both the cut and the draw conditions hold from some element of the sorted order on, so the
+  // element is in the first thread whose last element meets the condition; that thread alone
+  // scans its keys for the group (first_group), then the position inside the group.
   constexpr int kNone = 0x7FFFFFFF;
   auto first_group = [&](int mode, float target, uint64_t* start, uint32_t* n_out, uint64_t* pf_out,
                          float* pr_out) -> int {
     uint64_t run = mbase;
-    for (int q = kKeysPerThread / 4 - 1; q >= 0; --q) {
-      const uint4 w = h4[q];
-      const uint32_t cnt[4] = {w.w, w.z, w.y, w.x};
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t key = kl + 4u * static_cast<uint32_t>(q) + 3u - static_cast<uint32_t>(i);
-        const uint32_t n = topk_count(key, cnt[i], T, need);
-        if (n == 0u) continue;
-        const float pr = __fdiv_rn(expf(tail_logit<DT>(p, key) - mf), z);
-        const uint64_t pf = prob_to_fixed(pr);
-        const uint64_t end = run + static_cast<uint64_t>(n) * pf;
-        const bool hit = mode == 0 ? !((fixed_to_float(end) - pr) < pp) : fixed_to_float(end) >= target;
-        if (hit) {
-          *start = run;
-          *n_out = n;
-          *pf_out = pf;
-          *pr_out = pr;
-          return t * kKeysPerThread + (kKeysPerThread - 1 - (4 * q + 3 - i));
-        }
-        run = end;
+    int found = kNone;
+    each_key([&](uint32_t key, uint32_t cnt, int rank) {
+      const uint32_t n = topk_count(key, cnt, T, need);
+      if (n == 0u) return false;
+      const float pr = __fdiv_rn(expf(tail_logit<DT>(p, key) - mf), z);
+      const uint64_t pf = prob_to_fixed(pr);
+      const uint64_t end = run + static_cast<uint64_t>(n) * pf;
+      const bool hit = mode == 0 ? !((fixed_to_float(end) - pr) < pp) : fixed_to_float(end) >= target;
+      if (hit) {
+        *start = run;
+        *n_out = n;
+        *pf_out = pf;
+        *pr_out = pr;
+        found = rank;
+        return true;
       }
-    }
-    return kNone;
+      run = end;
+      return false;
+    });
+    return found;
   };
 
   // ---- the cut: xr = the exact mass through r ----
   uint64_t xr = mtot;
   if (pp < 1.0f) {
-    uint64_t start = 0ull, pf = 0ull;
-    uint32_t n = 0u;
-    float pr = 0.0f;
-    const int mine = first_group(0, 0.0f, &start, &n, &pf, &pr);
-    const int gc = block_min<kRowThreads>(mine, iscr);
-    if (gc != kNone && mine == gc) {
+    const bool meets = has && !((fixed_to_float(mend) - last_pr) < pp);
+    const int owner = block_min<kRowThreads>(meets ? t : kNone, iscr);
+    if (t == owner) {
+      uint64_t start = 0ull, pf = 0ull;
+      uint32_t n = 0u;
+      float pr = 0.0f;
+      first_group(0, 0.0f, &start, &n, &pf, &pr);
       // the first position j of the group that meets the condition (it holds at j = n - 1)
       uint32_t lo = 0u, hi = n - 1u;
       while (lo < hi) {
@@ -1389,34 +1416,32 @@ __global__ void __launch_bounds__(kRowThreads, 1)
       found[0] = start + static_cast<uint64_t>(lo) * pf;
     }
     __syncthreads();
-    if (gc != kNone) xr = found[0];
+    if (owner != kNone) xr = found[0];
   }
   const float zp = fixed_to_float(xr);
   const float target = __fmul_rn(row_uniform(p, b), zp);
 
   // ---- the draw: the first element with c_i >= target ----
-  {
+  const int owner = block_min<kRowThreads>(has && fixed_to_float(mend) >= target ? t : kNone, iscr);
+  if (t == owner) {
     uint64_t start = 0ull, pf = 0ull;
     uint32_t n = 0u;
     float pr = 0.0f;
-    const int mine = first_group(1, target, &start, &n, &pf, &pr);
-    const int gd = block_min<kRowThreads>(mine, iscr);
-    if (mine == gd && gd != kNone) {
-      uint32_t lo = 0u, hi = n - 1u;
-      while (lo < hi) {
-        const uint32_t mid = (lo + hi) >> 1;
-        if (fixed_to_float(start + static_cast<uint64_t>(mid + 1u) * pf) >= target) hi = mid;
-        else lo = mid + 1u;
-      }
-      rr[0] = static_cast<uint32_t>(FS_ROW_OK);
-      rr[1] = static_cast<uint32_t>(kKeys - 1 - gd);  // the key of rank gd from the top
-      rr[2] = lo;
-      rr[3] = 1u;
+    const int gd = first_group(1, target, &start, &n, &pf, &pr);
+    uint32_t lo = 0u, hi = n - 1u;
+    while (lo < hi) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if (fixed_to_float(start + static_cast<uint64_t>(mid + 1u) * pf) >= target) hi = mid;
+      else lo = mid + 1u;
     }
-    if (gd == kNone && t == 0) {  // (not reached: the last group with elements meets the draw)
-      rr[0] = static_cast<uint32_t>(FS_ROW_OK);
-      rr[3] = 0u;
-    }
+    rr[0] = static_cast<uint32_t>(FS_ROW_OK);
+    rr[1] = static_cast<uint32_t>(kKeys - 1 - gd);  // the key of rank gd
+    rr[2] = lo;
+    rr[3] = 1u;
+  }
+  if (owner == kNone && t == 0) {  // (not reached: the last element meets the draw)
+    rr[0] = static_cast<uint32_t>(FS_ROW_OK);
+    rr[3] = 0u;
   }
 }
 
