@@ -1249,13 +1249,17 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   float pp;
   bool bad;
   row_params(p, b, &kk, &pp, &bad);
+  // the slices' flags, smallest keys and maxima: each warp reads them a lane per slice
   uint32_t F = 0u, mkey = 0u, kmin = 0xFFFFu;
-  for (int r = 0; r < S; ++r) {
+  for (int r = lane; r < S; r += 32) {
     const uint32_t w = sflag[static_cast<size_t>(b) * S + r];
     F |= w & 0xFFFFu;
     kmin = min(kmin, w >> 16);
     mkey = max(mkey, smax[static_cast<size_t>(b) * S + r]);
   }
+  F = __reduce_or_sync(0xFFFFFFFFu, F);
+  kmin = __reduce_min_sync(0xFFFFFFFFu, kmin);
+  mkey = __reduce_max_sync(0xFFFFFFFFu, mkey);
   int st = FS_ROW_OK;
   if (bad) st = FS_ROW_BAD_PARAM;
   else if (F & kFlagNaN) st = FS_ROW_NAN;
@@ -1275,9 +1279,9 @@ __global__ void __launch_bounds__(kRowThreads, 1)
 
   // The keys holding elements span [kmin, mkey]; thread t takes an equal share of that span
   // (rounded to whole 16-byte vectors), from the top down, so that the per-key work is spread over
-  // every thread however narrow the span. each_key(fn) calls fn(key, count, rank) for the
-  // thread's keys in descending order (rank = 65535 - key: ascending in the sorted order),
-  // reading the counts in batches of eight 16-byte loads issued together; fn returns true to stop.
+  // every thread however narrow the span. each_key(fn) calls fn(key, count) for the thread's
+  // keys in descending order (ascending in the sorted order), reading the counts in batches of
+  // eight 16-byte loads issued together; fn returns true to stop.
   const uint32_t top = mkey | 3u, bot = min(kmin, mkey) & ~3u;
   const uint32_t span = top - bot + 1u;
   const uint32_t share = (((span + kRowThreads - 1) / kRowThreads) + 3u) & ~3u;
@@ -1298,7 +1302,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const uint32_t key = mine_lo + 4u * static_cast<uint32_t>(v0 - i) + 3u - static_cast<uint32_t>(j);
-          if (fn(key, cnt[j], static_cast<int>(65535u - key))) return;
+          if (fn(key, cnt[j])) return;
         }
       }
     }
@@ -1309,7 +1313,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   uint32_t T = 0u, need = 0u;
   if (kk < p.vocab) {
     uint32_t csum = 0u;
-    each_key([&](uint32_t, uint32_t n, int) {
+    each_key([&](uint32_t, uint32_t n) {
       csum += n;
       return false;
     });
@@ -1317,7 +1321,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     const uint32_t cbase = block_incl_scan<uint32_t, kRowThreads>(csum, uscr, &ctot) - csum;
     if (cbase < ukk && ukk <= cbase + csum) {
       uint32_t run = cbase;
-      each_key([&](uint32_t key, uint32_t n, int) {
+      each_key([&](uint32_t key, uint32_t n) {
         if (run + n >= ukk) {
           uscr[36] = key;
           uscr[37] = ukk - run;
@@ -1334,7 +1338,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
 
   // ---- Z over the top-k, in a fixed order ----
   double part = 0.0;
-  each_key([&](uint32_t key, uint32_t cnt, int) {
+  each_key([&](uint32_t key, uint32_t cnt) {
     const uint32_t n = topk_count(key, cnt, T, need);
     if (n != 0u) part += static_cast<double>(n) * static_cast<double>(expf(tail_logit<DT>(p, key) - mf));
     return false;
@@ -1354,7 +1358,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   uint64_t msum = 0ull;
   float last_pr = 0.0f;
   bool has = false;
-  each_key([&](uint32_t key, uint32_t cnt, int) {
+  each_key([&](uint32_t key, uint32_t cnt) {
     const uint32_t n = topk_count(key, cnt, T, need);
     if (n != 0u) {
       last_pr = __fdiv_rn(expf(tail_logit<DT>(p, key) - mf), z);
@@ -1368,32 +1372,48 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   const uint64_t mend = mbase + msum;  // the exact mass through this thread's last element
 
   // Both the cut and the draw conditions hold from some element of the sorted order on, so the
-  // element is in the first thread whose last element meets the condition; that thread alone
-  // scans its keys for the group (first_group), then the position inside the group.
+  // element is in the first thread whose last element meets the condition (the owner). The
+  // owner's warp searches the owner's keys (at most 64): lane l takes the keys of ranks 2l and
+  // 2l + 1 within the owner's share, a warp scan of their masses gives each group's start, and
+  // the first lane holding a group whose last element meets the condition reports it (that lane
+  // then finds the position inside the group by binary search). Returns that lane, -1 if none.
   constexpr int kNone = 0x7FFFFFFF;
-  auto first_group = [&](int mode, float target, uint64_t* start, uint32_t* n_out, uint64_t* pf_out,
-                         float* pr_out) -> int {
-    uint64_t run = mbase;
-    int found = kNone;
-    each_key([&](uint32_t key, uint32_t cnt, int rank) {
-      const uint32_t n = topk_count(key, cnt, T, need);
-      if (n == 0u) return false;
-      const float pr = __fdiv_rn(expf(tail_logit<DT>(p, key) - mf), z);
-      const uint64_t pf = prob_to_fixed(pr);
-      const uint64_t end = run + static_cast<uint64_t>(n) * pf;
-      const bool hit = mode == 0 ? !((fixed_to_float(end) - pr) < pp) : fixed_to_float(end) >= target;
-      if (hit) {
-        *start = run;
-        *n_out = n;
-        *pf_out = pf;
-        *pr_out = pr;
-        found = rank;
-        return true;
-      }
-      run = end;
-      return false;
-    });
-    return found;
+  auto owner_group = [&](int owner, int mode, float target, uint64_t* start, uint32_t* n_out,
+                         uint64_t* pf_out, float* pr_out, uint32_t* key_out) -> int {
+    const int ol = owner & 31;
+    const uint64_t ob = __shfl_sync(0xFFFFFFFFu, mbase, ol);
+    const uint32_t ohi = __shfl_sync(0xFFFFFFFFu, mine_hi, ol);
+    const int onk = 4 * __shfl_sync(0xFFFFFFFFu, nvec, ol);
+    const uint32_t* hrow = hist + static_cast<size_t>(b) * kKeys;
+    uint32_t n[2];
+    float pr[2];
+    uint64_t pf[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int i = 2 * lane + j;
+      const uint32_t key = ohi - static_cast<uint32_t>(i);
+      n[j] = i < onk ? topk_count(key, hrow[key], T, need) : 0u;
+      pr[j] = n[j] != 0u ? __fdiv_rn(expf(tail_logit<DT>(p, key) - mf), z) : 0.0f;
+      pf[j] = prob_to_fixed(pr[j]);
+    }
+    const uint64_t m0 = static_cast<uint64_t>(n[0]) * pf[0], m1 = static_cast<uint64_t>(n[1]) * pf[1];
+    const uint64_t run0 = ob + warp_incl_scan<uint64_t>(m0 + m1) - (m0 + m1);
+    const uint64_t ends[2] = {run0 + m0, run0 + m0 + m1};
+    int hit = -1;
+#pragma unroll
+    for (int j = 1; j >= 0; --j) {
+      const float c = fixed_to_float(ends[j]);
+      if (n[j] != 0u && (mode == 0 ? !((c - pr[j]) < pp) : c >= target)) hit = j;
+    }
+    const int f = __ffs(__ballot_sync(0xFFFFFFFFu, hit >= 0)) - 1;
+    if (lane == f) {
+      *start = hit == 0 ? run0 : run0 + m0;
+      *n_out = n[hit];
+      *pf_out = pf[hit];
+      *pr_out = pr[hit];
+      *key_out = ohi - static_cast<uint32_t>(2 * lane + hit);
+    }
+    return f;
   };
 
   // ---- the cut: xr = the exact mass through r ----
@@ -1401,19 +1421,22 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   if (pp < 1.0f) {
     const bool meets = has && !((fixed_to_float(mend) - last_pr) < pp);
     const int owner = block_min<kRowThreads>(meets ? t : kNone, iscr);
-    if (t == owner) {
+    if (owner != kNone && (t >> 5) == (owner >> 5)) {
       uint64_t start = 0ull, pf = 0ull;
-      uint32_t n = 0u;
+      uint32_t n = 0u, key = 0u;
       float pr = 0.0f;
-      first_group(0, 0.0f, &start, &n, &pf, &pr);
-      // the first position j of the group that meets the condition (it holds at j = n - 1)
-      uint32_t lo = 0u, hi = n - 1u;
-      while (lo < hi) {
-        const uint32_t mid = (lo + hi) >> 1;
-        if (!((fixed_to_float(start + static_cast<uint64_t>(mid + 1u) * pf) - pr) < pp)) hi = mid;
-        else lo = mid + 1u;
+      const int f = owner_group(owner, 0, 0.0f, &start, &n, &pf, &pr, &key);
+      if (lane == f) {
+        // the first position j of the group that meets the condition (it holds at j = n - 1)
+        uint32_t lo = 0u, hi = n - 1u;
+        while (lo < hi) {
+          const uint32_t mid = (lo + hi) >> 1;
+          if (!((fixed_to_float(start + static_cast<uint64_t>(mid + 1u) * pf) - pr) < pp)) hi = mid;
+          else lo = mid + 1u;
+        }
+        found[0] = start + static_cast<uint64_t>(lo) * pf;
       }
-      found[0] = start + static_cast<uint64_t>(lo) * pf;
+      if (f < 0 && lane == 0) found[0] = mtot;  // (not reached: the owner's last element meets it)
     }
     __syncthreads();
     if (owner != kNone) xr = found[0];
@@ -1423,21 +1446,27 @@ __global__ void __launch_bounds__(kRowThreads, 1)
 
   // ---- the draw: the first element with c_i >= target ----
   const int owner = block_min<kRowThreads>(has && fixed_to_float(mend) >= target ? t : kNone, iscr);
-  if (t == owner) {
+  if (owner != kNone && (t >> 5) == (owner >> 5)) {
     uint64_t start = 0ull, pf = 0ull;
-    uint32_t n = 0u;
+    uint32_t n = 0u, key = 0u;
     float pr = 0.0f;
-    const int gd = first_group(1, target, &start, &n, &pf, &pr);
-    uint32_t lo = 0u, hi = n - 1u;
-    while (lo < hi) {
-      const uint32_t mid = (lo + hi) >> 1;
-      if (fixed_to_float(start + static_cast<uint64_t>(mid + 1u) * pf) >= target) hi = mid;
-      else lo = mid + 1u;
+    const int f = owner_group(owner, 1, target, &start, &n, &pf, &pr, &key);
+    if (lane == f) {
+      uint32_t lo = 0u, hi = n - 1u;
+      while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (fixed_to_float(start + static_cast<uint64_t>(mid + 1u) * pf) >= target) hi = mid;
+        else lo = mid + 1u;
+      }
+      rr[0] = static_cast<uint32_t>(FS_ROW_OK);
+      rr[1] = key;
+      rr[2] = lo;
+      rr[3] = 1u;
     }
-    rr[0] = static_cast<uint32_t>(FS_ROW_OK);
-    rr[1] = static_cast<uint32_t>(kKeys - 1 - gd);  // the key of rank gd
-    rr[2] = lo;
-    rr[3] = 1u;
+    if (f < 0 && lane == 0) {
+      rr[0] = static_cast<uint32_t>(FS_ROW_OK);
+      rr[3] = 0u;
+    }
   }
   if (owner == kNone && t == 0) {  // (not reached: the last element meets the draw)
     rr[0] = static_cast<uint32_t>(FS_ROW_OK);
