@@ -8,9 +8,14 @@ the measured peak (the C3 config, reported in `roofline`).
 
 * A step is one sampling call on one batch. `value` is the amortised device time per call over
   exactly K back-to-back steps, inputs resident in HBM, cold L2: the steps rotate over enough
-  distinct input buffers to exceed 2x L2 (126 MB).
-* `e2e` is the same metric through the public API with host buffers: pinned host logits copied
-  to the device, the call, and the ids copied back, every step, inside the timed region.
+  distinct input buffers to exceed 2x L2 (126 MB). A short device spin before the start event
+  lets the host queue the calls ahead of the GPU, so a small K measures device latency rather
+  than the host's first launches into an idle GPU; `no_queue_fill_us` is the same K calls
+  without it.
+* `e2e` is the same metric through the public API with host buffers, every step inside the timed
+  region: `fused.sample_fused` on pinned host logits, which the kernel reads over PCIe in place,
+  writing the id into a pinned host tensor (`staged_us`: the same with copy-engine transfers, an
+  upload into a device buffer and a download of the id).
 * `roofline` is the B=1024 call (311 MB of logits per call, two rotating buffers > 2x L2). At that
   batch the call is the streaming path's two launches (slice kernel, then row merge); the time
   is the CUDA-event time of the whole call, so `achieved` (algorithmic bytes B*V*2 + B*8 over it)
@@ -206,16 +211,27 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
-def timed_steps(fn, steps, warmup, world):
+QUEUE_FILL_US = 200  # device spin ahead of the start event (see timed_steps)
+
+
+def timed_steps(fn, steps, warmup, world, queue_fill=True):
     """Warm-up, then exactly `steps` calls between CUDA events on the current stream with a
     barrier + synchronize on both sides. Returns the device ms of the timed region. Step indices
     continue past the warm-up (fn(warmup + i)), so a timed step never reuses the input buffer of a
-    warm-up step."""
+    warm-up step.
+
+    queue_fill: a device spin of QUEUE_FILL_US is enqueued before the start event, so the host
+    has issued the first calls by the time the GPU reaches them and the events time the calls'
+    amortised device latency, not the host's first launches into an idle GPU (the reference's
+    harness gets the same by calibrating thousands of calls per sample). The spin is outside the
+    events; the timed region holds exactly the `steps` calls."""
     for i in range(warmup):
         fn(i)
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
+    if queue_fill:
+        torch.cuda._sleep(int(QUEUE_FILL_US * 2000))  # cycles at about 2 GHz
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for i in range(steps):
@@ -311,10 +327,15 @@ def run_ours(args):
         ms = timed_steps(c1_step, args.steps, args.warmup, world)
         launches += args.steps
         c1_us = max_over_ranks(ms * 1000.0 / args.steps, world)
+        # the same K calls issued into an idle GPU (host launch rate included)
+        ms_nf = timed_steps(c1_step, args.steps, args.warmup, world, queue_fill=False)
+        launches += args.steps
+        c1_nofill_us = max_over_ranks(ms_nf * 1000.0 / args.steps, world)
         # hot L2 (one buffer), for reference
         ms_hot = timed_steps(lambda i: ops.sample_fused(bufs[0], C1["k"], C1["p"], 0x5EED, i, 0),
                              args.steps, args.warmup, world)
         c1_hot_us = max_over_ranks(ms_hot * 1000.0 / args.steps, world)
+        launches += args.steps
         # the same calls replayed from a CUDA graph (how a serving engine issues a decode step):
         # 64 calls over 64 rotating buffers per graph; generator mode so replays advance the RNG
         per_graph = 64
@@ -335,17 +356,35 @@ def run_ours(args):
         del g
 
         # ---- e2e through the public API with host buffers (pinned) ----
-        host = [b.cpu().pin_memory() for b in bufs[:8]]
+        # Each step samples a different pinned host buffer (as many as the device-resident anchor
+        # rotates over, > 2x L2, so no step can reuse lines another step brought in): the call
+        # reads the logits over PCIe in place and writes the id into a pinned host tensor. The
+        # copy-engine variant (upload into a device buffer, the call, download of the id) is
+        # timed beside it as `staged_us`.
+        host = [b.cpu().pin_memory() for b in bufs]
         ids_host = torch.empty(C1["B"], dtype=torch.int64).pin_memory()
         dev_in = torch.empty_like(bufs[0])
+        e2e_out = []
 
         def e2e_step(i):
+            out = fused.sample_fused(host[i % len(host)], C1["k"], C1["p"], offset=i)
+            if i == 0:
+                e2e_out.append(out)
+
+        ms_e2e = timed_steps(e2e_step, args.steps, args.warmup, world, queue_fill=False)
+        e2e_us = max_over_ranks(ms_e2e * 1000.0 / args.steps, world)
+        # the first step's id, read on the host, equals the device-resident call's
+        e2e_ok = int(e2e_out[0][0]) == int(ops.sample_fused(bufs[0], C1["k"], C1["p"], 0x5EED, 0, 0).cpu()[0])
+        launches += args.steps
+
+        def staged_step(i):
             dev_in.copy_(host[i % len(host)], non_blocking=True)
             out = fused.sample_fused(dev_in, C1["k"], C1["p"], offset=i)
             ids_host.copy_(out, non_blocking=True)
 
-        ms_e2e = timed_steps(e2e_step, args.steps, args.warmup, world)
-        e2e_us = max_over_ranks(ms_e2e * 1000.0 / args.steps, world)
+        ms_staged = timed_steps(staged_step, args.steps, args.warmup, world, queue_fill=False)
+        staged_us = max_over_ranks(ms_staged * 1000.0 / args.steps, world)
+        launches += args.steps
         del bufs, host
 
         # ---- C3 B=1024 HBM-bound launch (roofline); rows sharded across ranks ----
@@ -405,10 +444,17 @@ def run_ours(args):
             "plan": {"splits": plan1[0], "chunks": plan1[1], "threads": plan1[2], "capacity": plan1[3]},
             "parallelism": f"dp{world} (independent rows, no collective)",
         },
+        "queue_fill": f"{QUEUE_FILL_US} us device spin before the start event (amortised device latency)",
+        "no_queue_fill_us": round(c1_nofill_us, 3),
         "hot_l2_us": round(c1_hot_us, 3),
         "graph_replay_us": round(c1_graph_us, 3),
         "e2e": {"value": round(e2e_us, 3), "unit": "µs/call", "h2d_bytes_per_step": per,
-                "d2h_bytes_per_step": C1["B"] * 8, "api": "llm_sampling_kernel_b200.fused.sample_fused"},
+                "d2h_bytes_per_step": C1["B"] * 8, "api": "llm_sampling_kernel_b200.fused.sample_fused",
+                "transfer": "pinned host logits read in place over PCIe by the call's kernel, id written "
+                            "to a pinned host tensor; one host buffer per step, rotating over > 2x L2",
+                "ids_match_device_call": e2e_ok,
+                "staged_us": round(staged_us, 3),
+                "staged": "copy-engine upload to a device buffer, the call, copy-engine download of the id"},
         "roofline": {
             "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 4),

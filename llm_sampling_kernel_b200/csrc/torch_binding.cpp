@@ -4,6 +4,7 @@
 // (csrc/bindings.cpp:16-25, csrc/fused_sampling.cu:337-540). The only work done here is
 // unpacking tensors, the current stream and torch's generator state; every computation goes
 // through the C ABI of libfs_b200.so (include/fused_sampling_b200.h).
+#include <ATen/core/CachingHostAllocator.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <ATen/cuda/CUDAGeneratorImpl.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -19,15 +20,59 @@
 
 namespace {
 
+// Where a call's logits live. A cuda tensor runs on its own device. A tensor in pinned host
+// memory (deliberate extension of the reference, which takes cuda tensors only) is read in place
+// by the kernels over PCIe -- pinned pages are mapped into every device's address space -- on the
+// current CUDA device, with no copy-engine transfer; the call's outputs are then pinned host
+// tensors that the kernels write directly. Like a non_blocking copy to the host, they hold their
+// values once the stream has reached the call.
+struct Source {
+  const void* ptr = nullptr;  // device-accessible address of the logits
+  bool host = false;          // pinned host memory
+  c10::Device device = c10::Device(c10::kCUDA, 0);
+  torch::TensorOptions opts;  // outputs: on the logits' device, or in pinned host memory
+};
+
 // Deliberate difference to the reference: top_k may be anything up to the vocabulary size
 // (the reference rejected top_k > 128, csrc/fused_sampling.cu:351).
-void check_logits(const torch::Tensor& logits) {
-  TORCH_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.stride(1) == 1 &&
+Source check_logits(const torch::Tensor& logits, bool allow_host = false) {
+  const bool host = allow_host && !logits.is_cuda() && logits.device().is_cpu() && logits.is_pinned();
+  TORCH_CHECK((logits.is_cuda() || host) && logits.dim() == 2 && logits.stride(1) == 1 &&
                   logits.stride(0) >= logits.size(1),
-              "logits must be a contiguous cuda [B, V] tensor");
+              allow_host ? "logits must be a contiguous cuda [B, V] tensor (or one in pinned host memory)"
+                         : "logits must be a contiguous cuda [B, V] tensor");
   TORCH_CHECK(logits.scalar_type() == at::kBFloat16 || logits.scalar_type() == at::kHalf,
               "logits must be float16 or bfloat16");
   TORCH_CHECK(logits.size(0) >= 1 && logits.size(1) >= 1, "logits must be a non-empty [B, V] tensor");
+  Source src;
+  if (!host) {
+    src.ptr = logits.data_ptr();
+    src.device = logits.device();
+    src.opts = logits.options();
+    return src;
+  }
+  cudaPointerAttributes at = {};
+  const cudaError_t e = cudaPointerGetAttributes(&at, logits.data_ptr());
+  if (e != cudaSuccess) cudaGetLastError();
+  TORCH_CHECK(e == cudaSuccess && at.type == cudaMemoryTypeHost && at.devicePointer != nullptr,
+              "pinned host logits are not mapped into the device address space");
+  src.ptr = at.devicePointer;
+  src.host = true;
+  src.device = c10::Device(c10::kCUDA, c10::cuda::current_device());
+  src.opts = logits.options().pinned_memory(true);
+  return src;
+}
+
+// Host tensors that the call's kernels read or write stay out of the pinned-memory cache's reuse
+// until the stream has passed the call (what torch does for a non_blocking host copy).
+void hold_host(const Source& src, std::initializer_list<const torch::Tensor*> ts) {
+  if (!src.host) return;
+  const c10::Stream stream = at::cuda::getCurrentCUDAStream().unwrap();
+  for (const torch::Tensor* t : ts) {
+    if (t == nullptr || !t->defined()) continue;
+    const auto& dp = t->storage().data_ptr();
+    at::getHostAllocator(at::kCUDA)->record_event(dp.get(), dp.get_context(), stream);
+  }
 }
 
 void check_top_k(int64_t top_k) { TORCH_CHECK(top_k >= 1, "top_k must be >= 1"); }
@@ -47,10 +92,10 @@ fs_stream_t current_stream() {
 // Reference top_p is a double compared as p >= 1.0 before narrowing (benchmarks/reference.py:58).
 float narrow_top_p(double top_p) { return top_p >= 1.0 ? 1.0f : static_cast<float>(top_p); }
 
-fs_sample_args base_args(const torch::Tensor& logits, int64_t top_k, double top_p,
+fs_sample_args base_args(const torch::Tensor& logits, const Source& src, int64_t top_k, double top_p,
                          int64_t splits) {
   fs_sample_args a = {};
-  a.logits = logits.data_ptr();
+  a.logits = src.ptr;
   a.dtype = logits.scalar_type() == at::kBFloat16 ? FS_BF16 : FS_F16;
   a.batch = logits.size(0);
   a.vocab = logits.size(1);
@@ -88,10 +133,10 @@ int64_t clamp_k(const torch::Tensor& logits, int64_t top_k) { return std::min(to
 
 // Device workspace for the streaming path, from torch's caching allocator (stream-ordered, so it
 // may be released as soon as the launches are enqueued). Empty when the plan needs none.
-torch::Tensor attach_workspace(fs_sample_args* a, const torch::Tensor& like) {
+torch::Tensor attach_workspace(fs_sample_args* a, c10::Device device) {
   const uint64_t bytes = fs_workspace_size(a);
   if (bytes == 0) return torch::Tensor();
-  auto ws = torch::empty({static_cast<int64_t>(bytes)}, like.options().dtype(torch::kUInt8));
+  auto ws = torch::empty({static_cast<int64_t>(bytes)}, torch::TensorOptions().device(device).dtype(torch::kUInt8));
   a->workspace = ws.data_ptr();
   a->workspace_bytes = bytes;
   return ws;
@@ -101,54 +146,61 @@ torch::Tensor empty_i64(const torch::Tensor& like, at::IntArrayRef shape) {
   return torch::empty(shape, like.options().dtype(torch::kInt64));
 }
 
+torch::Tensor empty_out(const Source& src, at::IntArrayRef shape, at::ScalarType dt) {
+  return torch::empty(shape, src.opts.dtype(dt));
+}
+
 }  // namespace
 
 torch::Tensor sample_fused(torch::Tensor logits, int64_t top_k, double top_p, int64_t seed,
                            int64_t offset, int64_t splits_override) {
   check_top_p(top_p);
-  check_logits(logits);
+  const Source src = check_logits(logits, true);
   check_top_k(top_k);
-  c10::cuda::CUDAGuard guard(logits.device());
-  auto out = empty_i64(logits, {logits.size(0)});
-  fs_sample_args a = base_args(logits, top_k, top_p, splits_override);
+  c10::cuda::CUDAGuard guard(src.device);
+  auto out = empty_out(src, {logits.size(0)}, torch::kInt64);
+  fs_sample_args a = base_args(logits, src, top_k, top_p, splits_override);
   set_rng(&a.rng, seed, offset);
   a.out_ids = out.data_ptr<int64_t>();
-  auto ws = attach_workspace(&a, logits);
+  auto ws = attach_workspace(&a, src.device);
   check(fs_sample(&a, current_stream()), "fs_sample");
+  hold_host(src, {&logits, &out});
   return out;
 }
 
 torch::Tensor topk_fused(torch::Tensor logits, int64_t top_k, int64_t splits_override) {
-  check_logits(logits);
+  const Source src = check_logits(logits, true);
   check_top_k(top_k);
-  c10::cuda::CUDAGuard guard(logits.device());
+  c10::cuda::CUDAGuard guard(src.device);
   const int64_t K = clamp_k(logits, top_k);
-  auto ids = empty_i64(logits, {logits.size(0), K});
-  fs_sample_args a = base_args(logits, top_k, 1.0, splits_override);
+  auto ids = empty_out(src, {logits.size(0), K}, torch::kInt64);
+  fs_sample_args a = base_args(logits, src, top_k, 1.0, splits_override);
   a.topk_ids = ids.data_ptr<int64_t>();
-  auto ws = attach_workspace(&a, logits);
+  auto ws = attach_workspace(&a, src.device);
   check(fs_topk(&a, current_stream()), "fs_topk");
+  hold_host(src, {&logits, &ids});
   return ids;
 }
 
 std::vector<torch::Tensor> stages_fused(torch::Tensor logits, int64_t top_k, double top_p,
                                         int64_t seed, int64_t offset, int64_t splits_override) {
   check_top_p(top_p);
-  check_logits(logits);
+  const Source src = check_logits(logits, true);
   check_top_k(top_k);
-  c10::cuda::CUDAGuard guard(logits.device());
+  c10::cuda::CUDAGuard guard(src.device);
   const int64_t B = logits.size(0), K = clamp_k(logits, top_k);
-  auto out = empty_i64(logits, {B});
-  auto keep = torch::empty({B, K}, logits.options().dtype(torch::kBool));
-  auto renormed = torch::empty({B, K}, logits.options().dtype(torch::kFloat32));
-  fs_sample_args a = base_args(logits, top_k, top_p, splits_override);
+  auto out = empty_out(src, {B}, torch::kInt64);
+  auto keep = empty_out(src, {B, K}, torch::kBool);
+  auto renormed = empty_out(src, {B, K}, torch::kFloat32);
+  fs_sample_args a = base_args(logits, src, top_k, top_p, splits_override);
   a.rng.seed = static_cast<uint64_t>(seed);
   a.rng.offset = static_cast<uint64_t>(offset);
   a.out_ids = out.data_ptr<int64_t>();
   a.keep = reinterpret_cast<uint8_t*>(keep.data_ptr<bool>());
   a.renormed = renormed.data_ptr<float>();
-  auto ws = attach_workspace(&a, logits);
+  auto ws = attach_workspace(&a, src.device);
   check(fs_sample(&a, current_stream()), "fs_sample");
+  hold_host(src, {&logits, &out, &keep, &renormed});
   return {out, keep, renormed};
 }
 
@@ -156,11 +208,11 @@ torch::Tensor probe_phase(torch::Tensor logits, int64_t top_k, double top_p, int
                           int64_t splits_override) {
   TORCH_CHECK(phase >= 1 && phase <= FS_NUM_PHASES, "phase must be in [1, ", FS_NUM_PHASES, "]");
   check_top_p(top_p);
-  check_logits(logits);
+  const Source src = check_logits(logits);
   check_top_k(top_k);
   c10::cuda::CUDAGuard guard(logits.device());
   auto out = empty_i64(logits, {logits.size(0)});
-  fs_sample_args a = base_args(logits, top_k, top_p, splits_override);
+  fs_sample_args a = base_args(logits, src, top_k, top_p, splits_override);
   a.out_ids = out.data_ptr<int64_t>();
   a.stop_phase = static_cast<int32_t>(phase);
   check(fs_probe_phase(&a, current_stream()), "fs_probe_phase");
@@ -216,29 +268,29 @@ torch::Tensor probe_scan_split(torch::Tensor logits, int64_t splits) {
 
 namespace {
 
-void fill_rows(fs_sample_args* a, const torch::Tensor& logits,
+void fill_rows(fs_sample_args* a, c10::Device device,
                const std::optional<torch::Tensor>& top_k_rows,
                const std::optional<torch::Tensor>& top_p_rows,
                const std::optional<torch::Tensor>& uniforms, int64_t B) {
   if (top_k_rows.has_value()) {
     const auto& t = *top_k_rows;
-    TORCH_CHECK(t.is_cuda() && t.device() == logits.device() && t.scalar_type() == at::kInt &&
+    TORCH_CHECK(t.is_cuda() && t.device() == device && t.scalar_type() == at::kInt &&
                     t.dim() == 1 && t.size(0) == B && t.is_contiguous(),
-                "top_k_rows must be a contiguous int32 [B] tensor on the logits' device");
+                "top_k_rows must be a contiguous int32 [B] tensor on the device the call runs on");
     a->top_k_rows = t.data_ptr<int32_t>();
   }
   if (top_p_rows.has_value()) {
     const auto& t = *top_p_rows;
-    TORCH_CHECK(t.is_cuda() && t.device() == logits.device() && t.scalar_type() == at::kFloat &&
+    TORCH_CHECK(t.is_cuda() && t.device() == device && t.scalar_type() == at::kFloat &&
                     t.dim() == 1 && t.size(0) == B && t.is_contiguous(),
-                "top_p_rows must be a contiguous float32 [B] tensor on the logits' device");
+                "top_p_rows must be a contiguous float32 [B] tensor on the device the call runs on");
     a->top_p_rows = t.data_ptr<float>();
   }
   if (uniforms.has_value()) {
     const auto& t = *uniforms;
-    TORCH_CHECK(t.is_cuda() && t.device() == logits.device() && t.scalar_type() == at::kFloat &&
+    TORCH_CHECK(t.is_cuda() && t.device() == device && t.scalar_type() == at::kFloat &&
                     t.dim() == 1 && t.size(0) == B && t.is_contiguous(),
-                "uniforms must be a contiguous float32 [B] tensor on the logits' device");
+                "uniforms must be a contiguous float32 [B] tensor on the device the call runs on");
     a->rng.uniforms = t.data_ptr<float>();
   }
 }
@@ -253,33 +305,34 @@ std::vector<std::optional<torch::Tensor>> sample_ex(
     std::optional<torch::Tensor> top_p_rows, std::optional<torch::Tensor> uniforms, int64_t seed,
     int64_t offset, int64_t splits, int64_t id_base, int64_t row_base, bool return_stages, int64_t path,
     double temperature) {
-  check_logits(logits);
+  const Source src = check_logits(logits, true);
   check_top_k(top_k);
   if (!top_p_rows.has_value()) check_top_p(top_p);
-  c10::cuda::CUDAGuard guard(logits.device());
+  c10::cuda::CUDAGuard guard(src.device);
   const int64_t B = logits.size(0), K = clamp_k(logits, top_k);
-  auto out = empty_i64(logits, {B});
-  auto status = torch::empty({B}, logits.options().dtype(torch::kInt32));
-  fs_sample_args a = base_args(logits, top_k, top_p_rows.has_value() ? 1.0 : top_p, splits);
+  auto out = empty_out(src, {B}, torch::kInt64);
+  auto status = empty_out(src, {B}, torch::kInt32);
+  fs_sample_args a = base_args(logits, src, top_k, top_p_rows.has_value() ? 1.0 : top_p, splits);
   a.id_base = id_base;
-  fill_rows(&a, logits, top_k_rows, top_p_rows, uniforms, B);
+  fill_rows(&a, src.device, top_k_rows, top_p_rows, uniforms, B);
   if (!uniforms.has_value()) set_rng(&a.rng, seed, offset);
   a.rng.row_base = row_base;
   a.out_ids = out.data_ptr<int64_t>();
   a.row_status = status.data_ptr<int32_t>();
   std::optional<torch::Tensor> ids, keep, ren;
   if (return_stages) {
-    ids = empty_i64(logits, {B, K});
-    keep = torch::empty({B, K}, logits.options().dtype(torch::kBool));
-    ren = torch::empty({B, K}, logits.options().dtype(torch::kFloat32));
+    ids = empty_out(src, {B, K}, torch::kInt64);
+    keep = empty_out(src, {B, K}, torch::kBool);
+    ren = empty_out(src, {B, K}, torch::kFloat32);
     a.topk_ids = ids->data_ptr<int64_t>();
     a.keep = reinterpret_cast<uint8_t*>(keep->data_ptr<bool>());
     a.renormed = ren->data_ptr<float>();
   }
   a.path = static_cast<int32_t>(path);
   a.temperature = static_cast<float>(temperature);
-  auto ws = attach_workspace(&a, logits);
+  auto ws = attach_workspace(&a, src.device);
   check(fs_sample(&a, current_stream()), "fs_sample");
+  hold_host(src, {&logits, &out, &status, ids ? &*ids : nullptr, keep ? &*keep : nullptr, ren ? &*ren : nullptr});
   return {out, ids, keep, ren, status};
 }
 
@@ -288,7 +341,7 @@ std::vector<std::optional<torch::Tensor>> sample_ex(
 // [parts, B, top_k + 1] block) that receives the candidates.
 torch::Tensor shard_candidates(torch::Tensor logits, int64_t top_k, int64_t id_base, int64_t splits,
                                std::optional<torch::Tensor> out) {
-  check_logits(logits);
+  const Source src = check_logits(logits);
   check_top_k(top_k);
   c10::cuda::CUDAGuard guard(logits.device());
   const int64_t B = logits.size(0);
@@ -302,9 +355,9 @@ torch::Tensor shard_candidates(torch::Tensor logits, int64_t top_k, int64_t id_b
   } else {
     cand = empty_i64(logits, {B, top_k + 1});
   }
-  fs_sample_args a = base_args(logits, top_k, 1.0, splits);
+  fs_sample_args a = base_args(logits, src, top_k, 1.0, splits);
   a.id_base = id_base;
-  auto ws = attach_workspace(&a, logits);
+  auto ws = attach_workspace(&a, logits.device());
   check(fs_shard_candidates(&a, reinterpret_cast<uint64_t*>(cand.data_ptr<int64_t>()), current_stream()),
         "fs_shard_candidates");
   return cand;
@@ -332,7 +385,7 @@ std::vector<torch::Tensor> merge_sample(torch::Tensor cand, bool bf16, int64_t t
   a.batch = B;
   a.top_k = top_k;
   a.top_p = top_p_rows.has_value() ? 1.0f : narrow_top_p(top_p);
-  fill_rows(&a, cand, top_k_rows, top_p_rows, uniforms, B);
+  fill_rows(&a, cand.device(), top_k_rows, top_p_rows, uniforms, B);
   if (!uniforms.has_value()) set_rng(&a.rng, seed, offset);
   a.rng.row_base = row_base;
   a.out_ids = out.data_ptr<int64_t>();
@@ -377,7 +430,7 @@ std::vector<torch::Tensor> tp_merge(torch::Tensor local_cand, bool bf16, int64_t
   a.batch = B;
   a.top_k = top_k;
   a.top_p = narrow_top_p(top_p);
-  fill_rows(&a, local_cand, std::nullopt, std::nullopt, uniforms, B);
+  fill_rows(&a, local_cand.device(), std::nullopt, std::nullopt, uniforms, B);
   if (!uniforms.has_value()) set_rng(&a.rng, seed, offset);
   a.rng.row_base = row_base;
   a.out_ids = out.data_ptr<int64_t>();

@@ -7,6 +7,12 @@ stream, ``splits`` overrides the number of CTAs per row (0 = the measured plan).
 
 ``sample`` is the general serving-engine form: per-row ``top_k`` / ``top_p`` tensors,
 caller-supplied uniforms, stage outputs and per-row input status.
+
+Every entry point also takes logits in pinned host memory (``tensor.pin_memory()``): the current
+CUDA device's kernels read them in place over PCIe (no copy-engine transfer, no staging buffer)
+and write the results into pinned host tensors, which hold their values once the current stream
+has reached the call (``torch.cuda.current_stream().synchronize()``), as after a non_blocking
+copy to the host.
 """
 
 from __future__ import annotations
@@ -76,24 +82,29 @@ def sample(
     (fp32 division by T > 0 keeps their order). 1 (or 0) means none.
     """
     k_rows = p_rows = None
+    # per-row tensors live on the device the call runs on (logits in pinned host memory are read
+    # in place by the current CUDA device)
+    dev = logits.device if logits.is_cuda else torch.device("cuda", torch.cuda.current_device())
     if isinstance(top_k, torch.Tensor):
-        k_rows = top_k.to(device=logits.device, dtype=torch.int32).contiguous()
+        k_rows = top_k.to(device=dev, dtype=torch.int32).contiguous()
         k_bound = int(k_rows.max().item()) if k_rows.numel() else 1
         k_bound = max(1, k_bound)
     else:
         k_bound = int(top_k)
     if isinstance(top_p, torch.Tensor):
-        p_rows = top_p.to(device=logits.device, dtype=torch.float32).contiguous()
+        p_rows = top_p.to(device=dev, dtype=torch.float32).contiguous()
         p_scalar = 1.0
     else:
         p_scalar = float(top_p)
     off = -1 if offset is None else int(offset)
     if uniforms is not None:
-        uniforms = uniforms.to(device=logits.device, dtype=torch.float32).contiguous()
+        uniforms = uniforms.to(device=dev, dtype=torch.float32).contiguous()
     ids, tk, keep, ren, status = ops().sample_ex(
         logits, k_bound, p_scalar, k_rows, p_rows, uniforms, int(seed), off, int(splits), int(id_base),
         int(row_base), bool(return_stages), 0, float(temperature))
     if check_inputs:
+        if not status.is_cuda:
+            torch.cuda.current_stream(dev).synchronize()  # host outputs are written by the launch
         bad = status[status != ROW_OK]
         if bad.numel():
             code = int(bad.min().item())
