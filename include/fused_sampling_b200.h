@@ -98,6 +98,14 @@ typedef struct fs_sample_args {
   float temperature;         /* softmax temperature T > 0; 0 or 1 = none (see below)     */
 } fs_sample_args;
 
+/* Pointers marked "device" above may be any address the kernels can dereference on the current
+ * device: device memory, or pinned host memory mapped into the device's address space (memory
+ * from cudaHostAlloc / cudaMallocHost under unified addressing; pass the address that
+ * cudaPointerGetAttributes reports as devicePointer). Logits in pinned host memory are then read
+ * in place over PCIe and the outputs written there, with no copy-engine transfer; the caller keeps
+ * those buffers alive and unmodified until the stream has passed the call. The workspace, the
+ * per-row k / p / uniform arrays and the generator pointers stay in device memory. */
+
 /* Temperature. The selected candidates' logits are divided by T in IEEE fp32 before the softmax,
  * which is what sampling fp32 logits / T gives (the convention of a temperature warper applied to
  * fp32 logits ahead of the top-k / top-p warpers). The selection itself is unchanged: fp32
