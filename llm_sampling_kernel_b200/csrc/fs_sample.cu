@@ -1289,16 +1289,23 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   const uint32_t mine_lo = mine_hi >= bot + share - 1u ? mine_hi - share + 1u : bot;
   const int nvec = static_cast<uint32_t>(t) * share < span ? static_cast<int>((mine_hi - mine_lo + 1u) / 4u) : 0;
   const uint4* h4 = reinterpret_cast<const uint4*>(hist + static_cast<size_t>(b) * kKeys + mine_lo);
+  // (the vectors of a batch are visited by a rolled loop, each picked out of the registers by
+  // predicated selects: fn is instantiated 4 times per pass, not 32, which keeps the passes in
+  // the instruction cache)
   auto each_key = [&](auto&& fn) {
 #pragma unroll 1
     for (int v0 = nvec - 1; v0 >= 0; v0 -= 8) {
       uint4 w[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) w[i] = v0 - i >= 0 ? h4[v0 - i] : make_uint4(0u, 0u, 0u, 0u);
+      const int nb = min(8, v0 + 1);
+#pragma unroll 1
+      for (int i = 0; i < nb; ++i) {
+        uint4 x = w[0];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (v0 - i < 0) return;
-        const uint32_t cnt[4] = {w[i].w, w[i].z, w[i].y, w[i].x};
+        for (int c = 1; c < 8; ++c)
+          if (i == c) x = w[c];
+        const uint32_t cnt[4] = {x.w, x.z, x.y, x.x};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const uint32_t key = mine_lo + 4u * static_cast<uint32_t>(v0 - i) + 3u - static_cast<uint32_t>(j);
@@ -1563,9 +1570,9 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 //     as packed candidates to cand[b][s][0..n) with n | flags << 24 in cnt[b][s]. A slice whose
 //     survivors would not fit its M slots writes its exact top-kk instead. The union over the
 //     slices holds the row's top-kk.
-//   fs_rowmerge_kernel: one CTA per row. It gathers the slices' candidates (L2-resident), finds
-//     the boundary of the kk-th largest with the anchored histogram, ranks the candidates at or
-//     above it, and runs the same tail as the cluster kernel.
+//   fs_rowmerge_kernel: four warps per row. They gather the slices' candidates (L2-resident),
+//     keep those at or above a row bound from the slices' threshold ladders, rank them, and run
+//     the same tail as the cluster kernel.
 // ------------------------------------------------------------------------------------------
 
 constexpr uint32_t kCountMask = 0xFFFFFFu;
@@ -1874,19 +1881,24 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C)) fs_slice_kernel(const Par
   }
 }
 
-// Row merge, one warp per row (blockDim.x / 32 rows per CTA, no block barrier). Per-warp shared
-// memory: a 256-bin histogram and 256 bin cursors, the row's candidate slots (capn), the sorted
-// top kk and the probabilities of the tail.
-constexpr int kMergeWarps = NT / 32;
+// Row merge: kMergeRowWarps warps per row, merge_rows_per_cta rows per CTA; a row's warps meet at
+// the row group's own named barrier, never at a block barrier. Per-row shared memory: a control
+// word (the compaction counter), a 256-bin histogram and 256 bin cursors, the row's candidate
+// slots as copied (capn), the compacted survivors (capn), the sorted top kk and the
+// probabilities of the tail.
+constexpr int kMergeRowWarps = 4;
+constexpr int kMergeRowThreads = 32 * kMergeRowWarps;
 
-__host__ __device__ constexpr size_t merge_warp_bytes(int capn, int K) {
-  return (2048 + static_cast<size_t>(capn) * 8 + static_cast<size_t>(K) * 8 + static_cast<size_t>(K) * 4 + 15) &
+__host__ __device__ constexpr size_t merge_row_bytes(int capn, int K) {
+  return (16 + 2048 + 2 * static_cast<size_t>(capn) * 8 + static_cast<size_t>(K) * 8 +
+          static_cast<size_t>(K) * 4 + 15) &
          ~static_cast<size_t>(15);
 }
 
-// Warps per row-merge CTA that fit the shared memory budget.
-__host__ __device__ constexpr int merge_warps(int capn, int K) {
-  return static_cast<int>(std::min<size_t>(kMergeWarps, (200u * 1024u) / merge_warp_bytes(capn, K)));
+// Rows per row-merge CTA that fit the shared memory budget (at least 1: capn <= kMaxMaxima and
+// K <= 256 need at most 71 KB per row).
+__host__ __device__ constexpr int merge_rows_per_cta(int capn, int K) {
+  return (200u * 1024u) / merge_row_bytes(capn, K) >= 2 ? 2 : 1;
 }
 
 // The need-th largest low word (0xFFFFFFFF - id: the need-th smallest id) among the n gathered
@@ -2028,59 +2040,125 @@ __device__ bool warp_count_rank_top(const uint64_t* g, uint32_t n, uint32_t kk, 
   return true;
 }
 
-// Row merge of the streaming path, one warp per row.
-//  1. The lanes start 16-byte async copies of the row's S * M candidate slots into the warp's
-//     shared memory (one L2 round trip for the whole row); lanes 0..S-1 load their slice's count
-//     word and threshold ladder meanwhile.
-//  2. A row-wide lower bound L* on the kk-th largest: slice s has at least n_j elements at or
-//     above its ladder key l_sj (n_j = ceil(kk/8), ceil(kk/4), ceil(kk/2), kk), so any t with
-//     sum_s max{n_j : l_sj >= t} >= kk has kk elements at or above it. L* is the largest such t
-//     among the ladder keys (32 or 64 of them, one or two per lane); L* >= every slice's own
+// The top kk of the n survivors g[0, n) into dst[0, kk), by one warp: a counting sort on the key
+// (t: room for n more candidates) when the keys span <= 256 values and no bin holds more than
+// 64; else, for at most 192 of them, a rank by comparisons; else two 8-bit radix levels for the
+// kk-th key E, the keys above E and the lowest-id ties at E compacted in place in g, then a rank.
+__device__ __noinline__ void warp_select_top(uint64_t* g, uint32_t n, int kk, uint32_t* hist, uint32_t* cursor,
+                                             uint64_t* t, uint64_t* dst) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t ukk = static_cast<uint32_t>(kk);
+  if (n >= ukk) {
+    if (warp_count_rank_top(g, n, ukk, hist, cursor, t, dst)) return;
+    if (n <= 192u) {
+      warp_rank_top(g, n, ukk, dst);
+      return;
+    }
+  }
+  // the histogram path: high byte, then low byte inside the boundary bin
+#pragma unroll
+  for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0u;
+  __syncwarp();
+  for (uint32_t d = lane; d < n; d += 32) atomicAdd(&hist[packed_key(g[d]) >> 8], 1u);
+  __syncwarp();
+  uint32_t hb = 0u, above = 0u;
+  warp_boundary_256(hist, ukk, &hb, &above);
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0u;
+  __syncwarp();
+  for (uint32_t d = lane; d < n; d += 32) {
+    const uint32_t key = packed_key(g[d]);
+    if ((key >> 8) == hb) atomicAdd(&hist[key & 0xFFu], 1u);
+  }
+  __syncwarp();
+  uint32_t lb = 0u, above2 = 0u;
+  warp_boundary_256(hist, ukk - above, &lb, &above2);
+  const uint32_t E = (hb << 8) | lb;
+  const uint32_t need = ukk - (above + above2);  // ties to take at E
+  const uint32_t eq = hist[lb];
+  // more than 32 surplus ties at E: keep only the `need` lowest ids among them
+  const bool cut = eq > need + 32u;
+  const uint32_t tcut = cut ? warp_tie_cut(g, n, E, need, hist) : 0u;
+  // compact in place (a kept candidate never moves up): keys above E and the kept ties
+  uint32_t nsel = 0u;
+  for (uint32_t d0 = 0; d0 < n; d0 += 32) {
+    const uint32_t d = d0 + lane;
+    const uint64_t x = d < n ? g[d] : 0ull;
+    const uint32_t key = packed_key(x);
+    const bool take = d < n && (key > E || (key == E && (!cut || static_cast<uint32_t>(x) >= tcut)));
+    const unsigned ball = __ballot_sync(0xFFFFFFFFu, take);
+    if (take) g[nsel + __popc(ball & ((1u << lane) - 1u))] = x;
+    nsel += __popc(ball);
+  }
+  __syncwarp();
+  // rank sort (packed values are distinct; nsel <= kk + 32): the top kk in order
+  warp_rank_top(g, nsel, ukk, dst);
+}
+
+// Row merge of the streaming path, kMergeRowWarps warps per row.
+//  1. The row's threads start 16-byte async copies of the row's S * M candidate slots into shared
+//     memory (one L2 round trip for the whole row); every warp loads the slices' count words and
+//     threshold ladders meanwhile (lanes 0..S-1).
+//  2. A row-wide lower bound L* on the kk-th largest, computed by every warp from the same words:
+//     slice s has at least n_j elements at or above its ladder key l_sj (n_j = ceil(kk/8),
+//     ceil(kk/4), ceil(kk/2), kk), so any t with sum_s max{n_j : l_sj >= t} >= kk has kk elements
+//     at or above it. L* is the largest such t among the ladder keys; L* >= every slice's own
 //     bound l_s3, so every element of the row's top kk is in the lists and >= L*.
-//  3. The listed candidates >= L* are compacted in place (ballots), usually a few dozen.
-//  4. Up to 192 of them are ranked directly; more take the histogram path (two 8-bit radix
-//     levels, tie cut, compaction) first. Then the tail shared with the cluster kernel.
+//  3. Warp w compacts the listed candidates >= L* of slices w, w + 4, ... into the survivor array
+//     (usually a few dozen in all), reserving slots with one shared atomic per ballot step.
+//  4. With kk <= n <= 256 survivors every thread ranks its survivors against all of them (packed
+//     values are distinct, so the order the warps wrote them in does not matter); otherwise warp 0
+//     selects (warp_select_top). Then warp 0 runs the tail shared with the cluster kernel.
+// Every branch before the last barrier depends only on values all the row's warps computed
+// alike, so they all take the same barriers.
 template <int DT>
 __global__ void __launch_bounds__(NT) fs_rowmerge_kernel(const Params p, const uint64_t* __restrict__ cand,
                                                          const uint64_t* __restrict__ lad,
                                                          const uint32_t* __restrict__ cnt, int S, int B) {
   const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int b = blockIdx.x * static_cast<int>(blockDim.x >> 5) + warp;
+  const int rg = static_cast<int>(threadIdx.x) / kMergeRowThreads;  // row group in the CTA
+  const int rt = static_cast<int>(threadIdx.x) - rg * kMergeRowThreads;  // thread in the row group
+  const int w = rt >> 5;                                                 // warp in the row group
+  const int rows = static_cast<int>(blockDim.x) / kMergeRowThreads;
+  const int b = static_cast<int>(blockIdx.x) * rows + rg;
   // the slices' lists are complete only when the slice grid is: wait for it, then let the next
   // kernel of the stream start launching
   grid_dependency_wait();
   grid_launch_dependents();
-  if (b >= B) return;  // whole warp
+  if (b >= B) return;  // the whole row group
+  const uint32_t bar = 1u + static_cast<uint32_t>(rg);  // barrier 0 is the block's
+  auto row_sync = [bar]() { asm volatile("bar.sync %0, %1;\n" ::"r"(bar), "r"(kMergeRowThreads) : "memory"); };
   const uint32_t M = static_cast<uint32_t>(p.slot);
   const int capn = p.cap;
-  unsigned char* base = g_smem + merge_warp_bytes(capn, p.K) * warp;
-  uint32_t* hist = reinterpret_cast<uint32_t*>(base);
+  unsigned char* base = g_smem + merge_row_bytes(capn, p.K) * rg;
+  uint32_t* ctl = reinterpret_cast<uint32_t*>(base);
+  uint32_t* hist = ctl + 4;
   uint32_t* cursor = hist + 256;
   uint64_t* g = reinterpret_cast<uint64_t*>(cursor + 256);
-  uint64_t* dst = g + capn;
+  uint64_t* sv = g + capn;  // survivors
+  uint64_t* dst = sv + capn;
   float* prob = reinterpret_cast<float*>(dst + p.K);
 
-  // 1. the row's S * M slots -> g (capn >= S * M), 16-byte async copies spread over the lanes
+  // 1. the row's S * M slots -> g (capn >= S * M), 16-byte async copies spread over the row group
   const size_t row0 = static_cast<size_t>(b) * S;
   {
     const uint4* src = reinterpret_cast<const uint4*>(cand + row0 * M);
     uint4* g4 = reinterpret_cast<uint4*>(g);
     const uint32_t pairs = static_cast<uint32_t>(S) * M / 2u;
-    for (uint32_t q = lane; q < pairs; q += 32u) cp_async_16(g4 + q, src + q);
+    for (uint32_t q = static_cast<uint32_t>(rt); q < pairs; q += kMergeRowThreads) cp_async_16(g4 + q, src + q);
   }
-  const uint32_t w = lane < S ? __ldcg(cnt + row0 + lane) : 0u;
+  const uint32_t wv = lane < S ? __ldcg(cnt + row0 + lane) : 0u;
   const uint64_t lw = lane < S ? __ldcg(lad + row0 + lane) : 0ull;
 
   int kk;
   float pp;
   bool bad;
   row_params(p, b, &kk, &pp, &bad);
-  const float u = row_uniform(p, b);
-  const uint32_t c = min(w & kCountMask, M);  // (never above M; the clamp keeps reads in range)
-  const uint32_t f = __reduce_or_sync(0xFFFFFFFFu, w >> 24);
+  const uint32_t c = min(wv & kCountMask, M);  // (never above M; the clamp keeps reads in range)
+  const uint32_t f = __reduce_or_sync(0xFFFFFFFFu, wv >> 24);
 
-  // 2. L* from the ladders
+  // 2. L* from the ladders (every warp)
   const uint32_t ukk = static_cast<uint32_t>(kk);
   const uint32_t n0 = (ukk + 7u) / 8u, n1 = (ukk + 3u) / 4u, n2 = (ukk + 1u) / 2u;
   uint32_t lstar = 0u;
@@ -2103,25 +2181,25 @@ __global__ void __launch_bounds__(NT) fs_rowmerge_kernel(const Params p, const u
   }
   lstar = __reduce_max_sync(0xFFFFFFFFu, lstar);
 
-  // the copies land before anything else touches g, or the warp leaves
+  if (rt == 0) ctl[0] = 0u;
+  // the copies land (each thread waits for its own, the barrier publishes them) before anything
+  // reads g, and the counter is zeroed before anything adds to it
   cp_async_wait_all();
-  __syncwarp();
+  row_sync();
   int st = FS_ROW_OK;
   if (bad) st = FS_ROW_BAD_PARAM;
   else if (f & kFlagNaN) st = FS_ROW_NAN;
   else if (f & kFlagPosInf) st = FS_ROW_POSINF;
   else if (!(f & kFlagAboveNegInf)) st = FS_ROW_ALL_NEGINF;
   if (st != FS_ROW_OK) {
-    write_invalid_row(p, b, st, lane, 32);
-    return;
+    if (w == 0) write_invalid_row(p, b, st, lane, 32);
+    return;  // every warp of the row (st is the same for all)
   }
 
-  // 3. keep the listed candidates >= L*, compacted in place to g[0, n): a step writes below
-  // n + 64 <= the first slot it reads, and every lane has read before any lane writes
-  uint32_t n = 0u;
+  // 3. survivors >= L*: warp w takes slices w, w + kMergeRowWarps, ...
   const ulonglong2* g2 = reinterpret_cast<const ulonglong2*>(g);
   const unsigned lt = (1u << lane) - 1u;
-  for (int r = 0; r < S; ++r) {
+  for (int r = w; r < S; r += kMergeRowWarps) {
     const uint32_t cr = __shfl_sync(0xFFFFFFFFu, c, r);
     for (uint32_t j0 = 0; j0 < cr; j0 += 64u) {
       const uint32_t j = j0 + 2u * lane;
@@ -2130,70 +2208,40 @@ __global__ void __launch_bounds__(NT) fs_rowmerge_kernel(const Params p, const u
       const bool k0 = j < cr && packed_key(x.x) >= lstar;
       const bool k1 = j + 1u < cr && packed_key(x.y) >= lstar;
       const unsigned b0 = __ballot_sync(0xFFFFFFFFu, k0), b1 = __ballot_sync(0xFFFFFFFFu, k1);
-      if (k0) g[n + __popc(b0 & lt)] = x.x;
-      if (k1) g[n + __popc(b0) + __popc(b1 & lt)] = x.y;
-      n += __popc(b0) + __popc(b1);
+      const uint32_t nb = static_cast<uint32_t>(__popc(b0) + __popc(b1));
+      uint32_t at = 0u;
+      if (lane == 0 && nb != 0u) at = atomicAdd(&ctl[0], nb);
+      at = __shfl_sync(0xFFFFFFFFu, at, 0);
+      if (k0) sv[at + __popc(b0 & lt)] = x.x;
+      if (k1) sv[at + __popc(b0) + __popc(b1 & lt)] = x.y;
     }
   }
-  __syncwarp();
+  row_sync();
+  const uint32_t n = ctl[0];
 
-  // 4. the survivors' top kk: a counting sort on the key (room for a second copy after g[0..n)),
-  // else, for at most 192 of them, a rank by comparisons
-  bool ranked = false;
-  if (n >= ukk) {
-    if (2u * n <= static_cast<uint32_t>(capn)) ranked = warp_count_rank_top(g, n, ukk, hist, cursor, g + n, dst);
-    if (!ranked && n <= 192u) {
-      warp_rank_top(g, n, ukk, dst);
-      ranked = true;
+  // 4. the survivors' top kk
+  if (n >= ukk && n <= 2u * kMergeRowThreads) {
+    const ulonglong2* s2 = reinterpret_cast<const ulonglong2*>(sv);
+    const uint32_t np = n >> 1;
+    for (uint32_t i = static_cast<uint32_t>(rt); i < n; i += kMergeRowThreads) {
+      const uint64_t x = sv[i];
+      uint32_t r = 0u;
+#pragma unroll 4
+      for (uint32_t j = 0; j < np; ++j) {
+        const ulonglong2 y = s2[j];
+        r += (y.x > x ? 1u : 0u) + (y.y > x ? 1u : 0u);
+      }
+      if (n & 1u) r += sv[n - 1u] > x ? 1u : 0u;
+      if (r < ukk) dst[r] = x;
     }
-  }
-  if (ranked) {
-    if (write_selection(p, b, dst, kk, lane, 32)) return;
-    if (kk <= 32) sample_tail_warp<DT, 1>(p, b, dst, kk, pp, u, prob);
-    else if (kk <= 64) sample_tail_warp<DT, 2>(p, b, dst, kk, pp, u, prob);
-    else sample_tail_warp<DT, 8>(p, b, dst, kk, pp, u, prob);
-    return;
-  }
-  // otherwise the histogram path: high byte, then low byte inside the boundary bin
-#pragma unroll
-  for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0u;
-  __syncwarp();
-  for (uint32_t d = lane; d < n; d += 32) atomicAdd(&hist[packed_key(g[d]) >> 8], 1u);
-  __syncwarp();
-  uint32_t hb = 0u, above = 0u;
-  warp_boundary_256(hist, static_cast<uint32_t>(kk), &hb, &above);
-  __syncwarp();
-#pragma unroll
-  for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0u;
-  __syncwarp();
-  // low byte inside the boundary bin
-  for (uint32_t d = lane; d < n; d += 32) {
-    const uint32_t key = packed_key(g[d]);
-    if ((key >> 8) == hb) atomicAdd(&hist[key & 0xFFu], 1u);
+    row_sync();
+    if (w != 0) return;
+  } else {
+    if (w != 0) return;
+    warp_select_top(sv, n, kk, hist, cursor, g, dst);  // g is free: room for n candidates
   }
   __syncwarp();
-  uint32_t lb = 0u, above2 = 0u;
-  warp_boundary_256(hist, static_cast<uint32_t>(kk) - above, &lb, &above2);
-  const uint32_t E = (hb << 8) | lb;
-  const uint32_t need = static_cast<uint32_t>(kk) - (above + above2);  // ties to take at E
-  const uint32_t eq = hist[lb];
-  // more than 32 surplus ties at E: keep only the `need` lowest ids among them
-  const bool cut = eq > need + 32u;
-  const uint32_t tcut = cut ? warp_tie_cut(g, n, E, need, hist) : 0u;
-  // compact in place (a kept candidate never moves up): keys above E and the kept ties
-  uint32_t nsel = 0u;
-  for (uint32_t d0 = 0; d0 < n; d0 += 32) {
-    const uint32_t d = d0 + lane;
-    const uint64_t x = d < n ? g[d] : 0ull;
-    const uint32_t key = packed_key(x);
-    const bool take = d < n && (key > E || (key == E && (!cut || static_cast<uint32_t>(x) >= tcut)));
-    const unsigned ball = __ballot_sync(0xFFFFFFFFu, take);
-    if (take) g[nsel + __popc(ball & ((1u << lane) - 1u))] = x;
-    nsel += __popc(ball);
-  }
-  __syncwarp();
-  // rank sort (packed values are distinct; nsel <= kk + 32): the top kk in order
-  warp_rank_top(g, nsel, static_cast<uint32_t>(kk), dst);
+  const float u = row_uniform(p, b);
   if (write_selection(p, b, dst, kk, lane, 32)) return;
   if (kk <= 32) sample_tail_warp<DT, 1>(p, b, dst, kk, pp, u, prob);
   else if (kk <= 64) sample_tail_warp<DT, 2>(p, b, dst, kk, pp, u, prob);
@@ -2593,8 +2641,8 @@ static fs_status make_plan_uncached(int64_t B, int64_t V, int64_t K, int32_t spl
     out->slot = M;
     out->smem = static_cast<int>(sizeof(Shared)) + kSliceStageBytes;
     out->merge_cap = std::max(256, pow2_ceil(static_cast<int64_t>(S) * M));
-    out->merge_smem = static_cast<int>(merge_warps(out->merge_cap, static_cast<int>(K)) *
-                                       merge_warp_bytes(out->merge_cap, static_cast<int>(K)));
+    out->merge_smem = static_cast<int>(merge_rows_per_cta(out->merge_cap, static_cast<int>(K)) *
+                                       merge_row_bytes(out->merge_cap, static_cast<int>(K)));
     // candidates [B][S][M], ladders [B][S], count words [B][S]
     out->workspace = static_cast<uint64_t>(B) * S * M * sizeof(uint64_t) + static_cast<uint64_t>(B) * S * 8 +
                      static_cast<uint64_t>(B) * S * 4 + 256;
@@ -2911,11 +2959,11 @@ static fs_status launch_stream(const fs_sample_args* a, const PlanOut& plan, con
   if (st != FS_OK) return st;
   Params mp = prm;
   mp.cap = plan.merge_cap;
-  const int mw = merge_warps(plan.merge_cap, static_cast<int>(prm.K));
-  const unsigned mgrid = static_cast<unsigned>((a->batch + mw - 1) / mw);
+  const int mr = merge_rows_per_cta(plan.merge_cap, static_cast<int>(prm.K));
+  const unsigned mgrid = static_cast<unsigned>((a->batch + mr - 1) / mr);
   cudaLaunchConfig_t mcfg = {};
   mcfg.gridDim = dim3(mgrid, 1, 1);
-  mcfg.blockDim = dim3(32 * mw, 1, 1);
+  mcfg.blockDim = dim3(kMergeRowThreads * mr, 1, 1);
   mcfg.dynamicSmemBytes = plan.merge_smem;
   mcfg.stream = stream;
   mcfg.attrs = pdl;
@@ -3061,7 +3109,7 @@ void append_cluster_attrs(std::vector<fs_kernel_attr>& rows) {
       r.param = 0;
       r.block = NT;
       fill_attr(reinterpret_cast<const void*>(dt ? fs_rowmerge_kernel<1> : fs_rowmerge_kernel<0>), NT,
-                static_cast<int>(kMergeWarps * merge_warp_bytes(1024, 64)), &r);
+                static_cast<int>(merge_rows_per_cta(1024, 64) * merge_row_bytes(1024, 64)), &r);
       rows.push_back(r);
     }
     {
