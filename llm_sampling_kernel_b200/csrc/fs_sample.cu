@@ -136,6 +136,20 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int q) {
 // Programmatic dependent launch (griddepcontrol): no-ops when the grid was launched without the
 // programmatic-serialization attribute.
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
+// Warms L2 with bytes [lo, lo + len) of row b (clipped to the row's 2V bytes), one 128-byte line
+// per thread and step. Called before grid_dependency_wait(): while the previous kernel of the
+// stream finishes, this grid's reads of its own input are already on their way from DRAM. Only
+// prefetches: the loads that use the data still follow the wait, and L2 is where every write of
+// the previous kernel lands, so they see its results.
+__device__ __forceinline__ void prefetch_row_l2(const uint16_t* __restrict__ logits, int64_t row_stride, int vocab,
+                                                int b, int64_t lo, int64_t len, int t, int nthreads) {
+  const char* row = reinterpret_cast<const char*>(logits + static_cast<int64_t>(b) * row_stride);
+  const int64_t end = min(lo + len, static_cast<int64_t>(vocab) * 2);
+  for (int64_t off = (lo & ~static_cast<int64_t>(127)) + static_cast<int64_t>(t) * 128; off < end;
+       off += static_cast<int64_t>(nthreads) * 128)
+    asm volatile("prefetch.global.L2 [%0];\n" ::"l"(row + off));
+}
 __device__ __forceinline__ void grid_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
@@ -862,8 +876,10 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
   cluster_arrive();  // B1 (split): waited for only before the first remote access
 
   // Programmatic dependent launch: this grid may have started while the previous kernel of the
-  // stream was still running; wait for it (and its writes) before reading any input, then let
-  // the next kernel of the stream start its own launch while this one runs.
+  // stream was still running; warm L2 with this CTA's part of the row meanwhile, wait for that
+  // kernel (and its writes) before reading any input, then let the next kernel of the stream
+  // start its own launch while this one runs.
+  prefetch_row_l2(p.logits, p.row_stride, V, b, static_cast<int64_t>(s) * C * NT * 16, C * NT * 16, t, NT);
   grid_dependency_wait();
   grid_launch_dependents();
 
