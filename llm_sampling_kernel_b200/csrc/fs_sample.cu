@@ -2368,9 +2368,13 @@ __device__ void tp_merge_row(const Params& p, const uint64_t* __restrict__ local
     for (int r = 0; r < W; ++r)
       tp.peer_recv[r][((static_cast<size_t>(slot) * W + tp.rank) * tp.max_batch + b) * K1 + i] = x;
   }
-  __threadfence_system();
+  // the CTA's stores are ordered before the flag by the barrier and one system-scope fence in
+  // each flag-raising thread (fences are cumulative), not by a fence in every thread
   __syncthreads();
-  if (t < W) st_release_sys(&tp.peer_flags[t][(static_cast<size_t>(slot) * W + tp.rank) * tp.max_batch + b], epoch);
+  if (t < W) {
+    __threadfence_system();
+    st_release_sys(&tp.peer_flags[t][(static_cast<size_t>(slot) * W + tp.rank) * tp.max_batch + b], epoch);
+  }
   // 2. wait for every rank's row (bounded)
   if (t < 32) {
     bool ok = true;
