@@ -24,6 +24,10 @@ the measured peak (the C3 config, reported in `roofline`).
   benchmarks/reference.py:sample_eager(check_inputs=False) built into oracle/_ref by
   `make -C oracle` (the oracle port of it when that is missing), on all host threads, on a
   bounded sample of C1 calls.
+* `adversarial` (one GPU): µs per call of the four adversarial configurations at B=8,
+  V=151936, FP16 (16 distinct values at k=1024; top-p only at k=V, the wide path; greedy; rows
+  with +-inf and the most negative finite value), cold L2. `lm_head` (one GPU): the LM-head
+  producer against the GEMM alone and GEMM + one sampler call.
 * N > 1 (torchrun, one process per GPU): weak scaling of the anchor (each rank samples its own
   B=1 row; value = max over ranks), plus the B=1024 batch-sharded config (rows split across
   ranks, no collective on the data path) and the vocab-sharded tensor-parallel config (B=32,
@@ -410,6 +414,12 @@ def run_ours(args):
             lm_head = run_lm_head(ops, device, args)
             launches += lm_head.pop("launches")
 
+        # ---- C5 adversarial cases (one GPU) ----
+        adversarial = None
+        if world == 1:
+            adversarial = run_adversarial(ops, device, args)
+            launches += adversarial.pop("launches")
+
         # ---- C4 vocab-sharded tensor parallel (N > 1) ----
         tp = None
         if world > 1:
@@ -479,6 +489,8 @@ def run_ours(args):
         line["tp"] = tp
     if lm_head is not None:
         line["lm_head"] = lm_head
+    if adversarial is not None:
+        line["adversarial"] = adversarial
     if world == 1 and not args.no_cpu:
         cpu_us, threads, n, kind, what = cpu_reference_time(C1["B"], C1["V"], C1["k"], C1["p"],
                                                             budget_s=args.cpu_budget)
@@ -486,6 +498,58 @@ def run_ours(args):
                                 "sample": f"C1 row (B=1, V=151936, k=50, p=0.9) x {n} calls of {what}, "
                                           f"{threads} host threads"}
     print(json.dumps(line), flush=True)
+
+
+def adversarial_buffers(case, n, B, V, device, seed):
+    """C5 inputs, fp16: 1 = logits taking 16 distinct values; 2 = near-flat N(0, 0.1^2);
+    3 = N(0, 2^2) (greedy); 4 = N(0, 2^2) with +-inf and the most negative finite value planted in
+    some rows (a +inf row, a row with -inf entries, a row that is entirely the lowest value)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    if case == 1:
+        levels = torch.linspace(-3.0, 3.0, 16, device=device)
+        x = levels[torch.randint(0, 16, (n * B, V), generator=g, device=device)]
+    elif case == 2:
+        x = torch.randn(n * B, V, generator=g, device=device) * 0.1
+    else:
+        x = torch.randn(n * B, V, generator=g, device=device) * 2.0
+    x = x.to(torch.float16)
+    if case == 4:
+        xv = x.view(n, B, V)
+        xv[:, 0, 7] = float("inf")
+        xv[:, 1, ::3] = float("-inf")
+        xv[:, 2, :] = -65504.0
+        xv[:, 3, 100] = -65504.0
+    return [x[i * B:(i + 1) * B] for i in range(n)]
+
+
+def run_adversarial(ops, device, args):
+    """The four adversarial configurations at B=8, V=151936, FP16: 16 distinct values at k=1024,
+    p=0.99; top-p only (k=V, p=0.5) on N(0, 0.1^2) (the wide path); greedy k=1; rows with +-inf and
+    the most negative finite value (k=1024, p=0.9). Each timed over rotating buffers > 2x L2."""
+    B, V = 8, C1["V"]
+    per = B * V * 2
+    nbuf = max(2, (2 * L2_BYTES) // per + 1)
+    steps = max(3, min(args.steps, 200))
+    warm = max(3, args.warmup)
+    cases = ((1, "case1_16_values_k1024_p099_us", 1024, 0.99), (2, "case2_top_p_only_k_eq_V_p05_us", V, 0.5),
+             (3, "case3_greedy_k1_us", 1, 0.9), (4, "case4_inf_and_lowest_finite_k1024_us", 1024, 0.9))
+    out = {}
+    launches = 0
+    for case, name, k, p in cases:
+        bufs = adversarial_buffers(case, nbuf, B, V, device, seed=40 + case)
+
+        def step(i, bufs=bufs, k=k, p=p):
+            ops.sample_fused(bufs[i % nbuf], k, p, 0x5EED, i, 0)
+
+        out[name] = round(timed_steps(step, steps, warm, 1) * 1000.0 / steps, 3)
+        launches += steps * (4 if ops.plan(B, V, k, 0)[7] == 3 else 1)
+        del bufs
+        torch.cuda.empty_cache()
+    out.update({"B": B, "V": V, "dtype": "fp16", "launches": launches,
+                "l2": f"cold: {nbuf} rotating buffers per case ({nbuf * per / 2**20:.0f} MiB > 2x L2)",
+                "paths": {"case2": "wide (histogram, row, count, pick launches + a histogram memset)",
+                          "others": "cluster (one launch)"}})
+    return out
 
 
 def run_lm_head(ops, device, args):

@@ -709,6 +709,9 @@ __device__ __forceinline__ uint4 load_chunk(const uint16_t* __restrict__ row, in
 // The slice is re-read from global memory (L2) chunk by chunk, so this rare path does not
 // hold the row in registers. Every thread of every CTA of the cluster calls it; it writes kk
 // packed candidates into the leader's buffer and returns kk.
+// exact_select: chunks whose loads one pass issues together (all of them for small C)
+__host__ __device__ constexpr int pass_batch(int C) { return C <= 6 ? C : 4; }
+
 template <int DT, int C>
 __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict__ row, int V, int vec,
                                          uint32_t id_base, int vbase, int kk, uint64_t* lsurv) {
@@ -716,21 +719,33 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
   const int S = static_cast<int>(cluster.num_blocks());
   const int s = static_cast<int>(cluster.block_rank());
   const int t = threadIdx.x;
+  // fn(e0, chunk) for the CTA's slice chunks in id order, re-read from L1/L2 in batches of
+  // pass_batch(C) whose loads are issued together (one round trip per batch, not per chunk)
+  constexpr int PB = pass_batch(C);
+  auto for_chunks = [&](auto&& fn) {
+#pragma unroll 1
+    for (int c0 = 0; c0 < C; c0 += PB) {
+      uint4 vv[PB];
+#pragma unroll
+      for (int i = 0; i < PB; ++i)
+        if (c0 + i < C) vv[i] = load_chunk<DT>(row, (vbase + (c0 + i) * NT + t) * 8, V, vec);
+#pragma unroll
+      for (int i = 0; i < PB; ++i)
+        if (c0 + i < C) fn((vbase + (c0 + i) * NT + t) * 8, vv[i]);
+    }
+  };
 
   // level 1: high byte
   sh.lh[t] = 0u;
   __syncthreads();
-#pragma unroll 1
-  for (int c = 0; c < C; ++c) {
-    const int e0 = (vbase + c * NT + t) * 8;
-    const uint4 v = load_chunk<DT>(row, e0, V, vec);
+  for_chunks([&](int e0, const uint4& v) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const uint32_t w = word_of(v, q);
       hist_add_warp(sh.lh, order_key(w & 0xFFFFu) >> 8, e0 + 2 * q < V);
       hist_add_warp(sh.lh, order_key(w >> 16) >> 8, e0 + 2 * q + 1 < V);
     }
-  }
+  });
   __syncthreads();
   if (sh.lh[t] != 0u) atomicAdd(cluster.map_shared_rank(&sh.fh1[t], 0), sh.lh[t]);
   cluster.sync();  // F1
@@ -749,10 +764,7 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
   const uint32_t n_above = sh.ctl[kCtlAbove];
 
   // level 2: low byte inside bucket hb
-#pragma unroll 1
-  for (int c = 0; c < C; ++c) {
-    const int e0 = (vbase + c * NT + t) * 8;
-    const uint4 v = load_chunk<DT>(row, e0, V, vec);
+  for_chunks([&](int e0, const uint4& v) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const uint32_t w = word_of(v, q);
@@ -760,7 +772,7 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
       hist_add_warp(sh.lh, k0 & 0xFFu, e0 + 2 * q < V && (k0 >> 8) == hb);
       hist_add_warp(sh.lh, k1 & 0xFFu, e0 + 2 * q + 1 < V && (k1 >> 8) == hb);
     }
-  }
+  });
   __syncthreads();
   if (sh.lh[t] != 0u) atomicAdd(cluster.map_shared_rank(&sh.fh2[t], 0), sh.lh[t]);
   cluster.sync();  // F2
@@ -781,10 +793,7 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
 
   // counts of keys > T and == T per thread, then per rank
   uint32_t ngt = 0u, ntie = 0u;
-#pragma unroll 1
-  for (int c = 0; c < C; ++c) {
-    const int e0 = (vbase + c * NT + t) * 8;
-    const uint4 v = load_chunk<DT>(row, e0, V, vec);
+  for_chunks([&](int e0, const uint4& v) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const uint32_t w = word_of(v, q);
@@ -798,7 +807,7 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
         ntie += k1 == T;
       }
     }
-  }
+  });
   uint32_t gt_total, tie_total;
   const uint32_t gt_off = block_incl_scan<uint32_t, NT>(ngt, sh.uscr, &gt_total) - ngt;
   block_incl_scan<uint32_t, NT>(ntie, sh.uscr, &tie_total);
@@ -815,10 +824,7 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
   // keys strictly above T, and the ties at T ranked in id order
   uint32_t slot = gt_base + gt_off;
   uint32_t chunk_base = tie_base;
-#pragma unroll 1
-  for (int c = 0; c < C; ++c) {
-    const int e0 = (vbase + c * NT + t) * 8;
-    const uint4 v = load_chunk<DT>(row, e0, V, vec);
+  for_chunks([&](int e0, const uint4& v) {
     uint32_t mask = 0u;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -844,7 +850,7 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
       ++rank;
     }
     chunk_base += ctot;
-  }
+  });
   return kk;
 }
 
@@ -1051,10 +1057,12 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
   }
 
   // ---- phase 4: survivors (every element >= L) into the leader's buffer ----
-  // The per-chunk maxima mark the chunks holding an element >= L (one packed compare per chunk);
-  // a thread takes its marked chunks out of its registers one at a time, reserves positions for
-  // the chunk's hits with one atomic on the leader's counter and stores them there, so the
-  // leader's survivors are contiguous when the cluster barrier completes.
+  // The per-chunk maxima mark the chunks holding an element >= L (one packed compare per chunk).
+  // Each lane counts the hits of its marked chunks, a warp scan gives every lane its offset, and
+  // one lane per warp reserves the warp's positions with one atomic on the leader's counter (a
+  // row made mostly of ties would otherwise send an atomic per chunk to that one counter); then
+  // each thread takes its marked chunks out of its registers one at a time and stores the hits,
+  // so the leader's survivors are contiguous when the cluster barrier completes.
   const uint32_t lbits = key_to_bits(lkey);
   const uint32_t l2 = lbits | (lbits << 16);
   const uint32_t cap = static_cast<uint32_t>(p.cap);
@@ -1063,23 +1071,41 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
   uint32_t cm = 0u;
 #pragma unroll
   for (int c = 0; c < C; ++c) cm |= (pair_ge_mask<DT>(cp[c], l2) != 0u ? 1u : 0u) << c;
-  while (cm != 0u) {
-    const int c = __ffs(cm) - 1;
-    cm &= cm - 1u;
-    uint4 x = v[0];
-#pragma unroll
-    for (int cc = 1; cc < C; ++cc)
-      if (c == cc) x = v[cc];
-    const int e0 = (vbase + c * NT + t) * 8;
-    uint32_t hits = 0u;  // bit 2w + h: half h of word w of the chunk is >= L
+  // bit 2w + h of chunk_hits(x, e0): half h of word w of the chunk is >= L (past the row end: 0)
+  auto chunk_hits = [&](const uint4& x, int e0) -> uint32_t {
+    uint32_t hits = 0u;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const uint32_t m = pair_ge_mask<DT>(word_of(x, w), l2);
       hits |= ((m & 1u) | ((m >> 15) & 2u)) << (2 * w);
     }
-    if (e0 + 8 > V) hits &= (e0 < V) ? ((1u << (V - e0)) - 1u) : 0u;  // past the row end
-    if (hits == 0u) continue;
-    uint32_t slot = atom_add_dsmem(ctr, static_cast<uint32_t>(__popc(hits)));
+    if (e0 + 8 > V) hits &= (e0 < V) ? ((1u << (V - e0)) - 1u) : 0u;
+    return hits;
+  };
+  // chunk c of this thread's slice, out of the registers (predicated selects, no local memory)
+  auto chunk_at = [&](int c) -> uint4 {
+    uint4 x = v[0];
+#pragma unroll
+    for (int cc = 1; cc < C; ++cc)
+      if (c == cc) x = v[cc];
+    return x;
+  };
+  uint32_t nmine = 0u;
+  for (uint32_t m = cm; m != 0u; m &= m - 1u) {
+    const int c = __ffs(m) - 1;
+    nmine += static_cast<uint32_t>(__popc(chunk_hits(chunk_at(c), (vbase + c * NT + t) * 8)));
+  }
+  const uint32_t lane_incl = warp_incl_scan(nmine);
+  const uint32_t wtot = __shfl_sync(0xFFFFFFFFu, lane_incl, 31);
+  uint32_t wbase = 0u;
+  if ((t & 31) == 31 && wtot != 0u) wbase = atom_add_dsmem(ctr, wtot);
+  uint32_t slot = __shfl_sync(0xFFFFFFFFu, wbase, 31) + lane_incl - nmine;
+  while (cm != 0u) {
+    const int c = __ffs(cm) - 1;
+    cm &= cm - 1u;
+    const uint4 x = chunk_at(c);
+    const int e0 = (vbase + c * NT + t) * 8;
+    uint32_t hits = chunk_hits(x, e0);
     while (hits != 0u) {
       const int bit = __ffs(hits) - 1;
       hits &= hits - 1u;
@@ -1153,6 +1179,7 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
 constexpr int kKeys = 65536;                             // 16-bit order keys
 constexpr int kRowThreads = 1024;                        // fs_wide_row_kernel
 constexpr int kKeysPerThread = kKeys / kRowThreads;      // 64 consecutive keys per thread
+constexpr int kWCacheKeys = 32768;  // fs_wide_row_kernel: per-key weights kept in shared memory
 constexpr float kTwo62f = 4611686018427387904.0f;        // 2^62: fixed-point unit of a probability
 constexpr float kTwoM62f = 2.168404344971008868e-19f;    // 2^-62
 
@@ -1360,12 +1387,23 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   }
 
   // ---- Z over the top-k, in a fixed order ----
+  // The weights expf(x_g - m) are kept in shared memory (indexed by key - bot) when the span fits
+  // kWCacheKeys, so the later passes read them back instead of evaluating them again; each
+  // thread reads back only what it wrote itself (the owner's warp reads the owner's, after the
+  // block barriers of the scans below).
+  float* wc = reinterpret_cast<float*>(g_smem);
+  const bool cache = span <= static_cast<uint32_t>(kWCacheKeys);
   double part = 0.0;
   each_key([&](uint32_t key, uint32_t cnt) {
     const uint32_t n = topk_count(key, cnt, T, need);
-    if (n != 0u) part += static_cast<double>(n) * static_cast<double>(expf(tail_logit<DT>(p, key) - mf));
+    if (n != 0u) {
+      const float w = expf(tail_logit<DT>(p, key) - mf);
+      if (cache) wc[key - bot] = w;
+      part += static_cast<double>(n) * static_cast<double>(w);
+    }
     return false;
   });
+  auto weight = [&](uint32_t key) -> float { return cache ? wc[key - bot] : expf(tail_logit<DT>(p, key) - mf); };
   part = warp_sum(part);
   if (lane == 0) dscr[t >> 5] = part;
   __syncthreads();
@@ -1384,7 +1422,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   each_key([&](uint32_t key, uint32_t cnt) {
     const uint32_t n = topk_count(key, cnt, T, need);
     if (n != 0u) {
-      last_pr = __fdiv_rn(expf(tail_logit<DT>(p, key) - mf), z);
+      last_pr = __fdiv_rn(weight(key), z);
       msum += static_cast<uint64_t>(n) * prob_to_fixed(last_pr);
       has = true;
     }
@@ -1416,7 +1454,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
       const int i = 2 * lane + j;
       const uint32_t key = ohi - static_cast<uint32_t>(i);
       n[j] = i < onk ? topk_count(key, hrow[key], T, need) : 0u;
-      pr[j] = n[j] != 0u ? __fdiv_rn(expf(tail_logit<DT>(p, key) - mf), z) : 0.0f;
+      pr[j] = n[j] != 0u ? __fdiv_rn(weight(key), z) : 0.0f;
       pf[j] = prob_to_fixed(pr[j]);
     }
     const uint64_t m0 = static_cast<uint64_t>(n[0]) * pf[0], m1 = static_cast<uint64_t>(n[1]) * pf[1];
@@ -2777,9 +2815,11 @@ struct WideKernels {
   static fs_status launch(const fs_sample_args* a, const PlanOut& plan, const Params& prm, uint32_t* hist,
                           uint32_t* smax, uint32_t* sflag, uint32_t* cnt, uint32_t* res, cudaStream_t stream) {
     const dim3 grid(plan.splits, static_cast<unsigned>(a->batch), 1);
+    fs_status st = prepare_kernel(reinterpret_cast<KernelFn>(fs_wide_row_kernel<DT>), 1, kWCacheKeys * 4);
+    if (st != FS_OK) return st;
     fs_wide_hist_kernel<DT, C><<<grid, NT, 0, stream>>>(prm, hist, smax, sflag);
-    fs_wide_row_kernel<DT><<<static_cast<unsigned>(a->batch), kRowThreads, 0, stream>>>(prm, hist, smax, sflag, res,
-                                                                                          plan.splits);
+    fs_wide_row_kernel<DT><<<static_cast<unsigned>(a->batch), kRowThreads, kWCacheKeys * 4, stream>>>(
+        prm, hist, smax, sflag, res, plan.splits);
     fs_wide_count_kernel<DT, C><<<grid, NT, 0, stream>>>(prm, res, cnt);
     fs_wide_pick_kernel<DT, C><<<grid, NT, 0, stream>>>(prm, res, cnt);
     return FS_OK;
@@ -3142,7 +3182,8 @@ void append_cluster_attrs(std::vector<fs_kernel_attr>& rows) {
       std::snprintf(r.name, sizeof(r.name), "fs_wide_row_kernel<%s>", dt ? "bf16" : "fp16");
       r.param = 0;
       r.block = kRowThreads;
-      fill_attr(reinterpret_cast<const void*>(dt ? fs_wide_row_kernel<1> : fs_wide_row_kernel<0>), kRowThreads, 0, &r);
+      fill_attr(reinterpret_cast<const void*>(dt ? fs_wide_row_kernel<1> : fs_wide_row_kernel<0>), kRowThreads,
+                kWCacheKeys * 4, &r);
       rows.push_back(r);
     }
     {
