@@ -615,6 +615,79 @@ __device__ void sample_tail_warp(const Params& p, int b, const uint64_t* cand, i
   }
 }
 
+// ctl slots of block_select_top (scratch of the fallback and of the survivor count, dead by then)
+constexpr int kCtlSelHb = kCtlHb, kCtlSelAbove = kCtlAbove, kCtlSelT = kCtlT, kCtlSelNgt = kCtlNgt;
+constexpr int kCtlSelEq = 5, kCtlSelCgt = 6, kCtlSelCtie = 2;
+constexpr int kSelTies = 384;  // ties at the kk-th key that block_select_top ranks (3 KB of Shared)
+
+// The kk largest of the n > kk distinct packed values src[0, n) into dst[0, kk), in no particular
+// order. Two 8-bit levels over the 16-bit key (histograms in sh.h1) give the kk-th largest key T
+// and the count above it; the values above T go straight to dst (positions from a shared
+// counter), the values at T to a buffer in the fallback histograms' space (fh1, fh2, lh: free by
+// now), where each is ranked among them by comparisons and the `need` largest (lowest ids) follow.
+// More than kSelTies values at T: nothing is written to dst and false is returned (the caller
+// sorts everything). All NT threads call it.
+__device__ bool block_select_top(const uint64_t* src, int n, int kk, uint64_t* dst, Shared& sh) {
+  const int t = threadIdx.x;
+  uint32_t* h = sh.h1;
+  uint64_t* ties = reinterpret_cast<uint64_t*>(sh.fh1);
+  static_assert(offsetof(Shared, fh2) == offsetof(Shared, fh1) + 1024 &&
+                    offsetof(Shared, lh) == offsetof(Shared, fh2) + 1024 && kSelTies * 8 <= 3 * 1024,
+                "the tie buffer spans fh1, fh2 and lh");
+  const uint32_t ukk = static_cast<uint32_t>(kk);
+  h[t] = 0u;
+  __syncthreads();
+  for (int i = t; i < n; i += NT) atomicAdd(&h[packed_key(src[i]) >> 8], 1u);
+  __syncthreads();
+  if (t < 32) {
+    uint32_t hb = 0u, above = 0u;
+    warp_boundary_256(h, ukk, &hb, &above);  // n > kk: the boundary exists
+    if (t == 0) {
+      sh.ctl[kCtlSelHb] = hb;
+      sh.ctl[kCtlSelAbove] = above;
+    }
+  }
+  __syncthreads();
+  const uint32_t hb = sh.ctl[kCtlSelHb], above = sh.ctl[kCtlSelAbove];
+  h[t] = 0u;
+  __syncthreads();
+  for (int i = t; i < n; i += NT) {
+    const uint32_t key = packed_key(src[i]);
+    if ((key >> 8) == hb) atomicAdd(&h[key & 0xFFu], 1u);
+  }
+  __syncthreads();
+  if (t < 32) {
+    uint32_t lb = 0u, above2 = 0u;
+    warp_boundary_256(h, ukk - above, &lb, &above2);
+    if (t == 0) {
+      sh.ctl[kCtlSelT] = (hb << 8) | lb;
+      sh.ctl[kCtlSelNgt] = above + above2;
+      sh.ctl[kCtlSelEq] = h[lb];
+      sh.ctl[kCtlSelCgt] = 0u;
+      sh.ctl[kCtlSelCtie] = 0u;
+    }
+  }
+  __syncthreads();
+  const uint32_t T = sh.ctl[kCtlSelT], ngt = sh.ctl[kCtlSelNgt], eq = sh.ctl[kCtlSelEq];
+  if (eq > static_cast<uint32_t>(kSelTies)) return false;  // the same decision in every thread
+  for (int i = t; i < n; i += NT) {
+    const uint64_t x = src[i];
+    const uint32_t key = packed_key(x);
+    if (key > T) dst[atomicAdd(&sh.ctl[kCtlSelCgt], 1u)] = x;
+    else if (key == T) ties[atomicAdd(&sh.ctl[kCtlSelCtie], 1u)] = x;
+  }
+  __syncthreads();
+  const uint32_t need = ukk - ngt;
+  for (uint32_t i = static_cast<uint32_t>(t); i < eq; i += NT) {
+    const uint64_t x = ties[i];
+    uint32_t r = 0u;
+    for (uint32_t j = 0; j < eq; ++j) r += ties[j] > x ? 1u : 0u;
+    if (r < need) dst[ngt + r] = x;
+  }
+  __syncthreads();
+  return true;
+}
+
 // Sorts n packed candidates (value desc, id asc) from `src` into the top kk of `dst`, then
 // writes the selection outputs or runs the tail. All NT threads of the CTA call it; `u` is the
 // row's uniform (valid in warp 0).
@@ -648,11 +721,34 @@ __device__ void finish_row(const Params& p, int b, uint64_t* src, int n, uint64_
   } else {
     int P = 32;
     while (P < n) P <<= 1;
-    for (int i = n + t; i < P; i += NT) src[i] = 0ull;
-    __syncthreads();
-    block_sort_desc<NT>(src, P);
-    for (int i = t; i < kk; i += NT) dst[i] = src[i];
-    __syncthreads();
+    int Pk = 32;
+    while (Pk < kk) Pk <<= 1;
+    // the exact top kk first when that shrinks the sort (dst holds Pk words: the maxima space
+    // holds kMaxMaxima / 2 >= Pk when kk <= kMaxMaxima / 2, else dst is a cap-word buffer)
+    if (Pk < P && block_select_top(src, n, kk, dst, sh)) {
+      if (kk <= NT) {
+        // rank counting of the kk selected (distinct values) into src, then back to dst
+        if (t < kk) {
+          const uint64_t mine = dst[t];
+          int rank = 0;
+          for (int j = 0; j < kk; ++j) rank += dst[j] > mine ? 1 : 0;
+          src[rank] = mine;
+        }
+        __syncthreads();
+        if (t < kk) dst[t] = src[t];
+        __syncthreads();
+      } else {
+        for (int i = kk + t; i < Pk; i += NT) dst[i] = 0ull;
+        __syncthreads();
+        block_sort_desc<NT>(dst, Pk);
+      }
+    } else {
+      for (int i = n + t; i < P; i += NT) src[i] = 0ull;
+      __syncthreads();
+      block_sort_desc<NT>(src, P);
+      for (int i = t; i < kk; i += NT) dst[i] = src[i];
+      __syncthreads();
+    }
   }
   if (p.stop == 5) {
     if (t == 0) p.out[b] = static_cast<int64_t>(packed_id(dst[0]));
