@@ -96,7 +96,17 @@ typedef struct fs_sample_args {
   void* workspace;           /* device scratch for the streaming and wide paths (below)  */
   uint64_t workspace_bytes;  /* its size; >= fs_workspace_size(args)                     */
   float temperature;         /* softmax temperature T > 0; 0 or 1 = none (see below)     */
+  uint32_t input_flags;      /* FS_INPUT_* bits (0: none)                                */
 } fs_sample_args;
+
+/* input_flags. FS_INPUT_READY: the logits are complete when the call is enqueued -- nothing still
+ * running on the GPU writes them (e.g. host memory the CPU filled before the call, or a buffer
+ * written by a kernel that has finished). The cluster path then issues its reads of the logits
+ * before it waits for the stream's previous kernel (programmatic dependent launch), so that for
+ * logits in pinned host memory the transfer over PCIe overlaps the previous call. Without the
+ * flag the reads follow that wait, which is what a producer that lets its dependents start early
+ * requires. No counterpart in the reference (its operators take device tensors only). */
+#define FS_INPUT_READY 1u
 
 /* Pointers marked "device" above may be any address the kernels can dereference on the current
  * device: device memory, or pinned host memory mapped into the device's address space (memory

@@ -49,6 +49,7 @@ EXPORTED = (
 )
 FS_IPC_HANDLE_BYTES = 64
 FS_PATH_AUTO, FS_PATH_CLUSTER, FS_PATH_STREAM, FS_PATH_WIDE = 0, 1, 2, 3
+FS_INPUT_READY = 1  # fs_sample_args.input_flags: the logits are complete when the call is enqueued
 
 
 class FsRng(ctypes.Structure):
@@ -87,6 +88,7 @@ class FsSampleArgs(ctypes.Structure):
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_uint64),
         ("temperature", ctypes.c_float),
+        ("input_flags", ctypes.c_uint32),
     ]
 
 

@@ -78,6 +78,7 @@ struct Params {
   int32_t stop;        // 0 = full pipeline, else ablation phase
   int32_t mode;        // kModeSample / kModeTopk / kModeShard
   float temperature;   // softmax temperature (1 = none): candidates' logits / T before the softmax
+  int32_t early;       // the logits are complete at enqueue: the cluster kernel reads them before the wait
 };
 
 constexpr int kModeSample = 0;
@@ -978,21 +979,17 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
   cluster_arrive();  // B1 (split): waited for only before the first remote access
 
   // Programmatic dependent launch: this grid may have started while the previous kernel of the
-  // stream was still running; warm L2 with this CTA's part of the row meanwhile, wait for that
-  // kernel (and its writes) before reading any input, then let the next kernel of the stream
-  // start its own launch while this one runs.
-  prefetch_row_l2(p.logits, p.row_stride, V, b, static_cast<int64_t>(s) * C * NT * 16, C * NT * 16, t, NT);
-  grid_dependency_wait();
-  grid_launch_dependents();
+  // stream was still running. Unless the caller marked the logits complete at enqueue (p.early: no
+  // running kernel writes them), L2 is warmed with this CTA's part of the row meanwhile and the
+  // reads below wait for that kernel (and its writes); marked logits are read right away, so
+  // that their transfer overlaps that kernel. Then the next kernel of the stream may start its
+  // own launch while this one runs.
+  if (!p.early) {
+    prefetch_row_l2(p.logits, p.row_stride, V, b, static_cast<int64_t>(s) * C * NT * 16, C * NT * 16, t, NT);
+    grid_dependency_wait();
+  }
 
-  int kk;
-  float pp;
-  bool bad;
-  row_params(p, b, &kk, &pp, &bad);
-  // the row's uniform, computed now so that it is off the leader's critical path later
-  const float u = (leader && t < 32) ? row_uniform(p, b) : 0.0f;
-
-  // ---- issue every load of this thread's slice (one HBM read of the row) ----
+  // ---- issue every load of this thread's slice (one read of the row) ----
   const uint16_t* row = p.logits + static_cast<int64_t>(b) * p.row_stride;
   const int vbase = s * C * NT;
   uint4 v[C];
@@ -1005,6 +1002,14 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
 #pragma unroll
     for (int c = 0; c < C; ++c) v[c] = load_chunk<DT>(row, (vbase + c * NT + t) * 8, V, p.vec);
   }
+  if (p.early) grid_dependency_wait();
+  grid_launch_dependents();
+
+  int kk;
+  float pp;
+  bool bad;
+  row_params(p, b, &kk, &pp, &bad);
+  const float u = (leader && t < 32) ? row_uniform(p, b) : 0.0f;
 
   sh.h1[t] = 0u;
   sh.h2[t] = 0u;
@@ -3049,6 +3054,7 @@ static Params base_params(const fs_sample_args* a, int64_t K) {
   prm.keep = a->keep;
   prm.renormed = a->renormed;
   prm.status = a->row_status;
+  prm.early = (a->input_flags & FS_INPUT_READY) != 0u ? 1 : 0;
   prm.vec = 0;
   const uintptr_t addr = reinterpret_cast<uintptr_t>(a->logits);
   if (addr % 16 == 0 && a->row_stride % 8 == 0) prm.vec = 1;

@@ -96,6 +96,8 @@ fs_sample_args base_args(const torch::Tensor& logits, const Source& src, int64_t
                          int64_t splits) {
   fs_sample_args a = {};
   a.logits = src.ptr;
+  // pinned host logits were written by the CPU before this call: no kernel still running writes them
+  if (src.host) a.input_flags = FS_INPUT_READY;
   a.dtype = logits.scalar_type() == at::kBFloat16 ? FS_BF16 : FS_F16;
   a.batch = logits.size(0);
   a.vocab = logits.size(1);

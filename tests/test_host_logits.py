@@ -113,3 +113,24 @@ def test_a_released_input_block_is_not_reused_before_the_call_has_run():
     torch.cuda.current_stream().synchronize()
     assert torch.equal(got, want)
     del other
+
+
+@pytest.mark.gpu
+def test_ready_input_flag_changes_only_when_the_logits_are_read():
+    """FS_INPUT_READY (set by the operators for pinned host logits) lets the cluster kernel read
+    the logits before it waits for the previous kernel; the ids are those of the unflagged call."""
+    import ctypes
+
+    x = anchor(8, 31).cuda()
+    lib = abi.lib()
+    outs = []
+    for flags in (0, abi.FS_INPUT_READY):
+        out = torch.empty(8, dtype=torch.int64, device="cuda")
+        ids = []
+        for off in range(4):  # back to back on one stream
+            a = abi.make_args(x, 50, 0.9, seed=0x5EED, offset=off, out_ids=out, path=abi.FS_PATH_CLUSTER)
+            a.input_flags = flags
+            abi.check(lib.fs_sample(ctypes.byref(a), abi._stream()), "fs_sample")
+            ids.append(out.clone())
+        outs.append(torch.stack(ids).cpu())
+    assert torch.equal(outs[0], outs[1])
