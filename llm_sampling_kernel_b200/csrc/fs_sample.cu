@@ -94,6 +94,7 @@ constexpr int kCtlLKey = 0;     // threshold key
 constexpr int kCtlStatus = 1;   // row status
 constexpr int kCtlLocal = 2;    // this rank's staged survivors
 constexpr int kCtlN = 3;        // survivors of the row
+constexpr int kCtlNgtL = 4;     // survivors strictly above the threshold key
 constexpr int kCtlScr0 = 5;     // two words of block-search results
 constexpr int kCtlHb = 8;       // fallback scratch
 constexpr int kCtlAbove = 9;
@@ -809,9 +810,12 @@ __device__ __forceinline__ uint4 load_chunk(const uint16_t* __restrict__ row, in
 // exact_select: chunks whose loads one pass issues together (all of them for small C)
 __host__ __device__ constexpr int pass_batch(int C) { return C <= 6 ? C : 4; }
 
+constexpr uint32_t kUnknownKey = 0xFFFFFFFFu;  // exact_select: T not known in advance
+
 template <int DT, int C>
 __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict__ row, int V, int vec,
-                                         uint32_t id_base, int vbase, int kk, uint64_t* lsurv) {
+                                         uint32_t id_base, int vbase, int kk, uint64_t* lsurv, uint32_t t_known,
+                                         uint32_t ngt_known) {
   cg::cluster_group cluster = cg::this_cluster();
   const int S = static_cast<int>(cluster.num_blocks());
   const int s = static_cast<int>(cluster.block_rank());
@@ -832,6 +836,10 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
     }
   };
 
+  // T known (the caller counted fewer than kk elements above its threshold L, and at least kk at
+  // or above it: T = L): the two radix levels are skipped, in every rank alike
+  uint32_t T = t_known, n_gt = ngt_known;
+  if (t_known == kUnknownKey) {
   // level 1: high byte
   sh.lh[t] = 0u;
   __syncthreads();
@@ -884,8 +892,9 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
     }
     __syncthreads();
   }
-  const uint32_t T = sh.ctl[kCtlT];
-  const uint32_t n_gt = sh.ctl[kCtlNgt];
+  T = sh.ctl[kCtlT];
+  n_gt = sh.ctl[kCtlNgt];
+  }
   const uint32_t need = static_cast<uint32_t>(kk) - n_gt;
 
   // counts of keys > T and == T per thread, then per rank
@@ -1191,11 +1200,29 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
       if (c == cc) x = v[cc];
     return x;
   };
-  uint32_t nmine = 0u;
+  // the elements strictly above L too (>= the next key's value; a row reaching this phase holds
+  // no NaN and no +inf, so key L + 1 exists): with fewer than kk of them and an overflow, the
+  // k-th key is L itself and the exact fallback needs no radix levels
+  const uint32_t gbits = key_to_bits(lkey + 1u);
+  const uint32_t l2g = gbits | (gbits << 16);
+  const uint32_t ctr_gt = dsmem_addr(&sh.ctl[kCtlNgtL], 0);
+  uint32_t nmine = 0u, ngt_mine = 0u;
   for (uint32_t m = cm; m != 0u; m &= m - 1u) {
     const int c = __ffs(m) - 1;
-    nmine += static_cast<uint32_t>(__popc(chunk_hits(chunk_at(c), (vbase + c * NT + t) * 8)));
+    const uint4 x = chunk_at(c);
+    const int e0 = (vbase + c * NT + t) * 8;
+    nmine += static_cast<uint32_t>(__popc(chunk_hits(x, e0)));
+    uint32_t gt = 0u;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const uint32_t mm = pair_ge_mask<DT>(word_of(x, w), l2g);
+      gt |= ((mm & 1u) | ((mm >> 15) & 2u)) << (2 * w);
+    }
+    if (e0 + 8 > V) gt &= (e0 < V) ? ((1u << (V - e0)) - 1u) : 0u;
+    ngt_mine += static_cast<uint32_t>(__popc(gt));
   }
+  const uint32_t wgt = __reduce_add_sync(0xFFFFFFFFu, ngt_mine);
+  if ((t & 31) == 0 && wgt != 0u) atom_add_dsmem(ctr_gt, wgt);
   const uint32_t lane_incl = warp_incl_scan(nmine);
   const uint32_t wtot = __shfl_sync(0xFFFFFFFFu, lane_incl, 31);
   uint32_t wbase = 0u;
@@ -1222,7 +1249,9 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
   const bool overflow = n > static_cast<int>(cap);  // the same decision in every rank
   if (overflow) {
     uint64_t* lsurv = cluster.map_shared_rank(surv, 0);
-    n = exact_select<DT, C>(sh, row, V, p.vec, p.id_base, vbase, kk, lsurv);
+    const uint32_t ngt_l = leader ? sh.ctl[kCtlNgtL] : ld_dsmem(ctr_gt);
+    const bool t_is_l = ngt_l < static_cast<uint32_t>(kk);  // and n > cap >= kk at or above L
+    n = exact_select<DT, C>(sh, row, V, p.vec, p.id_base, vbase, kk, lsurv, t_is_l ? lkey : kUnknownKey, ngt_l);
     cluster.sync();  // F4: the leader holds exactly kk candidates at [0, kk)
   }
   // Ranks other than the leader are done. The leader waits for their arrival before it exits,
