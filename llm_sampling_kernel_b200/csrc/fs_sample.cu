@@ -991,11 +991,14 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
   // stream was still running. Unless the caller marked the logits complete at enqueue (p.early: no
   // running kernel writes them), L2 is warmed with this CTA's part of the row meanwhile and the
   // reads below wait for that kernel (and its writes); marked logits are read right away, so
-  // that their transfer overlaps that kernel. Then the next kernel of the stream may start its
-  // own launch while this one runs.
+  // that their transfer overlaps that kernel, and the next kernel of the stream may start its
+  // launch at once (several calls on ready inputs then have their transfers in flight together).
+  // Otherwise the next kernel may start its launch once this one has waited.
   if (!p.early) {
     prefetch_row_l2(p.logits, p.row_stride, V, b, static_cast<int64_t>(s) * C * NT * 16, C * NT * 16, t, NT);
     grid_dependency_wait();
+  } else {
+    grid_launch_dependents();  // the next call may start its own reads now (it waits for this one)
   }
 
   // ---- issue every load of this thread's slice (one read of the row) ----
@@ -1012,7 +1015,7 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
     for (int c = 0; c < C; ++c) v[c] = load_chunk<DT>(row, (vbase + c * NT + t) * 8, V, p.vec);
   }
   if (p.early) grid_dependency_wait();
-  grid_launch_dependents();
+  else grid_launch_dependents();
 
   int kk;
   float pp;
