@@ -36,7 +36,14 @@ struct Source {
 // Deliberate difference to the reference: top_k may be anything up to the vocabulary size
 // (the reference rejected top_k > 128, csrc/fused_sampling.cu:351).
 Source check_logits(const torch::Tensor& logits, bool allow_host = false) {
-  const bool host = allow_host && !logits.is_cuda() && logits.device().is_cpu() && logits.is_pinned();
+  // one driver query tells pinned (and mapped) host memory apart from pageable memory
+  cudaPointerAttributes at = {};
+  bool host = false;
+  if (allow_host && !logits.is_cuda() && logits.device().is_cpu()) {
+    const cudaError_t e = cudaPointerGetAttributes(&at, logits.data_ptr());
+    if (e != cudaSuccess) cudaGetLastError();
+    host = e == cudaSuccess && at.type == cudaMemoryTypeHost;
+  }
   TORCH_CHECK((logits.is_cuda() || host) && logits.dim() == 2 && logits.stride(1) == 1 &&
                   logits.stride(0) >= logits.size(1),
               allow_host ? "logits must be a contiguous cuda [B, V] tensor (or one in pinned host memory)"
@@ -51,11 +58,7 @@ Source check_logits(const torch::Tensor& logits, bool allow_host = false) {
     src.opts = logits.options();
     return src;
   }
-  cudaPointerAttributes at = {};
-  const cudaError_t e = cudaPointerGetAttributes(&at, logits.data_ptr());
-  if (e != cudaSuccess) cudaGetLastError();
-  TORCH_CHECK(e == cudaSuccess && at.type == cudaMemoryTypeHost && at.devicePointer != nullptr,
-              "pinned host logits are not mapped into the device address space");
+  TORCH_CHECK(at.devicePointer != nullptr, "pinned host logits are not mapped into the device address space");
   src.ptr = at.devicePointer;
   src.host = true;
   src.device = c10::Device(c10::kCUDA, c10::cuda::current_device());
