@@ -1346,6 +1346,8 @@ __global__ void __launch_bounds__(NT, min_ctas_for(C))
     fs_wide_hist_kernel(const Params p, uint32_t* __restrict__ hist, uint32_t* __restrict__ smax,
                         uint32_t* __restrict__ sflag) {
   __shared__ uint32_t wf[NT / 32], wm[NT / 32];
+  grid_dependency_wait();  // the stream's previous work (histogram clear, the logits) is done
+  grid_launch_dependents();
   const int S = static_cast<int>(gridDim.x);
   const int s = blockIdx.x;
   const int b = blockIdx.y;
@@ -1418,6 +1420,8 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   __shared__ uint32_t uscr[40];
   __shared__ int iscr[40];
   __shared__ uint64_t found[4];
+  grid_dependency_wait();  // the histogram launch is complete
+  grid_launch_dependents();
   const int b = blockIdx.x;
   const int t = threadIdx.x;
   const int lane = t & 31;
@@ -1672,6 +1676,8 @@ template <int DT, int C>
 __global__ void __launch_bounds__(NT, min_ctas_for(C))
     fs_wide_count_kernel(const Params p, const uint32_t* __restrict__ res, uint32_t* __restrict__ cnt) {
   __shared__ uint32_t scr[40];
+  grid_dependency_wait();  // the row launch is complete
+  grid_launch_dependents();
   const int S = static_cast<int>(gridDim.x);
   const int s = blockIdx.x;
   const int b = blockIdx.y;
@@ -1700,6 +1706,8 @@ template <int DT, int C>
 __global__ void __launch_bounds__(NT, min_ctas_for(C))
     fs_wide_pick_kernel(const Params p, const uint32_t* __restrict__ res, const uint32_t* __restrict__ cnt) {
   __shared__ uint32_t scr[40];
+  grid_dependency_wait();  // the count launch (and, through it, the row launch) is complete
+  grid_launch_dependents();
   const int S = static_cast<int>(gridDim.x);
   const int s = blockIdx.x;
   const int b = blockIdx.y;
@@ -2950,11 +2958,46 @@ struct WideKernels {
     const dim3 grid(plan.splits, static_cast<unsigned>(a->batch), 1);
     fs_status st = prepare_kernel(reinterpret_cast<KernelFn>(fs_wide_row_kernel<DT>), 1, kWCacheKeys * 4);
     if (st != FS_OK) return st;
-    fs_wide_hist_kernel<DT, C><<<grid, NT, 0, stream>>>(prm, hist, smax, sflag);
-    fs_wide_row_kernel<DT><<<static_cast<unsigned>(a->batch), kRowThreads, kWCacheKeys * 4, stream>>>(
-        prm, hist, smax, sflag, res, plan.splits);
-    fs_wide_count_kernel<DT, C><<<grid, NT, 0, stream>>>(prm, res, cnt);
-    fs_wide_pick_kernel<DT, C><<<grid, NT, 0, stream>>>(prm, res, cnt);
+    // programmatic dependent launch: each kernel waits for its predecessor before it reads
+    // anything, so the next one may be launched (and placed) while the current one runs
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    auto cfg = [&](dim3 g, unsigned block, size_t smem) {
+      cudaLaunchConfig_t c = {};
+      c.gridDim = g;
+      c.blockDim = dim3(block, 1, 1);
+      c.dynamicSmemBytes = smem;
+      c.stream = stream;
+      c.attrs = pdl;
+      c.numAttrs = 1;
+      return c;
+    };
+    const char* what = "wide histogram launch";
+    cudaLaunchConfig_t c1 = cfg(grid, NT, 0);
+    cudaError_t e = cudaLaunchKernelEx(&c1, fs_wide_hist_kernel<DT, C>, prm, hist, smax, sflag);
+    if (e == cudaSuccess) {
+      what = "wide row launch";
+      cudaLaunchConfig_t c2 = cfg(dim3(static_cast<unsigned>(a->batch), 1, 1), kRowThreads, kWCacheKeys * 4);
+      e = cudaLaunchKernelEx(&c2, fs_wide_row_kernel<DT>, prm, static_cast<const uint32_t*>(hist),
+                             static_cast<const uint32_t*>(smax), static_cast<const uint32_t*>(sflag), res,
+                             plan.splits);
+    }
+    if (e == cudaSuccess) {
+      what = "wide count launch";
+      cudaLaunchConfig_t c3 = cfg(grid, NT, 0);
+      e = cudaLaunchKernelEx(&c3, fs_wide_count_kernel<DT, C>, prm, static_cast<const uint32_t*>(res), cnt);
+    }
+    if (e == cudaSuccess) {
+      what = "wide pick launch";
+      cudaLaunchConfig_t c4 = cfg(grid, NT, 0);
+      e = cudaLaunchKernelEx(&c4, fs_wide_pick_kernel<DT, C>, prm, static_cast<const uint32_t*>(res),
+                             static_cast<const uint32_t*>(cnt));
+    }
+    if (e != cudaSuccess) {
+      set_error("%s: %s", what, cudaGetErrorString(e));
+      return FS_ELAUNCH;
+    }
     return FS_OK;
   }
 };
