@@ -542,12 +542,12 @@ def run_adversarial(ops, device, args):
             ops.sample_fused(bufs[i % nbuf], k, p, 0x5EED, i, 0)
 
         out[name] = round(timed_steps(step, steps, warm, 1) * 1000.0 / steps, 3)
-        launches += steps * (4 if ops.plan(B, V, k, 0)[7] == 3 else 1)
+        launches += steps * (5 if ops.plan(B, V, k, 0)[7] == 3 else 1)
         del bufs
         torch.cuda.empty_cache()
     out.update({"B": B, "V": V, "dtype": "fp16", "launches": launches,
                 "l2": f"cold: {nbuf} rotating buffers per case ({nbuf * per / 2**20:.0f} MiB > 2x L2)",
-                "paths": {"case2": "wide (histogram, row, count, pick launches + a histogram memset)",
+                "paths": {"case2": "wide (histogram clear, histogram, row, count, pick launches)",
                           "others": "cluster (one launch)"}})
     return out
 

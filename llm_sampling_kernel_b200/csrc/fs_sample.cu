@@ -2951,6 +2951,16 @@ static fs_status launch_cluster(int dtype, const PlanOut& plan, int64_t B, const
   return FS_OK;
 }
 
+// Clears the wide path's [B, 65536] per-key histograms with 16-byte stores. It waits for the
+// stream's previous kernel first (the workspace may be memory that kernel still reads) and then
+// lets the histogram launch be placed while it runs.
+__global__ void __launch_bounds__(NT) fs_wide_zero_kernel(uint4* __restrict__ h, size_t n16) {
+  grid_dependency_wait();
+  grid_launch_dependents();
+  const size_t step = static_cast<size_t>(gridDim.x) * NT;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * NT + threadIdx.x; i < n16; i += step) h[i] = make_uint4(0u, 0u, 0u, 0u);
+}
+
 template <int DT, int C>
 struct WideKernels {
   static fs_status launch(const fs_sample_args* a, const PlanOut& plan, const Params& prm, uint32_t* hist,
@@ -3038,7 +3048,18 @@ static fs_status launch_wide(const fs_sample_args* a, const PlanOut& plan, const
   uint32_t* sflag = smax + B * S;
   uint32_t* cnt = sflag + B * S;
   uint32_t* res = cnt + B * S;
-  cudaError_t e = cudaMemsetAsync(hist, 0, B * kKeys * sizeof(uint32_t), stream);
+  // the histograms start at zero: a clearing kernel in the same launch chain as the four below
+  const size_t n16 = B * kKeys * sizeof(uint32_t) / 16;
+  cudaLaunchAttribute pdl[1];
+  pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t zc = {};
+  zc.gridDim = dim3(static_cast<unsigned>(std::min<size_t>((n16 + NT - 1) / NT, 148 * 8)), 1, 1);
+  zc.blockDim = dim3(NT, 1, 1);
+  zc.stream = stream;
+  zc.attrs = pdl;
+  zc.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&zc, fs_wide_zero_kernel, reinterpret_cast<uint4*>(hist), n16);
   if (e != cudaSuccess) {
     set_error("wide path histogram clear: %s", cudaGetErrorString(e));
     return FS_ELAUNCH;
