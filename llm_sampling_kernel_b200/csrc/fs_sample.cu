@@ -1285,8 +1285,9 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
 // Wide path: top-k beyond the survivor buffer, up to k = V (top-p only). Nothing is sorted.
 // The probability of an element depends only on its 16-bit key, so the sorted order (value
 // desc, id asc) is a sequence of key groups, and every cumulative sum the tail needs is a sum of
-// (group size x group probability) over the groups above a point. Four launches (and a memset of
-// the histogram), plain CTAs, no cluster:
+// (group size x group probability) over the groups above a point. Five launches in one
+// programmatic-dependent-launch chain (a clear of the histograms, then these four), plain CTAs,
+// no cluster:
 //   fs_wide_hist_kernel  (S x B CTAs) one read of each row slice: the per-key element counts of
 //                        the row (a [B, 65536] histogram in the workspace; lanes holding the same
 //                        key add once), and the slice's maximum and row flags;
