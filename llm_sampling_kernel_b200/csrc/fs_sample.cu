@@ -2614,6 +2614,10 @@ __device__ void tp_merge_row(const Params& p, const uint64_t* __restrict__ local
 template <int DT>
 __global__ void __launch_bounds__(NT) fs_tp_merge_kernel(const Params p, const uint64_t* __restrict__ local_cand,
                                                          const TpPeers tp) {
+  // programmatic dependent launch: this grid may have been placed while the shard top-k kernel
+  // still runs; wait for it (and, through it, for the previous step) before reading anything
+  grid_dependency_wait();
+  grid_launch_dependents();
   // with a device counter every CTA reads the last epoch before any CTA writes it back: the
   // write-back comes from the CTA that finishes last, after every CTA has started
   uint32_t epoch = tp.epoch;
@@ -3333,8 +3337,17 @@ fs_status run_tp_merge(const fs_sample_args* a, const uint64_t* local_cand, cons
   auto fn = a->dtype == FS_BF16 ? fs_tp_merge_kernel<1> : fs_tp_merge_kernel<0>;
   fs_status st = prepare_kernel(reinterpret_cast<KernelFn>(fn), 1, smem);
   if (st != FS_OK) return st;
-  fn<<<static_cast<unsigned>(a->batch), NT, smem, stream>>>(prm, local_cand, tp);
-  const cudaError_t e = cudaGetLastError();
+  cudaLaunchAttribute pdl[1];
+  pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a->batch), 1, 1);
+  cfg.blockDim = dim3(NT, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = pdl;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, prm, local_cand, tp);
   if (e != cudaSuccess) {
     set_error("tp merge launch: %s", cudaGetErrorString(e));
     return FS_ELAUNCH;
