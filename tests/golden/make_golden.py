@@ -1,7 +1,7 @@
 """Generate golden vectors by running the reference's own CPU oracle.
 
 Imports ``benchmarks/reference.py`` of sathviknookala/llm_sampling_kernel from a local checkout
-(default ``/root/reference``, or ``--reference PATH``) and records, for seeded inputs, every
+(``--reference PATH``; the default is the checkout location of the build machine) and records, for seeded inputs, every
 stage ``sample_eager(..., return_stages=True)`` returns. The output ``golden_stages.npz`` is
 committed; the tests read it and never need the reference itself.
 
