@@ -94,7 +94,6 @@ constexpr int kCtlLKey = 0;     // threshold key
 constexpr int kCtlStatus = 1;   // row status
 constexpr int kCtlLocal = 2;    // this rank's staged survivors
 constexpr int kCtlN = 3;        // survivors of the row
-constexpr int kCtlNgtL = 4;     // survivors strictly above the threshold key
 constexpr int kCtlScr0 = 5;     // two words of block-search results
 constexpr int kCtlHb = 8;       // fallback scratch
 constexpr int kCtlAbove = 9;
@@ -800,22 +799,30 @@ __device__ __forceinline__ uint4 load_chunk(const uint16_t* __restrict__ row, in
 }
 
 // Exact top-kk selection of the cluster's row, used when the survivor filter overflows the
-// buffer (heavy ties). Two 8-bit radix levels over the order key give the k-th key T and the
-// count above it (csrc/fused_sampling.cu:163-209 computes the same two levels per slice);
-// the ties at T are then ranked in id order - rank boundaries follow the (rank, chunk,
-// thread, lane) layout, which is increasing in token id - and the lowest `need` are kept.
-// The slice is re-read from global memory (L2) chunk by chunk, so this rare path does not
-// hold the row in registers. Every thread of every CTA of the cluster calls it; it writes kk
-// packed candidates into the leader's buffer and returns kk.
+// buffer (heavy ties). The k-th key T comes from one counting pass when it lies within four
+// keys of the filter threshold L (at least kk keys are >= L): each thread counts its keys at
+// L, L + 1, L + 2, L + 3 and at or above L + 4, the per-rank totals go to every rank, and every
+// rank finds T and the per-rank counts above and at T from them. Otherwise two 8-bit radix
+// levels over the order key give T and the count above it (csrc/fused_sampling.cu:163-209
+// computes the same two levels per slice). The ties at T are then ranked in id order - rank
+// boundaries follow the (rank, chunk, thread, lane) layout, which is increasing in token id -
+// and the lowest `need` are kept. The slice is re-read from global memory (L2) chunk by chunk,
+// so this rare path does not hold the row in registers. Every thread of every CTA of the
+// cluster calls it; it writes kk packed candidates into the leader's buffer and returns kk.
 // exact_select: chunks whose loads one pass issues together (all of them for small C)
 __host__ __device__ constexpr int pass_batch(int C) { return C <= 6 ? C : 4; }
 
-constexpr uint32_t kUnknownKey = 0xFFFFFFFFu;  // exact_select: T not known in advance
+// exact_select's counting pass: keys at L + j for j < 4 and at or above L + 4, one 12-bit field
+// each in a thread's 64-bit counter (a thread holds at most 8 * C <= 128 keys; the fields are
+// taken apart before the warp sums)
+constexpr int kBins = 5;
+constexpr int kBinBits = 12;
+static_assert(kBins * kBinBits <= 64 && 8 * 16 < (1 << kBinBits), "bin counters overflow");
+static_assert(kBins * NT / 32 <= 40 && kBins * kMaxSplits <= 256, "bin totals do not fit uscr / lh");
 
 template <int DT, int C>
 __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict__ row, int V, int vec,
-                                         uint32_t id_base, int vbase, int kk, uint64_t* lsurv, uint32_t t_known,
-                                         uint32_t ngt_known) {
+                                         uint32_t id_base, int vbase, int kk, uint64_t* lsurv, uint32_t lkey) {
   cg::cluster_group cluster = cg::this_cluster();
   const int S = static_cast<int>(cluster.num_blocks());
   const int s = static_cast<int>(cluster.block_rank());
@@ -836,97 +843,165 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
     }
   };
 
-  // T known (the caller counted fewer than kk elements above its threshold L, and at least kk at
-  // or above it: T = L): the two radix levels are skipped, in every rank alike
-  uint32_t T = t_known, n_gt = ngt_known;
-  if (t_known == kUnknownKey) {
-  // level 1: high byte
-  sh.lh[t] = 0u;
-  __syncthreads();
+  static_assert(8 * C < (1 << kBinBits), "bin counters overflow");
+  const int lane = t & 31, warp = t >> 5;
+  // counting pass: this thread's keys at L + j (j < 4) and at or above L + 4
+  uint64_t bins = 0ull;
   for_chunks([&](int e0, const uint4& v) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const uint32_t w = word_of(v, q);
-      hist_add_warp(sh.lh, order_key(w & 0xFFFFu) >> 8, e0 + 2 * q < V);
-      hist_add_warp(sh.lh, order_key(w >> 16) >> 8, e0 + 2 * q + 1 < V);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t key = order_key(h ? (w >> 16) : (w & 0xFFFFu));
+        if (e0 + 2 * q + h < V && key >= lkey)
+          bins += 1ull << (kBinBits * min(key - lkey, static_cast<uint32_t>(kBins - 1)));
+      }
     }
   });
+  auto bin_of = [&](int j) -> uint32_t {
+    return static_cast<uint32_t>(bins >> (kBinBits * j)) & ((1u << kBinBits) - 1u);
+  };
+  // warp totals, rank totals, then every rank's totals in every rank (lh[kBins * rank + j])
+#pragma unroll
+  for (int j = 0; j < kBins; ++j) {
+    const uint32_t wj = __reduce_add_sync(0xFFFFFFFFu, bin_of(j));
+    if (lane == 0) sh.uscr[kBins * warp + j] = wj;
+  }
   __syncthreads();
-  if (sh.lh[t] != 0u) atomicAdd(cluster.map_shared_rank(&sh.fh1[t], 0), sh.lh[t]);
-  cluster.sync();  // F1
-  {
-    const uint32_t h = *cluster.map_shared_rank(&sh.fh1[255 - t], 0);
-    uint32_t total;
-    const uint32_t inc = block_incl_scan<uint32_t, NT>(h, sh.uscr, &total);
-    if (inc >= static_cast<uint32_t>(kk) && inc - h < static_cast<uint32_t>(kk)) {
-      sh.ctl[kCtlHb] = static_cast<uint32_t>(255 - t);
-      sh.ctl[kCtlAbove] = inc - h;
+  if (t < kBins * S) {
+    const int r = t / kBins, j = t - r * kBins;
+    uint32_t tot = 0u;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) tot += sh.uscr[kBins * w + j];
+    cluster.map_shared_rank(sh.lh, r)[kBins * s + j] = tot;
+  }
+  cluster.sync();  // F3: every rank holds every rank's totals
+  uint32_t row_bin[kBins], pre_bin[kBins];  // the row's, and the ranks' before this one
+#pragma unroll
+  for (int j = 0; j < kBins; ++j) row_bin[j] = pre_bin[j] = 0u;
+  for (int r = 0; r < S; ++r) {
+#pragma unroll
+    for (int j = 0; j < kBins; ++j) {
+      const uint32_t c = sh.lh[kBins * r + j];
+      row_bin[j] += c;
+      pre_bin[j] += r < s ? c : 0u;
     }
+  }
+  // T = L + j for the largest j < 4 with fewer than kk keys above L + j and at least kk at or
+  // above it; the same decision in every rank (the same totals)
+  uint32_t T = 0u, n_gt = 0u, ngt = 0u, ntie = 0u, gt_base = 0u, tie_base = 0u;
+  bool known = false;
+  {
+    uint32_t above = row_bin[kBins - 1], pabove = pre_bin[kBins - 1], mabove = bin_of(kBins - 1);
+#pragma unroll
+    for (int j = kBins - 2; j >= 0; --j) {
+      if (!known && above < static_cast<uint32_t>(kk) && above + row_bin[j] >= static_cast<uint32_t>(kk)) {
+        known = true;
+        T = lkey + static_cast<uint32_t>(j);
+        n_gt = above;
+        ngt = mabove;
+        ntie = bin_of(j);
+        gt_base = pabove;
+        tie_base = pre_bin[j];
+      }
+      above += row_bin[j];
+      pabove += pre_bin[j];
+      mabove += bin_of(j);
+    }
+  }
+  uint32_t gt_off;
+  if (known) {
+    uint32_t gt_total;
+    gt_off = block_incl_scan<uint32_t, NT>(ngt, sh.uscr, &gt_total) - ngt;
+  } else {
+    // T beyond L + 3: two radix levels find it
+    __syncthreads();  // every thread has read lh
+    // level 1: high byte
     sh.lh[t] = 0u;
     __syncthreads();
-  }
-  const uint32_t hb = sh.ctl[kCtlHb];
-  const uint32_t n_above = sh.ctl[kCtlAbove];
-
-  // level 2: low byte inside bucket hb
-  for_chunks([&](int e0, const uint4& v) {
+    for_chunks([&](int e0, const uint4& v) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t w = word_of(v, q);
-      const uint32_t k0 = order_key(w & 0xFFFFu), k1 = order_key(w >> 16);
-      hist_add_warp(sh.lh, k0 & 0xFFu, e0 + 2 * q < V && (k0 >> 8) == hb);
-      hist_add_warp(sh.lh, k1 & 0xFFu, e0 + 2 * q + 1 < V && (k1 >> 8) == hb);
-    }
-  });
-  __syncthreads();
-  if (sh.lh[t] != 0u) atomicAdd(cluster.map_shared_rank(&sh.fh2[t], 0), sh.lh[t]);
-  cluster.sync();  // F2
-  {
-    const uint32_t want = static_cast<uint32_t>(kk) - n_above;
-    const uint32_t h = *cluster.map_shared_rank(&sh.fh2[255 - t], 0);
-    uint32_t total;
-    const uint32_t inc = block_incl_scan<uint32_t, NT>(h, sh.uscr, &total);
-    if (inc >= want && inc - h < want) {
-      sh.ctl[kCtlT] = (hb << 8) | static_cast<uint32_t>(255 - t);
-      sh.ctl[kCtlNgt] = n_above + inc - h;
-    }
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t w = word_of(v, q);
+        hist_add_warp(sh.lh, order_key(w & 0xFFFFu) >> 8, e0 + 2 * q < V);
+        hist_add_warp(sh.lh, order_key(w >> 16) >> 8, e0 + 2 * q + 1 < V);
+      }
+    });
     __syncthreads();
-  }
-  T = sh.ctl[kCtlT];
-  n_gt = sh.ctl[kCtlNgt];
+    if (sh.lh[t] != 0u) atomicAdd(cluster.map_shared_rank(&sh.fh1[t], 0), sh.lh[t]);
+    cluster.sync();  // F1
+    {
+      const uint32_t h = *cluster.map_shared_rank(&sh.fh1[255 - t], 0);
+      uint32_t total;
+      const uint32_t inc = block_incl_scan<uint32_t, NT>(h, sh.uscr, &total);
+      if (inc >= static_cast<uint32_t>(kk) && inc - h < static_cast<uint32_t>(kk)) {
+        sh.ctl[kCtlHb] = static_cast<uint32_t>(255 - t);
+        sh.ctl[kCtlAbove] = inc - h;
+      }
+      sh.lh[t] = 0u;
+      __syncthreads();
+    }
+    const uint32_t hb = sh.ctl[kCtlHb];
+    const uint32_t n_above = sh.ctl[kCtlAbove];
+
+    // level 2: low byte inside bucket hb
+    for_chunks([&](int e0, const uint4& v) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t w = word_of(v, q);
+        const uint32_t k0 = order_key(w & 0xFFFFu), k1 = order_key(w >> 16);
+        hist_add_warp(sh.lh, k0 & 0xFFu, e0 + 2 * q < V && (k0 >> 8) == hb);
+        hist_add_warp(sh.lh, k1 & 0xFFu, e0 + 2 * q + 1 < V && (k1 >> 8) == hb);
+      }
+    });
+    __syncthreads();
+    if (sh.lh[t] != 0u) atomicAdd(cluster.map_shared_rank(&sh.fh2[t], 0), sh.lh[t]);
+    cluster.sync();  // F2
+    {
+      const uint32_t want = static_cast<uint32_t>(kk) - n_above;
+      const uint32_t h = *cluster.map_shared_rank(&sh.fh2[255 - t], 0);
+      uint32_t total;
+      const uint32_t inc = block_incl_scan<uint32_t, NT>(h, sh.uscr, &total);
+      if (inc >= want && inc - h < want) {
+        sh.ctl[kCtlT] = (hb << 8) | static_cast<uint32_t>(255 - t);
+        sh.ctl[kCtlNgt] = n_above + inc - h;
+      }
+      __syncthreads();
+    }
+    T = sh.ctl[kCtlT];
+    n_gt = sh.ctl[kCtlNgt];
+
+    // counts of keys > T and == T per thread, then per rank
+    for_chunks([&](int e0, const uint4& v) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t w = word_of(v, q);
+        const uint32_t k0 = order_key(w & 0xFFFFu), k1 = order_key(w >> 16);
+        if (e0 + 2 * q < V) {
+          ngt += k0 > T;
+          ntie += k0 == T;
+        }
+        if (e0 + 2 * q + 1 < V) {
+          ngt += k1 > T;
+          ntie += k1 == T;
+        }
+      }
+    });
+    uint32_t gt_total, tie_total;
+    gt_off = block_incl_scan<uint32_t, NT>(ngt, sh.uscr, &gt_total) - ngt;
+    block_incl_scan<uint32_t, NT>(ntie, sh.uscr, &tie_total);
+    if (t < S) {
+      cluster.map_shared_rank(sh.cnt, t)[s] = gt_total;
+      cluster.map_shared_rank(sh.cnt2, t)[s] = tie_total;
+    }
+    cluster.sync();  // F3b
+    for (int r = 0; r < s; ++r) {
+      gt_base += sh.cnt[r];
+      tie_base += sh.cnt2[r];
+    }
   }
   const uint32_t need = static_cast<uint32_t>(kk) - n_gt;
-
-  // counts of keys > T and == T per thread, then per rank
-  uint32_t ngt = 0u, ntie = 0u;
-  for_chunks([&](int e0, const uint4& v) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t w = word_of(v, q);
-      const uint32_t k0 = order_key(w & 0xFFFFu), k1 = order_key(w >> 16);
-      if (e0 + 2 * q < V) {
-        ngt += k0 > T;
-        ntie += k0 == T;
-      }
-      if (e0 + 2 * q + 1 < V) {
-        ngt += k1 > T;
-        ntie += k1 == T;
-      }
-    }
-  });
-  uint32_t gt_total, tie_total;
-  const uint32_t gt_off = block_incl_scan<uint32_t, NT>(ngt, sh.uscr, &gt_total) - ngt;
-  block_incl_scan<uint32_t, NT>(ntie, sh.uscr, &tie_total);
-  if (t < S) {
-    cluster.map_shared_rank(sh.cnt, t)[s] = gt_total;
-    cluster.map_shared_rank(sh.cnt2, t)[s] = tie_total;
-  }
-  cluster.sync();  // F3
-  uint32_t gt_base = 0u, tie_base = 0u;
-  for (int r = 0; r < s; ++r) {
-    gt_base += sh.cnt[r];
-    tie_base += sh.cnt2[r];
-  }
   // keys strictly above T, and the ties at T ranked in id order
   uint32_t slot = gt_base + gt_off;
   uint32_t chunk_base = tie_base;
@@ -1203,29 +1278,11 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
       if (c == cc) x = v[cc];
     return x;
   };
-  // the elements strictly above L too (>= the next key's value; a row reaching this phase holds
-  // no NaN and no +inf, so key L + 1 exists): with fewer than kk of them and an overflow, the
-  // k-th key is L itself and the exact fallback needs no radix levels
-  const uint32_t gbits = key_to_bits(lkey + 1u);
-  const uint32_t l2g = gbits | (gbits << 16);
-  const uint32_t ctr_gt = dsmem_addr(&sh.ctl[kCtlNgtL], 0);
-  uint32_t nmine = 0u, ngt_mine = 0u;
+  uint32_t nmine = 0u;
   for (uint32_t m = cm; m != 0u; m &= m - 1u) {
     const int c = __ffs(m) - 1;
-    const uint4 x = chunk_at(c);
-    const int e0 = (vbase + c * NT + t) * 8;
-    nmine += static_cast<uint32_t>(__popc(chunk_hits(x, e0)));
-    uint32_t gt = 0u;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const uint32_t mm = pair_ge_mask<DT>(word_of(x, w), l2g);
-      gt |= ((mm & 1u) | ((mm >> 15) & 2u)) << (2 * w);
-    }
-    if (e0 + 8 > V) gt &= (e0 < V) ? ((1u << (V - e0)) - 1u) : 0u;
-    ngt_mine += static_cast<uint32_t>(__popc(gt));
+    nmine += static_cast<uint32_t>(__popc(chunk_hits(chunk_at(c), (vbase + c * NT + t) * 8)));
   }
-  const uint32_t wgt = __reduce_add_sync(0xFFFFFFFFu, ngt_mine);
-  if ((t & 31) == 0 && wgt != 0u) atom_add_dsmem(ctr_gt, wgt);
   const uint32_t lane_incl = warp_incl_scan(nmine);
   const uint32_t wtot = __shfl_sync(0xFFFFFFFFu, lane_incl, 31);
   uint32_t wbase = 0u;
@@ -1252,9 +1309,7 @@ __global__ void __launch_bounds__(NT, cluster_min_ctas(C)) fs_cluster_kernel(con
   const bool overflow = n > static_cast<int>(cap);  // the same decision in every rank
   if (overflow) {
     uint64_t* lsurv = cluster.map_shared_rank(surv, 0);
-    const uint32_t ngt_l = leader ? sh.ctl[kCtlNgtL] : ld_dsmem(ctr_gt);
-    const bool t_is_l = ngt_l < static_cast<uint32_t>(kk);  // and n > cap >= kk at or above L
-    n = exact_select<DT, C>(sh, row, V, p.vec, p.id_base, vbase, kk, lsurv, t_is_l ? lkey : kUnknownKey, ngt_l);
+    n = exact_select<DT, C>(sh, row, V, p.vec, p.id_base, vbase, kk, lsurv, lkey);
     cluster.sync();  // F4: the leader holds exactly kk candidates at [0, kk)
   }
   // Ranks other than the leader are done. The leader waits for their arrival before it exits,

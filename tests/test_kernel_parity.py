@@ -94,6 +94,55 @@ def test_signed_zeros_tie_on_the_k_boundary():
             assert torch.equal(fused.topk_fused(xd, k).cpu(), oracle_topk(xd, k))
 
 
+ADJACENT_KEY_COUNTS = [
+    [3000] * 8,
+    [0, 0, 0, 0, 0, 0, 0, 3000],
+    [2000, 2000, 2000, 2000, 40, 10, 5, 1],
+    [0, 0, 0, 5000, 0, 0, 0, 1],
+    [5000, 0, 0, 0, 0, 0, 0, 30],
+    [100, 200, 400, 800, 1600, 3200, 6400, 12800],
+    [12800, 6400, 3200, 1600, 800, 400, 200, 100],
+    [0, 1500, 0, 1500, 0, 1500, 0, 1500],
+]
+
+
+def adjacent_key_rows(dtype, vocab, seed):
+    """Rows of -1.0 holding, at random positions, counts[i] copies of the i-th representable value
+    above 1.0 (adjacent order keys): heavy ties a few keys apart, more than the survivor buffer
+    holds, so the k-th key lies at, one to three keys above, or further above the threshold."""
+    g = torch.Generator().manual_seed(seed)
+    one = int(torch.tensor(1.0, dtype=dtype).view(torch.int16).item())
+    rows = []
+    for counts in ADJACENT_KEY_COUNTS:
+        r = torch.full((vocab,), -1.0, dtype=dtype).view(torch.int16)
+        perm = torch.randperm(vocab, generator=g)
+        pos = 0
+        for i, c in enumerate(counts):
+            c = min(c, vocab // 8)
+            r[perm[pos:pos + c]] = one + i
+            pos += c
+        rows.append(r.view(dtype))
+    return torch.stack(rows).cuda()
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("vocab", [20000, 151936])
+def test_heavy_ties_on_adjacent_keys_match_the_oracle(dtype, vocab):
+    x = adjacent_key_rows(dtype, vocab, seed=vocab)
+    for top_k in (1, 20, 50, 100, 256, 1024):
+        assert torch.equal(fused.topk_fused(x, top_k).cpu(), oracle_topk(x, top_k)), top_k
+    check_draw(x, 50, 0.9, seed=7)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_sixteen_level_rows_at_small_k_match_the_oracle(dtype):
+    g = torch.Generator().manual_seed(5)
+    levels = torch.linspace(-3.0, 3.0, 16)
+    x = levels[torch.randint(0, 16, (8, 151936), generator=g)].to(dtype).cuda()
+    for top_k in (1, 20, 50, 100, 1024):
+        assert torch.equal(fused.topk_fused(x, top_k).cpu(), oracle_topk(x, top_k)), top_k
+
+
 def check_draw(x, top_k, top_p, uniforms=None, seed=0, offset=0):
     """Kernel ids vs oracle ids for the same u; returns the number of exempt rows."""
     B = x.shape[0]
