@@ -525,14 +525,16 @@ def adversarial_buffers(case, n, B, V, device, seed):
 def run_adversarial(ops, device, args):
     """The four adversarial configurations at B=8, V=151936, FP16: 16 distinct values at k=1024,
     p=0.99; top-p only (k=V, p=0.5) on N(0, 0.1^2) (the wide path); greedy k=1; rows with +-inf and
-    the most negative finite value (k=1024, p=0.9). Each timed over rotating buffers > 2x L2."""
+    the most negative finite value (k=1024, p=0.9). Also the 16-value rows at k=50, p=0.9 (the tie
+    fallback at small k). Each timed over rotating buffers > 2x L2."""
     B, V = 8, C1["V"]
     per = B * V * 2
     nbuf = max(2, (2 * L2_BYTES) // per + 1)
     steps = max(3, min(args.steps, 200))
     warm = max(3, args.warmup)
     cases = ((1, "case1_16_values_k1024_p099_us", 1024, 0.99), (2, "case2_top_p_only_k_eq_V_p05_us", V, 0.5),
-             (3, "case3_greedy_k1_us", 1, 0.9), (4, "case4_inf_and_lowest_finite_k1024_us", 1024, 0.9))
+             (3, "case3_greedy_k1_us", 1, 0.9), (4, "case4_inf_and_lowest_finite_k1024_us", 1024, 0.9),
+             (1, "case1_16_values_k50_p09_us", 50, 0.9))
     out = {}
     launches = 0
     for case, name, k, p in cases:

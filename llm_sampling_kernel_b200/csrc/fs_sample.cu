@@ -910,10 +910,9 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
       mabove += bin_of(j);
     }
   }
-  uint32_t gt_off;
+  uint32_t gt_off, gt_rank;  // this thread's offset among the rank's keys above T; their number
   if (known) {
-    uint32_t gt_total;
-    gt_off = block_incl_scan<uint32_t, NT>(ngt, sh.uscr, &gt_total) - ngt;
+    gt_off = block_incl_scan<uint32_t, NT>(ngt, sh.uscr, &gt_rank) - ngt;
   } else {
     // T beyond L + 3: two radix levels find it
     __syncthreads();  // every thread has read lh
@@ -988,11 +987,11 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
         }
       }
     });
-    uint32_t gt_total, tie_total;
-    gt_off = block_incl_scan<uint32_t, NT>(ngt, sh.uscr, &gt_total) - ngt;
+    uint32_t tie_total;
+    gt_off = block_incl_scan<uint32_t, NT>(ngt, sh.uscr, &gt_rank) - ngt;
     block_incl_scan<uint32_t, NT>(ntie, sh.uscr, &tie_total);
     if (t < S) {
-      cluster.map_shared_rank(sh.cnt, t)[s] = gt_total;
+      cluster.map_shared_rank(sh.cnt, t)[s] = gt_rank;
       cluster.map_shared_rank(sh.cnt2, t)[s] = tie_total;
     }
     cluster.sync();  // F3b
@@ -1002,7 +1001,10 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
     }
   }
   const uint32_t need = static_cast<uint32_t>(kk) - n_gt;
-  // keys strictly above T, and the ties at T ranked in id order
+  // a rank with no key above T whose first tie ranks past the kept ones contributes nothing
+  if (gt_rank == 0u && tie_base >= need) return kk;
+  // keys strictly above T, and the ties at T ranked in id order (chunk_base is the same in every
+  // thread of the rank, so the scan is skipped by all of them once the kept ties are placed)
   uint32_t slot = gt_base + gt_off;
   uint32_t chunk_base = tie_base;
   for_chunks([&](int e0, const uint4& v) {
@@ -1020,17 +1022,19 @@ __device__ __noinline__ int exact_select(Shared& sh, const uint16_t* __restrict_
         if (k1 == T) mask |= 1u << (2 * q + 1);
       }
     }
-    const uint32_t cnt = __popc(mask);
-    uint32_t ctot;
-    const uint32_t excl = block_incl_scan<uint32_t, NT>(cnt, sh.uscr, &ctot) - cnt;
-    uint32_t rank = chunk_base + excl;
-    while (mask != 0u && rank < need) {
-      const int j = __ffs(mask) - 1;
-      mask &= mask - 1;
-      lsurv[n_gt + rank] = pack(T, id_base + e0 + j);
-      ++rank;
+    if (chunk_base < need) {
+      const uint32_t cnt = __popc(mask);
+      uint32_t ctot;
+      const uint32_t excl = block_incl_scan<uint32_t, NT>(cnt, sh.uscr, &ctot) - cnt;
+      uint32_t rank = chunk_base + excl;
+      while (mask != 0u && rank < need) {
+        const int j = __ffs(mask) - 1;
+        mask &= mask - 1;
+        lsurv[n_gt + rank] = pack(T, id_base + e0 + j);
+        ++rank;
+      }
+      chunk_base += ctot;
     }
-    chunk_base += ctot;
   });
   return kk;
 }
